@@ -1,0 +1,136 @@
+/*
+ * murm.h — C ABI of the B200 (sm_100a) slot_murmurate library.
+ *
+ * One operation, forward and backward:
+ *
+ *   slot_murmurate(q, slots_k, slots_v, rounds, top_k=7, causal)
+ *       -> (out, indices, weights)
+ *
+ * For R rounds every token (row of q) selects its 7 highest-scoring slots by
+ * q . slots_k (top-7, ties to the lowest slot index), attends over them with a
+ * softmax of the scaled scores, then the slots take an EMA step towards the
+ * weighted mean of the tokens that selected them and a 3-point Laplace
+ * diffusion along the slot axis. out = sum of the R attend outputs; indices
+ * and weights are those of the last round. Token keys and token values are q.
+ *
+ * Reference interface this replaces (beaglabs/murmurative-attention):
+ *   - torch-ext/torch_binding.cpp:6-33   TORCH_LIBRARY(murmurative_attention)
+ *     op schemas slot_select_attend / slot_update / slot_diffusion /
+ *     slot_update_diffuse and their _backward ops, which the Python round
+ *     loop src/murmurative/ops.py:330-422 (slot_murmurate) calls once per
+ *     phase per round;
+ *   - torch-ext/cuda_ops.h:6-68          the per-phase launcher signatures;
+ *   - src/murmurative/reference.py:138-191 the semantics (round loop).
+ * Here the whole round loop is one call; the per-phase ops are not exported.
+ *
+ * Conventions
+ *   - All tensors are device pointers on the current CUDA device. The caller
+ *     allocates everything: outputs, the `saved` block (written by forward,
+ *     read by backward, must stay untouched in between) and scratch
+ *     workspaces. Sizes come from murm_slot_murmurate_sizes(). Pointers must
+ *     be 16-byte aligned; `saved` and workspaces 256-byte aligned.
+ *   - Strides are in elements, {batch, head, row}; the innermost (head_dim)
+ *     stride is 1. A batch stride of 0 for slots_k / slots_v broadcasts one
+ *     slot table to every batch element.
+ *   - `stream` is a cudaStream_t. Calls only enqueue work; they never
+ *     synchronise the device and never allocate.
+ *   - Results are deterministic: the same inputs give bitwise-identical
+ *     outputs (no floating-point atomics anywhere).
+ *   - Errors come back as murm_status; murm_last_error_message() gives the
+ *     detail of the calling thread's last failure.
+ */
+#ifndef MURM_H_
+#define MURM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MURM_API __attribute__((visibility("default")))
+#else
+#define MURM_API
+#endif
+
+#define MURM_ABI_VERSION 1
+#define MURM_TOP_K 7
+
+typedef enum murm_status {
+  MURM_OK = 0,
+  MURM_ERR_INVALID_ARGUMENT = 1, /* shape, pointer, stride or size not valid   */
+  MURM_ERR_UNSUPPORTED = 2,      /* valid but not provided (top_k != 7, ...)    */
+  MURM_ERR_DTYPE = 3,            /* element type not fp32 / fp16 / bf16         */
+  MURM_ERR_WORKSPACE = 4,        /* saved / workspace block too small/unaligned */
+  MURM_ERR_CUDA = 5,             /* a CUDA runtime call or launch failed        */
+  MURM_ERR_DEVICE = 6            /* a kernel reported an error on the device    */
+} murm_status;
+
+typedef enum murm_dtype { MURM_F32 = 0, MURM_F16 = 1, MURM_BF16 = 2 } murm_dtype;
+
+typedef struct murm_shape {
+  int32_t batch;     /* B */
+  int32_t heads;     /* H */
+  int32_t tokens;    /* N, >= 1 */
+  int32_t slots;     /* M, 7 <= M <= 256 */
+  int32_t head_dim;  /* d, one of 16, 32, 64 */
+  int32_t rounds;    /* R, >= 0 */
+  int32_t top_k;     /* must be 7 */
+  int32_t causal;    /* nonzero: token n sees slots m <= n only */
+  double alpha;      /* EMA keep factor (reference default 0.9)   */
+  double gamma;      /* diffusion step (reference default 0.15)   */
+  double scale;      /* score scale; <= 0 means 1/sqrt(head_dim)  */
+  int32_t dtype;     /* murm_dtype of q, slots, out and gradients */
+} murm_shape;
+
+typedef struct murm_fwd_args {
+  murm_shape shape;
+  const void* q;       int64_t q_stride[3];   /* [B,H,N,d] */
+  const void* slots_k; int64_t sk_stride[3];  /* [B,H,M,d] */
+  const void* slots_v; int64_t sv_stride[3];  /* [B,H,M,d] */
+  void* out;           int64_t out_stride[3]; /* [B,H,N,d] */
+  int64_t* indices;    /* [B,H,N,7] contiguous int64, or NULL */
+  float* weights;      /* [B,H,N,7] contiguous fp32,  or NULL */
+  void* saved;         size_t saved_bytes;     /* kept for backward */
+  void* workspace;     size_t workspace_bytes; /* scratch */
+} murm_fwd_args;
+
+typedef struct murm_bwd_args {
+  murm_shape shape;                            /* same as the forward call */
+  const void* q;        int64_t q_stride[3];
+  const void* grad_out; int64_t go_stride[3];  /* dL/d out, [B,H,N,d] */
+  const float* grad_weights;                   /* dL/d weights [B,H,N,7] contiguous, or NULL */
+  const void* saved;    size_t saved_bytes;    /* written by the forward call */
+  void* grad_q;         int64_t gq_stride[3];
+  void* grad_slots_k;   int64_t gsk_stride[3]; /* [B,H,M,d]; batch stride must be nonzero */
+  void* grad_slots_v;   int64_t gsv_stride[3];
+  void* workspace;      size_t workspace_bytes;
+} murm_bwd_args;
+
+/* Bytes of the saved block and of the forward / backward scratch workspaces.
+ * Any output pointer may be NULL. */
+MURM_API murm_status murm_slot_murmurate_sizes(const murm_shape* shape, size_t* saved_bytes,
+                                      size_t* fwd_workspace_bytes,
+                                      size_t* bwd_workspace_bytes);
+
+/* Forward. Replaces the per-round ops.py:376-419 loop of
+ * slot_select_attend (torch_binding.cpp:7-10) + slot_update_diffuse
+ * (torch_binding.cpp:29-32). */
+MURM_API murm_status murm_slot_murmurate_fwd(const murm_fwd_args* args, void* stream);
+
+/* Backward. Replaces slot_select_attend_backward (torch_binding.cpp:11-14),
+ * slot_update_backward (19-22) and slot_diffusion_backward (26-28) chained by
+ * autograd through ops.py:75-92 and 188-208. */
+MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* stream);
+
+MURM_API const char* murm_status_string(murm_status status);
+MURM_API const char* murm_last_error_message(void);
+MURM_API int32_t murm_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MURM_H_ */

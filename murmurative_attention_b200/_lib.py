@@ -1,0 +1,126 @@
+"""ctypes binding of ``libmurm_b200.so`` (the C ABI in include/murm.h).
+
+Replaces the reference's extension loader (src/murmurative/_cuda_kernels.py:
+``ensure_compiled``): it loads the in-tree shared library once and raises
+``RuntimeError`` when the library is missing or CUDA is unavailable. There is
+no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmurm_b200.so")
+
+MURM_F32, MURM_F16, MURM_BF16 = 0, 1, 2
+TOP_K = 7
+
+
+class Shape(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("tokens", ctypes.c_int32),
+        ("slots", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("rounds", ctypes.c_int32),
+        ("top_k", ctypes.c_int32), ("causal", ctypes.c_int32),
+        ("alpha", ctypes.c_double), ("gamma", ctypes.c_double), ("scale", ctypes.c_double),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+Strides = ctypes.c_int64 * 3
+
+
+class FwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", Shape),
+        ("q", ctypes.c_void_p), ("q_stride", Strides),
+        ("slots_k", ctypes.c_void_p), ("sk_stride", Strides),
+        ("slots_v", ctypes.c_void_p), ("sv_stride", Strides),
+        ("out", ctypes.c_void_p), ("out_stride", Strides),
+        ("indices", ctypes.c_void_p),
+        ("weights", ctypes.c_void_p),
+        ("saved", ctypes.c_void_p), ("saved_bytes", ctypes.c_size_t),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class BwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", Shape),
+        ("q", ctypes.c_void_p), ("q_stride", Strides),
+        ("grad_out", ctypes.c_void_p), ("go_stride", Strides),
+        ("grad_weights", ctypes.c_void_p),
+        ("saved", ctypes.c_void_p), ("saved_bytes", ctypes.c_size_t),
+        ("grad_q", ctypes.c_void_p), ("gq_stride", Strides),
+        ("grad_slots_k", ctypes.c_void_p), ("gsk_stride", Strides),
+        ("grad_slots_v", ctypes.c_void_p), ("gsv_stride", Strides),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Every symbol include/murm.h declares; tests check the library exports them all.
+EXPORTS = (
+    "murm_slot_murmurate_sizes",
+    "murm_slot_murmurate_fwd",
+    "murm_slot_murmurate_bwd",
+    "murm_status_string",
+    "murm_last_error_message",
+    "murm_abi_version",
+)
+
+STATUS_NAMES = {
+    0: "MURM_OK", 1: "MURM_ERR_INVALID_ARGUMENT", 2: "MURM_ERR_UNSUPPORTED", 3: "MURM_ERR_DTYPE",
+    4: "MURM_ERR_WORKSPACE", 5: "MURM_ERR_CUDA", 6: "MURM_ERR_DEVICE",
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the shared library (no CUDA device needed) and declare prototypes."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"murmurative_attention_b200: CUDA library not built ({path} missing). "
+                "Build it with:  python -m murmurative_attention_b200.build")
+        lib = ctypes.CDLL(path)
+        lib.murm_slot_murmurate_sizes.argtypes = [ctypes.POINTER(Shape), ctypes.POINTER(ctypes.c_size_t),
+                                                  ctypes.POINTER(ctypes.c_size_t),
+                                                  ctypes.POINTER(ctypes.c_size_t)]
+        lib.murm_slot_murmurate_sizes.restype = ctypes.c_int
+        lib.murm_slot_murmurate_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.murm_slot_murmurate_fwd.restype = ctypes.c_int
+        lib.murm_slot_murmurate_bwd.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
+        lib.murm_slot_murmurate_bwd.restype = ctypes.c_int
+        lib.murm_status_string.argtypes = [ctypes.c_int]
+        lib.murm_status_string.restype = ctypes.c_char_p
+        lib.murm_last_error_message.argtypes = []
+        lib.murm_last_error_message.restype = ctypes.c_char_p
+        lib.murm_abi_version.argtypes = []
+        lib.murm_abi_version.restype = ctypes.c_int32
+        if lib.murm_abi_version() != 1:
+            raise RuntimeError("murmurative_attention_b200: libmurm_b200.so ABI version mismatch; rebuild it")
+        _lib = lib
+        return lib
+
+
+class MurmError(RuntimeError):
+    """A status other than MURM_OK from the C ABI."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+def check(status: int) -> None:
+    if status == 0:
+        return
+    msg = _lib.murm_last_error_message().decode() if _lib is not None else ""
+    if status == 3:
+        raise TypeError(msg)
+    raise MurmError(status, msg)

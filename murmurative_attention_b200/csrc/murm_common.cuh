@@ -1,0 +1,114 @@
+// murm_common.cuh — shared definitions for the slot_murmurate kernels.
+//
+// Numerics follow the reference's fp32 CPU path (src/murmurative/reference.py):
+// every slot-state quantity is fp32, and the EMA / diffusion arithmetic uses
+// explicitly rounded operations in the order reference.py evaluates them, so
+// no fused multiply-add changes a rounding there.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/murm.h"
+
+namespace murm {
+
+constexpr int kTopK = MURM_TOP_K;  // reference.py:38 hard-codes k = 7
+constexpr int kMaxSlots = 256;     // indices are stored as one byte per pick
+constexpr float kEmaEps = 1e-8f;   // reference.py:106-107
+constexpr int kTile = 128;         // tokens per tile (one thread or TMEM lane each)
+
+// ---------------------------------------------------------------------------
+// Element types
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
+  static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+
+// Order-preserving map of an fp32 score onto uint32. 0 means "empty" and is
+// below every real key, including -inf (0x007FFFFF); NaN ranks above +inf as in
+// torch.topk. Equal scores give equal keys; the selection keeps the earlier
+// (lower) slot index on equal keys.
+__device__ __forceinline__ uint32_t rank_key(float x) {
+  uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+constexpr uint32_t kNegInfKey = 0x007FFFFFu;
+
+// Sorted (descending) top-7 list. Insert only when key > k[6].
+struct Top7 {
+  uint32_t k[kTopK];
+  int i[kTopK];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) { k[j] = 0u; i[j] = 0; }
+  }
+  __device__ __forceinline__ void insert(uint32_t key, int idx) {
+    bool done = false;
+#pragma unroll
+    for (int j = kTopK - 1; j > 0; --j) {
+      const bool shift = !done && key > k[j - 1];
+      const bool place = !done && !shift;
+      k[j] = shift ? k[j - 1] : (place ? key : k[j]);
+      i[j] = shift ? i[j - 1] : (place ? idx : i[j]);
+      done = done || place;
+    }
+    if (!done) { k[0] = key; i[0] = idx; }
+  }
+  __device__ __forceinline__ void offer(uint32_t key, int idx) {
+    if (key > k[kTopK - 1]) insert(key, idx);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Problem description shared by host and device
+// ---------------------------------------------------------------------------
+struct Geom {
+  int B, H, N, M, D, R, causal;
+  int BH;
+  float alpha, one_minus_alpha, gamma, scale;
+  // token chunks: chunk c covers tokens [c*chunk_tokens, min(N, (c+1)*chunk_tokens))
+  int fwd_chunks, fwd_chunk_tokens;   // select/attend kernels (one tile per CTA)
+  int red_chunks, red_chunk_tokens;   // reduction kernels (many tiles per CTA)
+};
+
+// Round records kept from forward to backward and scratch areas. All fp32
+// slot tensors are [BH][M][D] row-major; token tensors [BH][N][...].
+struct Saved {
+  float* K;      // [R][BH][M][D] slot keys entering round r
+  float* V;      // [R][BH][M][D] slot values entering round r
+  float* U;      // [R][BH][M][D] update means ksum/(wsum+eps) of round r
+  float* W;      // [R][BH][M]    weight sums of round r
+  uint8_t* idx;  // [R][BH][N][8] selected slots (7 used)
+  float* w;      // [R][BH][N][8] softmax weights (7 used)
+};
+struct FwdScratch {
+  float* Spart;  // [BH][red_chunks][M][D]
+  float* Wpart;  // [BH][red_chunks][M]
+};
+struct BwdScratch {
+  float* dK[2];  // [BH][M][D] ping-pong slot-key gradients
+  float* dV[2];
+  float* dS;     // [BH][M][D] gradient w.r.t. the update sum
+  float* dW;     // [BH][M]    gradient w.r.t. the weight sum
+  float* dKdir;  // [BH][M][D] direct (EMA-kept) part of dK
+  float* dVdir;
+  float* dKpart; // [BH][red_chunks][M][D]
+  float* dVpart;
+  float* coef;   // [BH][N][8] scale * dlogit per pick
+  float* dq;     // [BH][N][D] running dL/dq over rounds
+};
+
+}  // namespace murm

@@ -1,0 +1,45 @@
+// murm_kernels.cuh — launcher interfaces between the C ABI layer and the kernels.
+#pragma once
+
+#include "murm_common.cuh"
+
+namespace murm {
+
+struct Strides3 {
+  int64_t s[3];  // {batch, head, row}, elements
+};
+
+template <typename T>
+__host__ __device__ __forceinline__ const T* row_ptr(const T* base, Strides3 st, int b, int h, int n) {
+  return base + (int64_t)b * st.s[0] + (int64_t)h * st.s[1] + (int64_t)n * st.s[2];
+}
+template <typename T>
+__host__ __device__ __forceinline__ T* row_ptr(T* base, Strides3 st, int b, int h, int n) {
+  return base + (int64_t)b * st.s[0] + (int64_t)h * st.s[1] + (int64_t)n * st.s[2];
+}
+
+struct FwdPtrs {
+  const void* q;  Strides3 qs;
+  const void* sk; Strides3 sks;
+  const void* sv; Strides3 svs;
+  void* out;      Strides3 os;
+  int64_t* indices;
+  float* weights;
+};
+
+struct BwdPtrs {
+  const void* q;  Strides3 qs;
+  const void* go; Strides3 gos;
+  const float* gw;
+  void* gq;  Strides3 gqs;
+  void* gsk; Strides3 gsks;
+  void* gsv; Strides3 gsvs;
+};
+
+// CUDA-core path (murm_simt.cu): every dtype, head_dim 16/32/64.
+template <typename T>
+cudaError_t fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st);
+template <typename T>
+cudaError_t bwd_simt(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdScratch& bs, cudaStream_t st);
+
+}  // namespace murm

@@ -1,0 +1,95 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol
+include/murm.h declares, its structs match the ctypes mirror, and argument
+validation reports the documented status codes."""
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from murmurative_attention_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "murm.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MURM_API\s+[\w\s\*]+?\b(murm_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load_library()
+    declared = header_functions()
+    assert declared, "no MURM_API declarations found"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in murm.h but not exported"
+    assert sorted(_lib.EXPORTS) == declared
+
+
+def test_abi_version():
+    assert _lib.load_library().murm_abi_version() == 1
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "murm.h"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu\\n\", sizeof(murm_shape), sizeof(murm_fwd_args),"
+        " sizeof(murm_bwd_args), offsetof(murm_shape, alpha), offsetof(murm_fwd_args, saved),"
+        " offsetof(murm_bwd_args, workspace)); return 0;}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    want = [ctypes.sizeof(_lib.Shape), ctypes.sizeof(_lib.FwdArgs), ctypes.sizeof(_lib.BwdArgs),
+            _lib.Shape.alpha.offset, _lib.FwdArgs.saved.offset, _lib.BwdArgs.workspace.offset]
+    assert [int(x) for x in got] == want
+
+
+def _sizes(**kw):
+    lib = _lib.load_library()
+    base = dict(batch=1, heads=16, tokens=8192, slots=256, head_dim=64, rounds=3, top_k=7, causal=0,
+                alpha=0.9, gamma=0.15, scale=0.0, dtype=_lib.MURM_F16)
+    base.update(kw)
+    s = _lib.Shape(**base)
+    a, b, c = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+    st = lib.murm_slot_murmurate_sizes(ctypes.byref(s), ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+    return st, a.value, b.value, c.value
+
+
+def test_sizes_scale_with_problem():
+    st, saved, fws, bws = _sizes()
+    assert st == 0 and saved > 0 and fws > 0 and bws > 0
+    st2, saved2, _, _ = _sizes(rounds=6)
+    assert st2 == 0 and saved2 > saved
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(top_k=5), 2),          # MURM_ERR_UNSUPPORTED: reference hard-codes k=7
+    (dict(slots=6), 1),          # fewer slots than picks (torch.topk raises too)
+    (dict(slots=300), 2),        # beyond one-byte slot indices
+    (dict(head_dim=48), 2),
+    (dict(tokens=0), 1),
+    (dict(rounds=-1), 1),
+    (dict(dtype=7), 3),          # MURM_ERR_DTYPE
+])
+def test_sizes_rejects_bad_shapes(kw, status):
+    st, *_ = _sizes(**kw)
+    assert st == status
+    msg = _lib.load_library().murm_last_error_message().decode()
+    assert msg
+
+
+def test_null_args_rejected_without_gpu():
+    lib = _lib.load_library()
+    assert lib.murm_slot_murmurate_fwd(None, None) == 1
+    assert lib.murm_slot_murmurate_bwd(None, None) == 1
+
+
+def test_status_strings():
+    lib = _lib.load_library()
+    for code in range(7):
+        assert lib.murm_status_string(code)
