@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""Benchmark: slot_murmurate forward + backward tokens/s on B200.
+
+Workload: B=1, H=16, N=8192, d=64, M=256, R=3, k=7,
+non-causal, fp16, the inputs of BASELINE configs[1] (q ~ N(0,1), slots_k ~
+N(0,1), slots_v = 0) plus grad_out ~ N(0,1) for the backward. One step = one
+forward and one backward pass over that batch. With N GPUs (torchrun, one
+process per GPU) every rank runs its own batch of 16 (batch, head) pairs —
+(b,h) pairs are independent, so there is no collective on the data path —
+and ``value`` is all ranks' tokens divided by the slowest rank's time
+(weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line. ``value`` is measured with the inputs resident
+in HBM, the step replayed from a CUDA graph, L2 flushed (256 MiB write)
+before every timed step and CUDA events around each step. ``e2e`` is the same
+metric through the public API (murmurative_attention_b200.slot_murmurate +
+autograd backward) with pinned host buffers: every step copies q, slots and
+grad_out to the device and copies out, indices, weights and the three
+gradients back. ``roofline`` covers the kernel with the largest device time,
+timed with CUDA events recorded on its own launch stream.
+``--impl reference`` times the reference's CPU path (the oracle port, which
+runs the reference.py operations) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "slot_murmurate fwd+bwd tokens/s at N=8192, 1/2/4/8 B200; % of roofline"
+WL = dict(B=1, H=16, N=8192, D=64, M=256, R=3, causal=False)
+DTYPE = torch.float16
+ESIZE = 2
+
+
+def workload_config(extra=None):
+    cfg = {"workload": "northstar: BASELINE configs[1] inputs (fp16 q~N(0,1) [1,16,8192,64], slots_k~N(0,1) "
+                       "[1,16,256,64], slots_v=0) with backward (grad_out~N(0,1)); R=3, k=7, non-causal",
+           "batch_per_rank": WL["B"], "heads": WL["H"], "tokens": WL["N"], "head_dim": WL["D"], "slots": WL["M"],
+           "rounds": WL["R"], "top_k": 7, "causal": WL["causal"],
+           "l2": "flushed by a 256 MiB write before every timed step (inputs 16 MiB < 126 MB L2)"}
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+def algorithmic_bytes():
+    """Every tensor touched once (fwd: q in, out/idx/w out; bwd: q, grad_out in, grad_q out;
+    slots read and written once per direction)."""
+    BH, N, D, M = WL["B"] * WL["H"], WL["N"], WL["D"], WL["M"]
+    per_token = 5 * D * ESIZE + 7 * 8 + 7 * 4
+    return BH * N * per_token + BH * 6 * M * D * ESIZE
+
+
+def select_flops_per_round():
+    return 2 * WL["M"] * WL["D"] * WL["B"] * WL["H"] * WL["N"]
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm_gbs=j["hbm_gbs"], bf16_tflops=j["bf16_tflops"],
+                    bf16_tflops_sustained=j.get("bf16_tflops_sustained"), source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, source="fallback")
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.dev = device_index
+
+    def start(self):
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.dev).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+class AbiStep:
+    """One fwd+bwd step through the C ABI with preallocated device buffers."""
+
+    def __init__(self, q, sk, sv, go):
+        from murmurative_attention_b200 import _lib, ops
+        self._lib = _lib
+        self.lib = _lib.load_library()
+        B, H, N, D = q.shape
+        self.shape = ops._make_shape(q, sk.shape[2], WL["R"], 7, WL["causal"], 0.9, 0.15, None)
+        saved_b, fws_b, bws_b = ops.slot_murmurate_sizes(self.shape)
+        dev = q.device
+        self.keep = dict(q=q, sk=sk, sv=sv, go=go)
+        self.out = torch.empty_like(q)
+        self.idx = torch.empty(B, H, N, 7, dtype=torch.int64, device=dev)
+        self.w = torch.empty(B, H, N, 7, dtype=torch.float32, device=dev)
+        self.saved = torch.empty(saved_b, dtype=torch.uint8, device=dev)
+        self.fws = torch.empty(fws_b, dtype=torch.uint8, device=dev)
+        self.bws = torch.empty(bws_b, dtype=torch.uint8, device=dev)
+        self.gq = torch.empty_like(q)
+        self.gsk = torch.empty_like(sk)
+        self.gsv = torch.empty_like(sv)
+        S = ops._strides
+        self.fargs = _lib.FwdArgs(self.shape, q.data_ptr(), S(q), sk.data_ptr(), S(sk), sv.data_ptr(), S(sv),
+                                  self.out.data_ptr(), S(self.out), self.idx.data_ptr(), self.w.data_ptr(),
+                                  self.saved.data_ptr(), saved_b, self.fws.data_ptr(), fws_b)
+        self.bargs = _lib.BwdArgs(self.shape, q.data_ptr(), S(q), go.data_ptr(), S(go), None,
+                                  self.saved.data_ptr(), saved_b, self.gq.data_ptr(), S(self.gq),
+                                  self.gsk.data_ptr(), S(self.gsk), self.gsv.data_ptr(), S(self.gsv),
+                                  self.bws.data_ptr(), bws_b)
+
+    def __call__(self):
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self._lib.check(self.lib.murm_slot_murmurate_fwd(ctypes.byref(self.fargs), st))
+        self._lib.check(self.lib.murm_slot_murmurate_bwd(ctypes.byref(self.bargs), st))
+
+
+def make_inputs(device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, H, N, D, M = WL["B"], WL["H"], WL["N"], WL["D"], WL["M"]
+    q = torch.randn(B, H, N, D, generator=g, device=device).to(DTYPE)
+    sk = torch.randn(B, H, M, D, generator=g, device=device).to(DTYPE)
+    sv = torch.zeros(B, H, M, D, device=device, dtype=DTYPE)
+    go = torch.randn(B, H, N, D, generator=g, device=device).to(DTYPE)
+    return q, sk, sv, go
+
+
+def time_steps(fn, steps, flush_buf):
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush_buf.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from murmurative_attention_b200 import _lib, slot_murmurate
+
+    q, sk, sv, go = make_inputs(dev, seed=1000 + rank)
+    step = AbiStep(q, sk, sv, go)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+
+    # launches per step (counted by the library)
+    n0 = _lib.kernel_launches()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.kernel_launches() - n0
+
+    # replay the step from a CUDA graph (no host launch overhead in the timed region)
+    fn = step
+    graph_used = False
+    if not args.no_graph:
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                step()
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            g.replay()
+            torch.cuda.synchronize()
+            fn = g.replay
+            graph_used = True
+        except Exception as e:  # noqa: BLE001
+            print(f"[bench] CUDA graph capture failed, timing eager launches: {e}", file=sys.stderr)
+            fn = step
+    for _ in range(args.warmup):
+        fn()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    times = time_steps(fn, args.steps, flush)
+    clk = clocks.stop()
+    barrier(world)
+    total_ms = max_over_ranks(sum(times), world)
+    ms_per_step = total_ms / args.steps
+    tokens_per_step = WL["B"] * WL["N"] * world
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    # per-kernel device time (eager launches, events on the launch stream)
+    prof_steps = min(args.steps, 20)
+    _lib.profile_begin()
+    for _ in range(prof_steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    prof = _lib.profile_end()
+
+    # end to end through the public API with host buffers
+    e2e = run_e2e(q, sk, sv, go, min(args.steps, 20), args.warmup, flush, slot_murmurate, world)
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    peaks = load_peaks()
+    roof = roofline(prof, prof_steps, peaks)
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": workload_config({"parallelism": f"(batch,head)-sharded weak scaling, {world} rank(s)",
+                                       "timing": "CUDA graph replay" if graph_used else "eager launches"}),
+            "roofline": roof, "e2e": e2e, "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk,
+            "kernels": {k: {"launches_per_step": v[0] / prof_steps, "ms_per_step": round(v[1] / prof_steps, 5)}
+                        for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}}
+    if world == 1 and not args.skip_cpu:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def roofline(prof, prof_steps, peaks):
+    if not prof:
+        return None
+    name, (launches, total) = max(prof.items(), key=lambda kv: kv[1][1])
+    avg_ms = total / launches
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(name)
+    if name.startswith("select"):
+        flops = select_flops_per_round()  # one round per launch
+        achieved = flops / (avg_ms / 1e3) / 1e12
+        return {"kernel": name, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} (burst dense bf16)",
+                "work_per_launch": f"select GEMM 2*M*d*tokens = {flops:.4g} FLOP",
+                "avg_launch_ms": round(avg_ms, 5), "launches": launches}
+    # memory-bound kernels: algorithmic bytes of the whole step spread over its launches
+    per_launch = algorithmic_bytes() / (launches / prof_steps)
+    achieved = per_launch / (avg_ms / 1e3) / 1e9
+    return {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+            "peak_source": f"{peaks['source']} copy bandwidth", "avg_launch_ms": round(avg_ms, 5),
+            "launches": launches}
+
+
+def run_e2e(q, sk, sv, go, steps, warmup, flush, op, world):
+    host = {k: t.detach().cpu().pin_memory() for k, t in dict(q=q, sk=sk, sv=sv, go=go).items()}
+    dev = q.device
+    outs = None
+
+    def one():
+        nonlocal outs
+        qd = host["q"].to(dev, non_blocking=True).requires_grad_(True)
+        skd = host["sk"].to(dev, non_blocking=True).requires_grad_(True)
+        svd = host["sv"].to(dev, non_blocking=True).requires_grad_(True)
+        god = host["go"].to(dev, non_blocking=True)
+        out, idx, w = op(qd, skd, svd, rounds=WL["R"], causal=WL["causal"])
+        out.backward(god)
+        res = (out.detach(), idx, w.detach(), qd.grad, skd.grad, svd.grad)
+        if outs is None:
+            outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in res]
+        for h, t in zip(outs, res):
+            h.copy_(t, non_blocking=True)
+
+    for _ in range(max(warmup, 1)):
+        one()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(one, steps, flush)
+    total = max_over_ranks(sum(times), world)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+    ms = total / steps
+    return {"value": round(WL["B"] * WL["N"] * world / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "path": "murmurative_attention_b200.slot_murmurate + autograd backward, pinned host buffers"}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference path (oracle port of reference.py) on the host cores
+# ---------------------------------------------------------------------------
+def cpu_sample_step(heads, seed=0):
+    import oracle
+    g = torch.Generator().manual_seed(seed)
+    N, D, M = WL["N"], WL["D"], WL["M"]
+    q = torch.randn(1, heads, N, D, generator=g).to(DTYPE).float().requires_grad_(True)
+    sk = torch.randn(1, heads, M, D, generator=g).to(DTYPE).float().requires_grad_(True)
+    sv = torch.zeros(1, heads, M, D, requires_grad=True)
+    go = torch.randn(1, heads, N, D, generator=g).to(DTYPE).float()
+
+    def step():
+        q.grad = sk.grad = sv.grad = None
+        out, idx, w = oracle.slot_murmurate(q, sk, sv, rounds=WL["R"], causal=WL["causal"], tie_rule="topk")
+        out.backward(go)
+    return step
+
+
+def cpu_baseline(seconds=12.0, heads=2):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step = cpu_sample_step(heads)
+    step()  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        step()
+        n += 1
+        if time.perf_counter() - t0 >= seconds and n >= 2:
+            break
+    dt = (time.perf_counter() - t0) / n
+    full = dt * (WL["B"] * WL["H"]) / heads  # (b,h) pairs are independent: time scales with their count
+    return {"value": round(WL["B"] * WL["N"] / full, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{heads} of {WL['B'] * WL['H']} (batch,head) pairs of the workload, fwd+bwd, fp32 CPU, "
+                      f"{n} timed steps of {dt * 1e3:.0f} ms, scaled by the pair count",
+            "cpu": cpu_model()}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    heads = 1
+    step = cpu_sample_step(heads)
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    full = dt * (WL["B"] * WL["H"]) / heads
+    value = round(WL["B"] * WL["N"] / full, 1)
+    sample = (f"{heads} of {WL['B'] * WL['H']} (batch,head) pairs per step, fwd+bwd, fp32 CPU (reference.py "
+              f"operations, torch.topk), scaled by the pair count")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(full * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": workload_config({"parallelism": "host CPU, one process"}),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample, "cpu": cpu_model()},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -125,6 +125,22 @@ MURM_API murm_status murm_slot_murmurate_fwd(const murm_fwd_args* args, void* st
  * autograd through ops.py:75-92 and 188-208. */
 MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* stream);
 
+/* Launch accounting and per-kernel timing (host-side instrumentation; no
+ * effect on results). murm_kernel_launches() counts every kernel this library
+ * has launched in the process. Between murm_profile_begin() and
+ * murm_profile_end() every launch is bracketed by CUDA events recorded on the
+ * launch's own stream; murm_profile_end() waits for them and returns, per
+ * kernel name, the launch count and summed device time. */
+typedef struct murm_kernel_time {
+  char name[48];
+  int64_t launches;
+  double total_ms;
+} murm_kernel_time;
+
+MURM_API uint64_t murm_kernel_launches(void);
+MURM_API murm_status murm_profile_begin(void);
+MURM_API murm_status murm_profile_end(murm_kernel_time* out, int32_t capacity, int32_t* count);
+
 MURM_API const char* murm_status_string(murm_status status);
 MURM_API const char* murm_last_error_message(void);
 MURM_API int32_t murm_abi_version(void);

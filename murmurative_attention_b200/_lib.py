@@ -31,6 +31,10 @@ class Shape(ctypes.Structure):
 Strides = ctypes.c_int64 * 3
 
 
+class KernelTime(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
+
+
 class FwdArgs(ctypes.Structure):
     _fields_ = [
         ("shape", Shape),
@@ -67,6 +71,9 @@ EXPORTS = (
     "murm_status_string",
     "murm_last_error_message",
     "murm_abi_version",
+    "murm_kernel_launches",
+    "murm_profile_begin",
+    "murm_profile_end",
 )
 
 STATUS_NAMES = {
@@ -103,6 +110,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_last_error_message.restype = ctypes.c_char_p
         lib.murm_abi_version.argtypes = []
         lib.murm_abi_version.restype = ctypes.c_int32
+        lib.murm_kernel_launches.argtypes = []
+        lib.murm_kernel_launches.restype = ctypes.c_uint64
+        lib.murm_profile_begin.argtypes = []
+        lib.murm_profile_begin.restype = ctypes.c_int
+        lib.murm_profile_end.argtypes = [ctypes.POINTER(KernelTime), ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
+        lib.murm_profile_end.restype = ctypes.c_int
         if lib.murm_abi_version() != 1:
             raise RuntimeError("murmurative_attention_b200: libmurm_b200.so ABI version mismatch; rebuild it")
         _lib = lib
@@ -124,3 +137,22 @@ def check(status: int) -> None:
     if status == 3:
         raise TypeError(msg)
     raise MurmError(status, msg)
+
+
+def kernel_launches() -> int:
+    """Kernels this library has launched in this process."""
+    return int(load_library().murm_kernel_launches())
+
+
+def profile_begin() -> None:
+    check(load_library().murm_profile_begin())
+
+
+def profile_end() -> dict:
+    """{kernel name: (launches, total device ms)} since profile_begin()."""
+    lib = load_library()
+    cap = 64
+    buf = (KernelTime * cap)()
+    n = ctypes.c_int32()
+    check(lib.murm_profile_end(buf, cap, ctypes.byref(n)))
+    return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(min(n.value, cap))}

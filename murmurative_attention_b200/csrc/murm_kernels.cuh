@@ -36,6 +36,16 @@ struct BwdPtrs {
   void* gsv; Strides3 gsvs;
 };
 
+// Launch accounting (murm_profile.cu). Every launch goes through MURM_LAUNCH.
+void launch_begin(const char* name, cudaStream_t st);
+void launch_end(cudaStream_t st);
+#define MURM_LAUNCH(name, kernel, grid, block, smem, stream, ...)        \
+  do {                                                                   \
+    ::murm::launch_begin(name, stream);                                  \
+    kernel<<<grid, block, smem, stream>>>(__VA_ARGS__);                  \
+    ::murm::launch_end(stream);                                          \
+  } while (0)
+
 // CUDA-core path (murm_simt.cu): every dtype, head_dim 16/32/64.
 template <typename T>
 cudaError_t fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st);

@@ -580,22 +580,26 @@ static cudaError_t run_fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv
   const int smem_sa = 2 * g.M * D * (int)sizeof(float);
   const int smem_up = (g.M * D + g.M + kTile * D + kTile * 8) * 4 + g.M * 16 + (kMaxSlots + 4 + 8) * 4 +
                       kTile * 8 + 2 * kTile * kTopK;
-  cudaFuncSetAttribute(k_select_attend<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sa);
-  cudaFuncSetAttribute(k_update_partial<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
+  static int attr_smem = 0;  // dynamic-smem opt-in once per instantiation (largest size seen)
+  if (smem_sa > attr_smem || smem_up > attr_smem) {
+    cudaFuncSetAttribute(k_select_attend<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sa);
+    cudaFuncSetAttribute(k_update_partial<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
+    attr_smem = smem_sa > smem_up ? smem_sa : smem_up;
+  }
   const T* q = static_cast<const T*>(p.q);
   if (g.R > 0)  // with zero rounds the saved block is empty and nothing reads the slots
-    k_load_slots<T><<<dim3(g.BH, 4), 256, 0, st>>>(g, static_cast<const T*>(p.sk), p.sks,
+    MURM_LAUNCH("load_slots", k_load_slots<T>, dim3(g.BH, 4), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
                                                     static_cast<const T*>(p.sv), p.svs, sv.K, sv.V);
   for (int r = 0; r < g.R; ++r) {
-    k_select_attend<T, D><<<dim3(g.fwd_chunks, g.BH), kTile, smem_sa, st>>>(
+    MURM_LAUNCH("select_attend_simt", (k_select_attend<T, D>), dim3(g.fwd_chunks, g.BH), kTile, smem_sa, st, 
         g, r, q, p.qs, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv);
     if (r + 1 < g.R) {
-      k_update_partial<T, D><<<dim3(g.red_chunks, g.BH), 256, smem_up, st>>>(g, r, q, p.qs, sv, fs);
-      k_update_finalize<<<dim3(g.BH, g.D / 8), 256, 0, st>>>(g, r, sv, fs);
+      MURM_LAUNCH("update_partial", (k_update_partial<T, D>), dim3(g.red_chunks, g.BH), 256, smem_up, st, g, r, q, p.qs, sv, fs);
+      MURM_LAUNCH("update_finalize", k_update_finalize, dim3(g.BH, g.D / 8), 256, 0, st, g, r, sv, fs);
     }
   }
   if (g.R == 0) {
-    k_fill_zero_rows<T><<<g.BH, 256, 0, st>>>(g, static_cast<T*>(p.out), p.os, g.N);
+    MURM_LAUNCH("fill_zero", k_fill_zero_rows<T>, g.BH, 256, 0, st, g, static_cast<T*>(p.out), p.os, g.N);
     const size_t n7 = (size_t)g.BH * g.N * kTopK;
     if (p.indices) cudaMemsetAsync(p.indices, 0, n7 * sizeof(int64_t), st);
     if (p.weights) cudaMemsetAsync(p.weights, 0, n7 * sizeof(float), st);
@@ -609,25 +613,29 @@ static cudaError_t run_bwd_simt(const Geom& g, const BwdPtrs& p, const Saved& sv
   const int smem_tok = (3 * g.M * D + g.M) * (int)sizeof(float);
   const int smem_sc = (2 * g.M * D + 2 * kTile * D + 2 * kTile * 8) * 4 + g.M * 16 + (kMaxSlots + 4 + 8) * 4 +
                       kTile * 8 + 2 * kTile * kTopK;
-  cudaFuncSetAttribute(k_bwd_tokens<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_tok);
-  cudaFuncSetAttribute(k_bwd_scatter<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sc);
+  static int attr_smem = 0;
+  if (smem_tok > attr_smem || smem_sc > attr_smem) {
+    cudaFuncSetAttribute(k_bwd_tokens<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_tok);
+    cudaFuncSetAttribute(k_bwd_scatter<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sc);
+    attr_smem = smem_tok > smem_sc ? smem_tok : smem_sc;
+  }
   const T* q = static_cast<const T*>(p.q);
   const T* go = static_cast<const T*>(p.go);
   if (g.R == 0) {
-    k_fill_zero_rows<T><<<g.BH, 256, 0, st>>>(g, static_cast<T*>(p.gq), p.gqs, g.N);
-    k_fill_zero_rows<T><<<g.BH, 256, 0, st>>>(g, static_cast<T*>(p.gsk), p.gsks, g.M);
-    k_fill_zero_rows<T><<<g.BH, 256, 0, st>>>(g, static_cast<T*>(p.gsv), p.gsvs, g.M);
+    MURM_LAUNCH("fill_zero", k_fill_zero_rows<T>, g.BH, 256, 0, st, g, static_cast<T*>(p.gq), p.gqs, g.N);
+    MURM_LAUNCH("fill_zero", k_fill_zero_rows<T>, g.BH, 256, 0, st, g, static_cast<T*>(p.gsk), p.gsks, g.M);
+    MURM_LAUNCH("fill_zero", k_fill_zero_rows<T>, g.BH, 256, 0, st, g, static_cast<T*>(p.gsv), p.gsvs, g.M);
     return cudaGetLastError();
   }
   int cur = 0;
   const int fin_y = (g.M * D + 255) / 256;
   for (int r = g.R - 1; r >= 0; --r) {
     const int has_slot_grad = r < g.R - 1;
-    if (has_slot_grad) k_bwd_prep<<<g.BH, 256, 0, st>>>(g, r, sv, bs.dK[cur], bs.dV[cur], bs);
-    k_bwd_tokens<T, D><<<dim3(g.fwd_chunks, g.BH), kTile, smem_tok, st>>>(
+    if (has_slot_grad) MURM_LAUNCH("bwd_prep", k_bwd_prep, g.BH, 256, 0, st, g, r, sv, bs.dK[cur], bs.dV[cur], bs);
+    MURM_LAUNCH("bwd_tokens", (k_bwd_tokens<T, D>), dim3(g.fwd_chunks, g.BH), kTile, smem_tok, st, 
         g, r, has_slot_grad, q, p.qs, go, p.gos, p.gw, static_cast<T*>(p.gq), p.gqs, sv, bs);
-    k_bwd_scatter<T, D><<<dim3(g.red_chunks, g.BH), 256, smem_sc, st>>>(g, r, q, p.qs, go, p.gos, sv, bs);
-    k_bwd_finalize<T><<<dim3(g.BH, fin_y), 256, 0, st>>>(g, r, bs, has_slot_grad, bs.dK[cur ^ 1],
+    MURM_LAUNCH("bwd_scatter", (k_bwd_scatter<T, D>), dim3(g.red_chunks, g.BH), 256, smem_sc, st, g, r, q, p.qs, go, p.gos, sv, bs);
+    MURM_LAUNCH("bwd_finalize", k_bwd_finalize<T>, dim3(g.BH, fin_y), 256, 0, st, g, r, bs, has_slot_grad, bs.dK[cur ^ 1],
                                                            bs.dV[cur ^ 1], static_cast<T*>(p.gsk), p.gsks,
                                                            static_cast<T*>(p.gsv), p.gsvs);
     cur ^= 1;
