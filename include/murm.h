@@ -125,6 +125,24 @@ MURM_API murm_status murm_slot_murmurate_fwd(const murm_fwd_args* args, void* st
  * autograd through ops.py:75-92 and 188-208. */
 MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* stream);
 
+/* Forward that needs no caller-provided scratch. No counterpart in the
+ * reference. For callers that cannot allocate device memory: a serving plugin
+ * that is handed only its input and output buffers under a memory budget fixed
+ * at start-up, code running inside a global-mode CUDA stream capture (where
+ * cudaMalloc is not permitted), or a foreign-language host with no binding to
+ * the CUDA allocator. The round records and partial sums live in one
+ * file-scope device array of MURM_NOSCRATCH_BYTES (64 MiB) that every GPU
+ * loading this library holds until the process exits; this call allocates
+ * nothing. `saved` and `workspace` in args must be NULL / 0; the caller still
+ * passes q, slots and the outputs. A problem whose scratch exceeds the array
+ * is rejected with MURM_ERR_WORKSPACE. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture. All calls share the array: calls that overlap on
+ * the GPU (different streams, or other host threads) race on it; serialise
+ * them. Output only — there is no backward for this entry point. */
+#define MURM_NOSCRATCH_BYTES (64u << 20)
+MURM_API murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* args, void* stream);
+
 /* Launch accounting and per-kernel timing (host-side instrumentation; no
  * effect on results). murm_kernel_launches() counts every kernel this library
  * has launched in the process. Between murm_profile_begin() and

@@ -68,6 +68,7 @@ EXPORTS = (
     "murm_slot_murmurate_sizes",
     "murm_slot_murmurate_fwd",
     "murm_slot_murmurate_bwd",
+    "murm_slot_murmurate_fwd_noscratch",
     "murm_status_string",
     "murm_last_error_message",
     "murm_abi_version",
@@ -104,6 +105,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_slot_murmurate_fwd.restype = ctypes.c_int
         lib.murm_slot_murmurate_bwd.argtypes = [ctypes.POINTER(BwdArgs), ctypes.c_void_p]
         lib.murm_slot_murmurate_bwd.restype = ctypes.c_int
+        lib.murm_slot_murmurate_fwd_noscratch.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.murm_slot_murmurate_fwd_noscratch.restype = ctypes.c_int
         lib.murm_status_string.argtypes = [ctypes.c_int]
         lib.murm_status_string.restype = ctypes.c_char_p
         lib.murm_last_error_message.argtypes = []

@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "murm_kernels.cuh"
@@ -258,3 +259,84 @@ murm_status murm_slot_murmurate_bwd(const murm_bwd_args* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward without caller scratch (murm_slot_murmurate_fwd_noscratch)
+// ---------------------------------------------------------------------------
+namespace murm {
+namespace {
+
+constexpr size_t kNoScratchBytes = MURM_NOSCRATCH_BYTES;
+constexpr int kMaxDevices = 64;
+
+// The scratch of murm_slot_murmurate_fwd_noscratch: round records + partial
+// sums. In host code `g_noscratch` is only a host-side stand-in for the
+// symbol; kernels get the device address looked up below.
+__device__ __align__(256) unsigned char g_noscratch[kNoScratchBytes];
+
+std::mutex g_noscratch_mu;
+void* g_noscratch_addr[kMaxDevices] = {};
+
+// Device address of g_noscratch on the current device (looked up once per device).
+murm_status noscratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MURM_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lk(g_noscratch_mu);
+  if (!g_noscratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noscratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(built-in scratch)");
+    g_noscratch_addr[dev] = p;
+  }
+  *out = g_noscratch_addr[dev];
+  return MURM_OK;
+}
+
+}  // namespace
+}  // namespace murm
+
+extern "C" murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* a, void* stream) {
+  if (!a) return fail(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = check_shape(&a->shape)) return s;
+  if (a->saved || a->saved_bytes || a->workspace || a->workspace_bytes)
+    return fail(MURM_ERR_INVALID_ARGUMENT,
+                "murm_slot_murmurate_fwd_noscratch uses its built-in scratch: saved/workspace must be NULL and 0");
+  const Geom g = make_geom(&a->shape);
+  const Sizes z = make_sizes(g);
+  const size_t need = z.saved + z.fwd_ws;  // both already multiples of 256
+  if (need > kNoScratchBytes)
+    return fail(MURM_ERR_WORKSPACE,
+                "problem needs %zu bytes of scratch; the built-in scratch of murm_slot_murmurate_fwd_noscratch "
+                "holds %zu bytes (use murm_slot_murmurate_fwd with caller-provided buffers)",
+                need, kNoScratchBytes);
+  if (murm_status s = check_tensor(a->q, a->q_stride, "q", false)) return s;
+  if (murm_status s = check_tensor(a->slots_k, a->sk_stride, "slots_k", true)) return s;
+  if (murm_status s = check_tensor(a->slots_v, a->sv_stride, "slots_v", true)) return s;
+  if (murm_status s = check_tensor(a->out, a->out_stride, "out", false)) return s;
+  void* base = nullptr;
+  if (murm_status s = noscratch_address(&base)) return s;
+  FwdPtrs p;
+  p.q = a->q; p.sk = a->slots_k; p.sv = a->slots_v; p.out = a->out;
+  for (int i = 0; i < 3; ++i) {
+    p.qs.s[i] = a->q_stride[i]; p.sks.s[i] = a->sk_stride[i]; p.svs.s[i] = a->sv_stride[i];
+    p.os.s[i] = a->out_stride[i];
+  }
+  p.indices = a->indices;
+  p.weights = a->weights;
+  // Every byte of the scratch that a kernel reads is written earlier in the
+  // same call, so nothing needs clearing between calls.
+  const Saved sv = saved_views(z, base);
+  FwdScratch fs;
+  fs.Spart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fS);
+  fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fW);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  switch (a->shape.dtype) {
+    case MURM_F32: e = fwd_simt<float>(g, p, sv, fs, st); break;
+    case MURM_F16: e = fwd_simt<__half>(g, p, sv, fs, st); break;
+    case MURM_BF16: e = fwd_simt<__nv_bfloat16>(g, p, sv, fs, st); break;
+  }
+  return cuda_status(e, "slot_murmurate forward (built-in scratch) launch");
+}
