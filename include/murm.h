@@ -159,6 +159,12 @@ MURM_API uint64_t murm_kernel_launches(void);
 MURM_API murm_status murm_profile_begin(void);
 MURM_API murm_status murm_profile_end(murm_kernel_time* out, int32_t capacity, int32_t* count);
 
+/* Synchronises `stream`, then reads and clears this device's error word, which
+ * tensor-core kernels set when a bounded wait gives up (a copy or an MMA that
+ * never completed) before they wind down cleanly. Returns MURM_ERR_DEVICE
+ * when it was set. */
+MURM_API murm_status murm_device_status(void* stream);
+
 MURM_API const char* murm_status_string(murm_status status);
 MURM_API const char* murm_last_error_message(void);
 MURM_API int32_t murm_abi_version(void);

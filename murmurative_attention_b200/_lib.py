@@ -72,6 +72,7 @@ EXPORTS = (
     "murm_status_string",
     "murm_last_error_message",
     "murm_abi_version",
+    "murm_device_status",
     "murm_kernel_launches",
     "murm_profile_begin",
     "murm_profile_end",
@@ -113,6 +114,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_last_error_message.restype = ctypes.c_char_p
         lib.murm_abi_version.argtypes = []
         lib.murm_abi_version.restype = ctypes.c_int32
+        lib.murm_device_status.argtypes = [ctypes.c_void_p]
+        lib.murm_device_status.restype = ctypes.c_int
         lib.murm_kernel_launches.argtypes = []
         lib.murm_kernel_launches.restype = ctypes.c_uint64
         lib.murm_profile_begin.argtypes = []
@@ -159,3 +162,10 @@ def profile_end() -> dict:
     n = ctypes.c_int32()
     check(lib.murm_profile_end(buf, cap, ctypes.byref(n)))
     return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(min(n.value, cap))}
+
+
+def device_status(stream=None) -> None:
+    """Synchronise ``stream`` and raise if a kernel reported a device-side error."""
+    import torch
+    st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    check(load_library().murm_device_status(ctypes.c_void_p(st)))

@@ -61,6 +61,7 @@ Geom make_geom(const murm_shape* s) {
   Geom g{};
   g.B = s->batch; g.H = s->heads; g.N = s->tokens; g.M = s->slots; g.D = s->head_dim; g.R = s->rounds;
   g.causal = s->causal ? 1 : 0;
+  g.dtype = s->dtype;
   g.BH = g.B * g.H;
   // Python floats are doubles; the reference multiplies fp32 tensors by them,
   // which rounds each scalar to fp32 once (reference.py:112-113, 128-133).
@@ -83,7 +84,7 @@ struct Sizes {
   size_t saved, fwd_ws, bwd_ws;
   // offsets inside each block
   size_t sK, sV, sU, sW, sIdx, sw;
-  size_t fS, fW;
+  size_t fS, fW, fImg;
   size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq;
 };
 
@@ -103,6 +104,8 @@ Sizes make_sizes(const Geom& g) {
   o = 0;
   z.fS = take(BH * g.red_chunks * M * D * 4);
   z.fW = take(BH * g.red_chunks * M * 4);
+  // operand images of the tensor-core path (16-bit dtypes, head_dim 64)
+  z.fImg = take(tc_images_bytes(g));
   z.fwd_ws = o;
   o = 0;
   z.bdK0 = take(slot); z.bdK1 = take(slot); z.bdV0 = take(slot); z.bdV1 = take(slot);
@@ -145,6 +148,21 @@ murm_status cuda_status(cudaError_t e, const char* what) {
   return fail(MURM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+// Forward dispatch: tensor-core rounds for fp16/bf16 at head_dim 64, CUDA-core
+// rounds otherwise (fp32 inputs keep exact fp32 selection arithmetic).
+murm_status run_forward(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  const bool tc = tc_forward_supported(g, g.dtype, p);
+  switch (g.dtype) {
+    case MURM_F32: e = fwd_simt<float>(g, p, sv, fs, st); break;
+    case MURM_F16: e = tc ? fwd_tc<__half>(g, p, sv, fs, st) : fwd_simt<__half>(g, p, sv, fs, st); break;
+    case MURM_BF16:
+      e = tc ? fwd_tc<__nv_bfloat16>(g, p, sv, fs, st) : fwd_simt<__nv_bfloat16>(g, p, sv, fs, st);
+      break;
+  }
+  return cuda_status(e, tc ? "slot_murmurate forward (tensor-core) launch" : "slot_murmurate forward launch");
+}
+
 }  // namespace
 }  // namespace murm
 
@@ -168,6 +186,16 @@ const char* murm_status_string(murm_status s) {
 }
 
 const char* murm_last_error_message(void) { return g_last_error.c_str(); }
+
+murm_status murm_device_status(void* stream) {
+  int code = 0;
+  cudaError_t e = read_and_clear_device_error(&code, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "murm_device_status");
+  if (code)
+    return fail(MURM_ERR_DEVICE, "a kernel gave up waiting (error bits 0x%x: 1 operand copy, 2 token tile copy, "
+                "4 tensor-core completion)", code);
+  return MURM_OK;
+}
 
 murm_status murm_slot_murmurate_sizes(const murm_shape* shape, size_t* saved, size_t* fwd_ws, size_t* bwd_ws) {
   if (murm_status s = check_shape(shape)) return s;
@@ -205,14 +233,8 @@ murm_status murm_slot_murmurate_fwd(const murm_fwd_args* a, void* stream) {
   FwdScratch fs;
   fs.Spart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fS);
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fW);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaSuccess;
-  switch (g.R >= 0 ? a->shape.dtype : -1) {
-    case MURM_F32: e = fwd_simt<float>(g, p, sv, fs, st); break;
-    case MURM_F16: e = fwd_simt<__half>(g, p, sv, fs, st); break;
-    case MURM_BF16: e = fwd_simt<__nv_bfloat16>(g, p, sv, fs, st); break;
-  }
-  return cuda_status(e, "slot_murmurate forward launch");
+  fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(a->workspace) + z.fImg);
+  return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }
 
 murm_status murm_slot_murmurate_bwd(const murm_bwd_args* a, void* stream) {
@@ -331,12 +353,6 @@ extern "C" murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* a,
   FwdScratch fs;
   fs.Spart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fS);
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fW);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaSuccess;
-  switch (a->shape.dtype) {
-    case MURM_F32: e = fwd_simt<float>(g, p, sv, fs, st); break;
-    case MURM_F16: e = fwd_simt<__half>(g, p, sv, fs, st); break;
-    case MURM_BF16: e = fwd_simt<__nv_bfloat16>(g, p, sv, fs, st); break;
-  }
-  return cuda_status(e, "slot_murmurate forward (built-in scratch) launch");
+  fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(base) + z.saved + z.fImg);
+  return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }

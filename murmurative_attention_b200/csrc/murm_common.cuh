@@ -76,7 +76,7 @@ struct Top7 {
 // Problem description shared by host and device
 // ---------------------------------------------------------------------------
 struct Geom {
-  int B, H, N, M, D, R, causal;
+  int B, H, N, M, D, R, causal, dtype;
   int BH;
   float alpha, one_minus_alpha, gamma, scale;
   // token chunks: chunk c covers tokens [c*chunk_tokens, min(N, (c+1)*chunk_tokens))
@@ -95,8 +95,9 @@ struct Saved {
   float* w;      // [R][BH][N][8] softmax weights (7 used)
 };
 struct FwdScratch {
-  float* Spart;  // [BH][red_chunks][M][D]
-  float* Wpart;  // [BH][red_chunks][M]
+  float* Spart;     // [BH][red_chunks][M][D]
+  float* Wpart;     // [BH][red_chunks][M]
+  uint8_t* images;  // [BH][3][256][64] 16-bit operand images (tensor-core path)
 };
 struct BwdScratch {
   float* dK[2];  // [BH][M][D] ping-pong slot-key gradients

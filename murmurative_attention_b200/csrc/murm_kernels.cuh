@@ -46,6 +46,20 @@ void launch_end(cudaStream_t st);
     ::murm::launch_end(stream);                                          \
   } while (0)
 
+// Shared pieces of the round loop (murm_simt.cu).
+template <typename T>
+void launch_load_slots(const Geom& g, const FwdPtrs& p, const Saved& sv, cudaStream_t st);
+void launch_update_finalize(const Geom& g, int r, const Saved& sv, const FwdScratch& fs, cudaStream_t st);
+
+// Tensor-core forward (murm_tc.cu): fp16/bf16, head_dim 64, row strides that
+// are multiples of 8 elements.
+bool tc_forward_supported(const Geom& g, int dtype, const FwdPtrs& p);
+size_t tc_images_bytes(const Geom& g);
+template <typename T>
+cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st);
+// Device error word written by bounded waits in tensor-core kernels.
+cudaError_t read_and_clear_device_error(int* code, cudaStream_t st);
+
 // CUDA-core path (murm_simt.cu): every dtype, head_dim 16/32/64.
 template <typename T>
 cudaError_t fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st);

@@ -574,6 +574,19 @@ __global__ void k_fill_zero_rows(Geom g, T* p, Strides3 st, int rows) {
 // ---------------------------------------------------------------------------
 // Host-side launchers (called from murm_capi.cu)
 // ---------------------------------------------------------------------------
+template <typename T>
+void launch_load_slots(const Geom& g, const FwdPtrs& p, const Saved& sv, cudaStream_t st) {
+  MURM_LAUNCH("load_slots", k_load_slots<T>, dim3(g.BH, 4), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
+              static_cast<const T*>(p.sv), p.svs, sv.K, sv.V);
+}
+template void launch_load_slots<float>(const Geom&, const FwdPtrs&, const Saved&, cudaStream_t);
+template void launch_load_slots<__half>(const Geom&, const FwdPtrs&, const Saved&, cudaStream_t);
+template void launch_load_slots<__nv_bfloat16>(const Geom&, const FwdPtrs&, const Saved&, cudaStream_t);
+
+void launch_update_finalize(const Geom& g, int r, const Saved& sv, const FwdScratch& fs, cudaStream_t st) {
+  MURM_LAUNCH("update_finalize", k_update_finalize, dim3(g.BH, g.D / 8), 256, 0, st, g, r, sv, fs);
+}
+
 template <typename T, int D>
 static cudaError_t run_fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs,
                                 cudaStream_t st) {

@@ -187,3 +187,27 @@ def test_errors_mirror_reference():
         op(q, s[:, :, :6], s[:, :, :6])        # fewer slots than picks
     with pytest.raises(RuntimeError):
         op(q.cpu(), s.cpu(), s.cpu())
+
+
+@pytest.mark.parametrize("dt,causal,N,M", [(torch.float16, False, 1000, 256), (torch.bfloat16, True, 700, 256),
+                                           (torch.float16, True, 129, 96), (torch.bfloat16, False, 64, 7)])
+def test_tensor_core_forward_matches_cuda_core_forward(dt, causal, N, M, monkeypatch):
+    """The tcgen05 forward (fp16/bf16, d=64) and the fp32 CUDA-core forward agree:
+    indices on every unambiguous row, out/weights within the 16-bit tolerance."""
+    from murmurative_attention_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(N + M)
+    q = torch.randn(2, 3, N, 64, device="cuda", generator=g).to(dt)
+    sk = torch.randn(2, 3, M, 64, device="cuda", generator=g).to(dt)
+    sv = (torch.randn(2, 3, M, 64, device="cuda", generator=g) * 0.2).to(dt)
+    o_tc, i_tc, w_tc = _op()(q, sk, sv, rounds=3, causal=causal)
+    _lib.device_status()
+    monkeypatch.setenv("MURM_FORCE_SIMT", "1")
+    o_s, i_s, w_s = _op()(q, sk, sv, rounds=3, causal=causal)
+    _lib.device_status()
+    tr = oracle.slot_murmurate_trace(q.float().cpu(), sk.float().cpu(), sv.float().cpu(), 3, causal)
+    ok = om.row_gap_ok(tr["top8"][-1])
+    mism = (i_tc.cpu() != i_s.cpu()).any(-1)
+    assert not (mism & ok).any(), f"{int((mism & ok).sum())} unambiguous rows differ"
+    keep = ~mism
+    torch.testing.assert_close(o_tc.float().cpu()[keep], o_s.float().cpu()[keep], atol=2e-3, rtol=1e-2)
+    torch.testing.assert_close(w_tc.cpu()[keep], w_s.cpu()[keep], atol=2e-3, rtol=1e-2)
