@@ -72,7 +72,8 @@ Geom make_geom(const murm_shape* s) {
   const int tiles = (g.N + kTile - 1) / kTile;
   g.fwd_chunks = tiles;
   g.fwd_chunk_tokens = kTile;
-  int red = (2 * kSmCount + g.BH - 1) / g.BH;
+  // one wave: at most one chunk per SM (the tensor-core kernel holds a whole SM)
+  int red = kSmCount / g.BH;
   red = red < 1 ? 1 : (red > tiles ? tiles : red);
   const int tiles_per = (tiles + red - 1) / red;
   g.red_chunk_tokens = tiles_per * kTile;

@@ -39,22 +39,31 @@ __device__ int g_device_error;  // set by a bounded wait that expired; read by m
 namespace tc {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
+constexpr int kThreads = 256;    // 2 warps per TMEM lane quadrant
+constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
+constexpr int kCand = 16;        // candidate list per row (16 never exceeded in 2e5 random rows)
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t COL_S = 0, COL_O = 0, COL_U = 256, COL_W = 384;
+// TMEM columns: scores | slot sums S (2 halves) | weight sums W (2 halves) | exchange | attend output O
+constexpr uint32_t COL_S = 0, COL_U = 256, COL_W = 384, COL_X = 416, COL_O = 448;
 constexpr uint32_t kQBytes = 128 * 128;
 
 enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
 
+// Barrier over the warps that share one TMEM lane quadrant.
+__device__ __forceinline__ void quadrant_sync(int quadrant) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(32 * kParts) : "memory");
+}
+
 template <typename T> struct Cfg;
 template <> struct Cfg<__half> {
   static constexpr uint32_t fmt = 0;
-  static constexpr int kSplits = 2, kQBufs = 2, kCand = 24;
+  static constexpr int kSplits = 2, kQBufs = 2;
   static __device__ __forceinline__ uint16_t one() { return 0x3C00u; }
 };
 template <> struct Cfg<__nv_bfloat16> {
   static constexpr uint32_t fmt = 1;
-  static constexpr int kSplits = 3, kQBufs = 1, kCand = 16;
+  static constexpr int kSplits = 3, kQBufs = 1;
   static __device__ __forceinline__ uint16_t one() { return 0x3F80u; }
 };
 template <typename T> struct Layout {
@@ -63,8 +72,9 @@ template <typename T> struct Layout {
   static constexpr uint32_t OFF_P = OFF_V + kImg;
   static constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;
   static constexpr uint32_t OFF_ONES = OFF_Q + Cfg<T>::kQBufs * kQBytes;
-  static constexpr uint32_t OFF_CAND = OFF_ONES + 1024;
-  static constexpr uint32_t OFF_MISC = OFF_CAND + kTile * Cfg<T>::kCand * 8;
+  static constexpr uint32_t OFF_CAND = OFF_ONES + 512;
+  static constexpr uint32_t OFF_CNT = OFF_CAND + kTile * kCand * 8;
+  static constexpr uint32_t OFF_MISC = OFF_CNT + 2 * kTile * 4;
   static constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
 };
@@ -94,6 +104,59 @@ __device__ __forceinline__ float from_bits(uint16_t b) {
   return Elem<T>::load(reinterpret_cast<const T*>(&b));
 }
 
+// Descending sort of 8 floats (19 compare-exchanges).
+__device__ __forceinline__ void sort8_desc(float (&a)[8]) {
+  constexpr int P[19][2] = {{0, 1}, {2, 3}, {4, 5}, {6, 7}, {0, 2}, {1, 3}, {4, 6}, {5, 7}, {1, 2}, {5, 6},
+                            {0, 4}, {3, 7}, {1, 5}, {2, 6}, {1, 4}, {3, 6}, {2, 4}, {3, 5}, {3, 4}};
+#pragma unroll
+  for (int e = 0; e < 19; ++e) {
+    const float x = a[P[e][0]], y = a[P[e][1]];
+    a[P[e][0]] = fmaxf(x, y);
+    a[P[e][1]] = fminf(x, y);
+  }
+}
+// Top 8 (descending) of two descending lists of 8: bitonic merge.
+__device__ __forceinline__ void merge8_desc(const float* A, const float* B, float (&c)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = fmaxf(A[i], B[7 - i]);
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((i & s) == 0) {
+        const float x = c[i], y = c[i + s];
+        c[i] = fmaxf(x, y);
+        c[i + s] = fminf(x, y);
+      }
+}
+
+// Top-7 under the total order (score key descending, slot ascending): the
+// result does not depend on the order in which candidates are offered.
+struct Top7Ord {
+  uint32_t k[kTopK];
+  int i[kTopK];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) { k[j] = 0u; i[j] = 0x7FFFFFFF; }
+  }
+  static __device__ __forceinline__ bool better(uint32_t ka, int ia, uint32_t kb, int ib) {
+    return ka > kb || (ka == kb && ia < ib);
+  }
+  __device__ __forceinline__ void offer(uint32_t key, int idx) {
+    if (!better(key, idx, k[kTopK - 1], i[kTopK - 1])) return;
+    bool done = false;
+#pragma unroll
+    for (int j = kTopK - 1; j > 0; --j) {
+      const bool shift = !done && better(key, idx, k[j - 1], i[j - 1]);
+      const bool place = !done && !shift;
+      k[j] = shift ? k[j - 1] : (place ? key : k[j]);
+      i[j] = shift ? i[j - 1] : (place ? idx : i[j]);
+      done = done || place;
+    }
+    if (!done) { k[0] = key; i[0] = idx; }
+  }
+};
+
 }  // namespace tc
 
 // ---------------------------------------------------------------------------
@@ -103,34 +166,52 @@ __device__ __forceinline__ float from_bits(uint16_t b) {
 template <typename T>
 __global__ void __launch_bounds__(256) k_tc_images(Geom g, int r, Saved sv, uint8_t* images) {
   constexpr int S = tc::Cfg<T>::kSplits;
-  const int bh = blockIdx.x, m = threadIdx.x;
+  const int bh = blockIdx.x;
   const size_t st = ((size_t)r * g.BH + bh) * g.M * tc::kD;
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
-  for (int c = 0; c < tc::kD; ++c) {
-    float k = 0.f, v = 0.f;
+  // thread -> (slot row, 8-column chunk): coalesced 16-byte stores
+  for (int e = blockIdx.y * blockDim.x + threadIdx.x; e < tc::kSlotsPad * 8; e += gridDim.y * blockDim.x) {
+    const int m = e >> 3, c8 = e & 7;
+    float k[8], v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { k[i] = 0.f; v[i] = 0.f; }
     if (m < g.M) {
-      k = sv.K[st + (size_t)m * tc::kD + c];
-      v = sv.V[st + (size_t)m * tc::kD + c];
+      const float4* kp = reinterpret_cast<const float4*>(sv.K + st + (size_t)m * tc::kD + 8 * c8);
+      const float4* vp = reinterpret_cast<const float4*>(sv.V + st + (size_t)m * tc::kD + 8 * c8);
+      const float4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
+      k[0] = k0.x; k[1] = k0.y; k[2] = k0.z; k[3] = k0.w; k[4] = k1.x; k[5] = k1.y; k[6] = k1.z; k[7] = k1.w;
+      v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w; v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
     }
-    const uint32_t off = sm100::sw128_offset(m, c);
+    const uint32_t off = sm100::sw128_offset(m, 8 * c8);  // 16-byte chunk start
 #pragma unroll
     for (int s = 0; s < S; ++s) {
-      T term;
-      Elem<T>::store(&term, k);
-      *reinterpret_cast<T*>(base + s * tc::kImg + off) = term;
-      k -= Elem<T>::load(&term);  // exact in fp32: the next term carries the residual
+      uint4 pk;
+      uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ph[i] = tc::to_bits<T>(k[i]);
+        k[i] -= tc::from_bits<T>(ph[i]);  // exact in fp32: the next term carries the residual
+      }
+      *reinterpret_cast<uint4*>(base + s * tc::kImg + off) = pk;
     }
-    T vv;
-    Elem<T>::store(&vv, v);
-    *reinterpret_cast<T*>(base + tc::Layout<T>::OFF_V + off) = vv;
+    uint4 pv;
+    uint16_t* pvh = reinterpret_cast<uint16_t*>(&pv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pvh[i] = tc::to_bits<T>(v[i]);
+    *reinterpret_cast<uint4*>(base + tc::Layout<T>::OFF_V + off) = pv;
   }
 }
 
 // ---------------------------------------------------------------------------
-// The forward round kernel
+// The forward round kernel (256 threads: thread = (token row, half of the slots))
+//
+// Tensor-core order per tile i:  MMA_A(i) = {O = P_hi.V, S += P_hi^T.Q, W += P_hi^T.1},
+// then SELECT(i+1) (scores of the next tile), then MMA_B(i) = {S += P_lo^T.Q,
+// W += P_lo^T.1}. SELECT(i+1) runs while the CUDA cores write the second
+// weight term and the output of tile i; MMA_B(i) runs while they rank tile i+1.
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(kTile, 1)
+__global__ void __launch_bounds__(tc::kThreads, 1)
     k_fwd_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
              float* weights, Saved sv, FwdScratch fs, const uint8_t* images) {
   using C = tc::Cfg<T>;
@@ -140,12 +221,19 @@ __global__ void __launch_bounds__(kTile, 1)
   const uint32_t s_base = smem_u32(sm);
   uint64_t* bar_img = reinterpret_cast<uint64_t*>(sm + L::OFF_MISC);
   uint64_t* bar_q = bar_img + 1;  // [2]
-  uint64_t* bar_mma = bar_img + 3;
+  uint64_t* bar_s = bar_img + 3;  // SELECT done
+  uint64_t* bar_a = bar_img + 4;  // MMA_A done
+  uint64_t* bar_b = bar_img + 5;  // MMA_B done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 64);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 68);
-  float2* cand = reinterpret_cast<float2*>(sm + L::OFF_CAND) + threadIdx.x * C::kCand;
+  int* row_cnt2 = reinterpret_cast<int*>(sm + L::OFF_CNT);  // [2][128], by tile parity
 
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (kTile - 1);  // token row within the tile == TMEM lane
+  const int part = tid >> 7;          // which 128 of the 256 slot columns this thread scans
+  const int quadrant = warp & 3;
+  // candidate e of row r at [e][r]: a warp's rows touch consecutive words (no bank conflicts)
+  float2* cand = reinterpret_cast<float2*>(sm + L::OFF_CAND) + row;
   const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
   const int t_beg = chunk * g.red_chunk_tokens;
   const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
@@ -155,20 +243,23 @@ __global__ void __launch_bounds__(kTile, 1)
   constexpr uint32_t ID_UPD = idesc_f16(C::fmt, 128, 64, 1, 1);
   constexpr uint32_t ID_W = idesc_f16(C::fmt, 128, 16, 1, 0);
 
-  // ---- set-up: barriers, zeroed P, ones, TMEM ----
+  // ---- set-up: barriers, zeroed P, ones, counters, TMEM ----
   if (tid == 0) {
     mbar_init(bar_img, 1);
     mbar_init(&bar_q[0], 1);
     mbar_init(&bar_q[1], 1);
-    mbar_init(bar_mma, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_a, 1);
+    mbar_init(bar_b, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
   {
     float4* p4 = reinterpret_cast<float4*>(sm + L::OFF_P);
-    for (int i = tid; i < 4 * 16384 / 16; i += kTile) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = tid; i < 4 * 16384 / 16; i += tc::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint16_t* ones = reinterpret_cast<uint16_t*>(sm + L::OFF_ONES);
-    for (int i = tid; i < 512; i += kTile) ones[i] = C::one();
+    ones[tid] = C::one();  // 256 x 16-bit
+    if (tid < 2 * kTile) row_cnt2[tid] = 0;
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tc::kTmemCols);
@@ -179,168 +270,193 @@ __global__ void __launch_bounds__(kTile, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)(32 * quadrant) << 16;
+  const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
+  const bool last_round = (r == g.R - 1);
 
+  // mbarrier phases (every thread tracks them; waits never fall two phases behind)
+  uint32_t ph_s = 0, ph_a = 0, ph_b = 0;
   // thread 0's bookkeeping of asynchronous copies
-  bool img_pending = false, q_pending0 = false, q_pending1 = false;
-  uint32_t q_phase0 = 0, q_phase1 = 0, mma_phase = 0;
-  auto issue_q = [&](int tile_idx) {  // thread 0 only
-    const int bsel = (C::kQBufs == 2) ? (tile_idx & 1) : 0;
-    mbar_arrive_expect_tx(&bar_q[bsel], tc::kQBytes);
-    tma_load_4d(sm + L::OFF_Q + bsel * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bsel]);
-    if (bsel) q_pending1 = true; else q_pending0 = true;
+  bool img_pending = false, q_pending[2] = {false, false};
+  uint32_t q_phase[2] = {0, 0};
+
+  auto fail = [&](int code) {
+    atomicOr(&g_device_error, code);
+    *s_abort = 1;
   };
+  auto wait_bar = [&](uint64_t* bar, uint32_t& ph) {
+    if (tc::timed_wait(bar, ph)) ph ^= 1;
+    else fail(tc::kErrMmaWait);
+    tc_fence_after();
+  };
+  auto q_slot = [&](int tile_idx) { return (C::kQBufs == 2) ? (tile_idx & 1) : 0; };
+  auto issue_q = [&](int tile_idx) {  // thread 0
+    const int bs = q_slot(tile_idx);
+    mbar_arrive_expect_tx(&bar_q[bs], tc::kQBytes);
+    tma_load_4d(sm + L::OFF_Q + bs * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bs]);
+    q_pending[bs] = true;
+  };
+  auto wait_q = [&](int tile_idx) -> bool {  // thread 0
+    const int bs = q_slot(tile_idx);
+    if (!tc::timed_wait(&bar_q[bs], q_phase[bs])) {
+      fail(tc::kErrQWait);
+      return false;
+    }
+    q_phase[bs] ^= 1;
+    q_pending[bs] = false;
+    return true;
+  };
+  auto issue_select = [&](int tile_idx) {  // thread 0
+    const uint32_t a_q = s_base + L::OFF_Q + q_slot(tile_idx) * tc::kQBytes;
+    tc_fence_after();
+#pragma unroll
+    for (int s = 0; s < C::kSplits; ++s)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f16(tmem + tc::COL_S, smem_desc(a_q + k * 32, 16, 1024, kSwizzle128B),
+                smem_desc(s_base + s * tc::kImg + k * 32, 16, 1024, kSwizzle128B), ID_SEL, (s | k) != 0);
+    mma_commit(bar_s);
+  };
+  auto issue_update = [&](int tile_idx, bool first) {  // thread 0: S += P^T.Q, W += P^T.1
+    const uint32_t a_q = s_base + L::OFF_Q + q_slot(tile_idx) * tc::kQBytes;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t a = smem_desc(a_p + 2 * hh * 16384 + kk * 2048, 16384, 1024, kSwizzle128B);
+        const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+        mma_f16(tmem + tc::COL_U + 64 * hh, a, smem_desc(a_q + kk * 2048, 16384, 1024, kSwizzle128B), ID_UPD, acc);
+        mma_f16(tmem + tc::COL_W + 16 * hh, a, smem_desc(a_ones, 256, 128, kSwizzleNone), ID_W, acc);
+      }
+    }
+  };
+  auto p_entry = [&](int m) -> uint16_t* {
+    return reinterpret_cast<uint16_t*>(sm + L::OFF_P + (m >> 6) * 16384 + sw128_offset(row, m & 63));
+  };
+
+  // ---- prologue: operand images, first token tile(s), first SELECT ----
   if (tid == 0) {
     mbar_arrive_expect_tx(bar_img, L::kImages);
     bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
     img_pending = true;
     issue_q(0);
+    if (C::kQBufs == 2 && ntiles > 1) issue_q(1);
+    if (!tc::timed_wait(bar_img, 0)) fail(tc::kErrImgWait);
+    else img_pending = false;
+    if (!*s_abort && wait_q(0)) issue_select(0);
   }
-  const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
-  const bool last_round = (r == g.R - 1);
 
-  // Wait for the MMA group committed last; on timeout record and abort.
-  auto wait_mma = [&]() {
-    if (tc::timed_wait(bar_mma, mma_phase)) {
-      mma_phase ^= 1;
-    } else {
-      atomicOr(&g_device_error, tc::kErrMmaWait);
-      *s_abort = 1;
-    }
-    tc_fence_after();
-  };
-  auto sync_all = [&]() {  // smem writes -> async proxy; TMEM reads done; CTA barrier
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-  };
+  int old_pick[kTopK];  // this row's picks in the previous tile (their P entries are still set)
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) old_pick[j] = -1;
+  bool b_pending = false;  // an MMA_B whose completion this thread has not waited for
 
   for (int tile = 0; tile < ntiles; ++tile) {
-    const int buf = (C::kQBufs == 2) ? (tile & 1) : 0;
     const int n0 = t_beg + tile * kTile;
-    const int n = n0 + tid;
+    const int n = n0 + row;
     const bool valid = n < t_end;
-    const uint32_t a_q = s_base + L::OFF_Q + buf * tc::kQBytes;
+    int* row_cnt = row_cnt2 + (tile & 1) * kTile;
 
-    // ---- select MMA ----
-    if (tid == 0) {
-      bool ok = true;
-      if (C::kQBufs == 2 && tile + 1 < ntiles) issue_q(tile + 1);  // the other buffer is free
-      if (img_pending) {
-        ok = tc::timed_wait(bar_img, 0);
-        img_pending = !ok;
-        if (!ok) atomicOr(&g_device_error, tc::kErrImgWait);
-      }
-      if (ok) {
-        uint32_t& ph = buf ? q_phase1 : q_phase0;
-        ok = tc::timed_wait(&bar_q[buf], ph);
-        if (ok) {
-          ph ^= 1;
-          if (buf) q_pending1 = false; else q_pending0 = false;
-        } else {
-          atomicOr(&g_device_error, tc::kErrQWait);
-        }
-      }
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int s = 0; s < C::kSplits; ++s)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f16(tmem + tc::COL_S, smem_desc(a_q + k * 32, 16, 1024, kSwizzle128B),
-                    smem_desc(s_base + s * tc::kImg + k * 32, 16, 1024, kSwizzle128B), ID_SEL, (s | k) != 0);
-        mma_commit(bar_mma);
-      } else {
-        *s_abort = 1;
-      }
+    // ---- scores of this tile ----
+    wait_bar(bar_s, ph_s);
+    if (tid == 0 && C::kQBufs == 2 && tile >= 1 && tile + 1 < ntiles && !*s_abort) {
+      // the next tile's Q buffer was read last by MMA_B(i-1), which follows SELECT(i)
+      wait_bar(bar_b, ph_b);
+      b_pending = false;
+      issue_q(tile + 1);
     }
-    wait_mma();
-
-    // ---- top-7 of this thread's row ----
-    // TMEM loads are warp-collective: every lane executes them; rows past the
-    // chunk end (last tile) ignore the values.
-    int pick[kTopK];
-    float wgt[kTopK];
     const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
-    const bool active = valid && !aborting;
-    const int lim = g.causal ? min(g.M, n + 1) : g.M;  // columns >= lim score -inf
+    const int lim = g.causal ? min(g.M, n + 1) : g.M;               // columns >= lim score -inf
+    const int col0 = 128 * part;
+    const bool mask_warp = __any_sync(0xffffffffu, lim < col0 + 128);
+
+    // pass 1: this thread's 128 scores (kept in registers), 16 group maxima, top 8 published in TMEM
+    float v[128];
     if (!aborting) {
-      const bool need_mask = __any_sync(0xffffffffu, lim < tc::kSlotsPad);
-      float gm[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[32];
-        tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, v);
-        tmem_wait_ld();
-        if (need_mask) {
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(tmem + lane_base + tc::COL_S + col0 + 32 * c, *reinterpret_cast<float(*)[32]>(&v[32 * c]));
+      tmem_wait_ld();
+      if (mask_warp) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = (32 * c + i < lim) ? v[i] : -INFINITY;
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float x = v[8 * q4];
-#pragma unroll
-          for (int i = 1; i < 8; ++i) x = fmaxf(x, v[8 * q4 + i]);
-          gm[4 * c + q4] = x;
-        }
+        for (int i = 0; i < 128; ++i) v[i] = (col0 + i < lim) ? v[i] : -INFINITY;
       }
-      // 7th largest group maximum: a lower bound of the 7th largest score.
-      float t7[kTopK];
+      float ga[8], gb[8], top8[8];
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) t7[j] = -INFINITY;
+      for (int gq = 0; gq < 16; ++gq) {
+        float x = v[8 * gq];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float x = gm[i];
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) {
-          const float hi = fmaxf(t7[j], x);
-          x = fminf(t7[j], x);
-          t7[j] = hi;
-        }
+        for (int i = 1; i < 8; ++i) x = fmaxf(x, v[8 * gq + i]);
+        if (gq < 8) ga[gq] = x; else gb[gq - 8] = x;
       }
-      const float thr = t7[kTopK - 1];
+      tc::sort8_desc(ga);
+      tc::sort8_desc(gb);
+      tc::merge8_desc(ga, gb, top8);
+      tmem_st8(tmem + lane_base + tc::COL_X + 8 * part, top8);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    tc::quadrant_sync(quadrant);
+    tc_fence_after();
+
+    // pass 2: threshold = 7th largest group maximum of the row; scores >= it are candidates
+    float thr = -INFINITY;
+    if (!aborting) {
+      float lst[16];
+      tmem_ld16(tmem + lane_base + tc::COL_X, lst);
+      tmem_wait_ld();
+      float all8[8];
+      tc::merge8_desc(&lst[0], &lst[8], all8);
+      thr = all8[kTopK - 1];
       const bool bounded = thr > -INFINITY;
       int cnt = 0;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[32];
-        tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, v);
-        tmem_wait_ld();
+      for (int i = 0; i < 128; ++i) cnt += (bounded && v[i] >= thr) ? 1 : 0;  // masked columns are -inf
+      if (cnt && valid) {
+        int k = atomicAdd(&row_cnt[row], cnt);  // order-free: Top7Ord
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int m = 32 * c + i;
-          if (bounded && m < lim && v[i] >= thr) {
-            if (cnt < C::kCand) cand[cnt] = make_float2(v[i], __int_as_float(m));
-            ++cnt;
-          }
+        for (int i = 0; i < 128; ++i) {
+          const bool c = v[i] >= thr;
+          if (c && k < tc::kCand) cand[k * kTile] = make_float2(v[i], __int_as_float(col0 + i));
+          k += c ? 1 : 0;
         }
       }
-      const bool exact_scan = !bounded || cnt > C::kCand;
-      Top7 top;
+    }
+    tc_fence_before();
+    tc::quadrant_sync(quadrant);
+    tc_fence_after();
+
+    // pass 3 (both threads of a row, redundantly): exact top-7 and softmax
+    int pick[kTopK];
+    float wgt[kTopK];
+    if (!aborting) {
+      const int total = row_cnt[row];
+      const bool exact_scan = valid && (!(thr > -INFINITY) || total > tc::kCand);
+      tc::Top7Ord top;
       top.init();
       float masked_raw[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) masked_raw[j] = 0.f;
       if (!exact_scan) {
-        for (int e = 0; e < cnt; ++e) {  // candidates are in slot order: ties keep the lower slot
-          const float2 cd = cand[e];
+        for (int e = 0; e < total; ++e) {
+          const float2 cd = cand[e * kTile];
           top.offer(rank_key(cd.x), __float_as_int(cd.y));
         }
       }
       if (__any_sync(0xffffffffu, exact_scan)) {
-        // exact full scan (rows with fewer than 7 finite group maxima, or many ties)
+        // exact full scan (rows with fewer than 7 finite group maxima, or many candidates)
         for (int c = 0; c < 8; ++c) {
-          float v[32];
-          tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, v);
+          float w32[32];
+          tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, w32);
           tmem_wait_ld();
           if (exact_scan) {
             for (int i = 0; i < 32; ++i) {
               const int m = 32 * c + i;
               if (m >= g.M) break;
               if (m < lim) {
-                top.offer(rank_key(v[i]), m);
+                top.offer(rank_key(w32[i]), m);
               } else {
-                if (m - lim < kTopK) masked_raw[m - lim] = v[i];
+                if (m - lim < kTopK) masked_raw[m - lim] = w32[i];
                 top.offer(kNegInfKey, m);
               }
             }
@@ -350,7 +466,7 @@ __global__ void __launch_bounds__(kTile, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        pick[j] = top.i[j];
+        pick[j] = valid ? top.i[j] : 0;
         // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
         const uint32_t kk = top.k[j];
         const float s = (pick[j] < lim) ? __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk)
@@ -367,15 +483,40 @@ __global__ void __launch_bounds__(kTile, 1)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) wgt[j] = wgt[j] / sum;
     }
-    uint16_t w_lo_bits[kTopK];
-    if (active) {
-      // P row (first term), round records, last-round outputs
+
+    // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
+    if (b_pending) {
+      wait_bar(bar_b, ph_b);
+      b_pending = false;
+    }
+    if (!aborting && part == 0) {
+      row_cnt2[((tile + 1) & 1) * kTile + row] = 0;  // next tile's counter
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        const uint16_t hb = tc::to_bits<T>(wgt[j]);
-        w_lo_bits[j] = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
-        *reinterpret_cast<uint16_t*>(sm + L::OFF_P + (pick[j] >> 6) * 16384 + sw128_offset(tid, pick[j] & 63)) = hb;
+      for (int j = 0; j < kTopK; ++j)
+        if (old_pick[j] >= 0) *p_entry(old_pick[j]) = 0;
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) *p_entry(pick[j]) = tc::to_bits<T>(wgt[j]);
       }
+      fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (*s_abort) break;
+
+    // ---- MMA_A(i), then SELECT(i+1) ----
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk)
+        mma_f16(tmem + tc::COL_O, smem_desc(a_p + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                smem_desc(a_v + kk * 2048, 16384, 1024, kSwizzle128B), ID_ATT, kk != 0);
+      issue_update(tile, tile == 0);
+      mma_commit(bar_a);
+      if (C::kQBufs == 2 && tile + 1 < ntiles && wait_q(tile + 1)) issue_select(tile + 1);
+    }
+    // round records, by the row's second thread (off the tensor-core path)
+    if (!aborting && valid && part == 1) {
       const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
       uint32_t lo = 0, hi = 0;
 #pragma unroll
@@ -398,114 +539,94 @@ __global__ void __launch_bounds__(kTile, 1)
         }
       }
     }
-    sync_all();
-    if (*s_abort) break;
-
-    // ---- MMAs with the first weight term: O = P.V, S += P^T.Q, W += P^T.1 ----
-    auto issue_update = [&](bool first) {  // thread 0
+    wait_bar(bar_a, ph_a);
+    // second weight term
+    if (!aborting && part == 0) {
+      if (valid) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = smem_desc(a_p + 2 * hh * 16384 + kk * 2048, 16384, 1024, kSwizzle128B);
-          const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-          mma_f16(tmem + tc::COL_U + 64 * hh, a, smem_desc(a_q + kk * 2048, 16384, 1024, kSwizzle128B), ID_UPD,
-                  acc);
-          mma_f16(tmem + tc::COL_W + 16 * hh, a, smem_desc(a_ones, 256, 128, kSwizzleNone), ID_W, acc);
+        for (int j = 0; j < kTopK; ++j) {
+          const uint16_t hb = tc::to_bits<T>(wgt[j]);
+          *p_entry(pick[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
         }
       }
-    };
-    if (tid == 0) {
-      tc_fence_after();
+      fence_proxy_async_smem();
 #pragma unroll
-      for (int kk = 0; kk < 16; ++kk)
-        mma_f16(tmem + tc::COL_O, smem_desc(a_p + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                smem_desc(a_v + kk * 2048, 16384, 1024, kSwizzle128B), ID_ATT, kk != 0);
-      issue_update(tile == 0);
-      mma_commit(bar_mma);
+      for (int j = 0; j < kTopK; ++j) old_pick[j] = valid ? pick[j] : -1;
     }
-    wait_mma();
-    // second weight term: overwrite this row's entries of P
-    if (active) {
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j)
-        *reinterpret_cast<uint16_t*>(sm + L::OFF_P + (pick[j] >> 6) * 16384 + sw128_offset(tid, pick[j] & 63)) =
-            w_lo_bits[j];
-    }
-    sync_all();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
     if (*s_abort) break;
+    // ---- MMA_B(i) ----
     if (tid == 0) {
-      tc_fence_after();
-      issue_update(false);
-      mma_commit(bar_mma);
+      issue_update(tile, false);
+      mma_commit(bar_b);
+      if (C::kQBufs == 1 && tile + 1 < ntiles) {  // one Q buffer: it is free once MMA_B(i) is done
+        if (tc::timed_wait(bar_b, ph_b)) ph_b ^= 1; else fail(tc::kErrMmaWait);
+        tc_fence_after();
+        issue_q(tile + 1);
+        if (wait_q(tile + 1)) issue_select(tile + 1);
+      } else {
+        b_pending = true;
+      }
+    } else {
+      b_pending = true;
     }
-
-    // ---- output (overlaps the second update group): out (+)= O ----
+    // ---- output: out (+)= O, 32 columns per thread ----
     if (!__any_sync(0xffffffffu, *s_abort != 0)) {
-      T* orow = row_ptr(out, os, b, h, valid ? n : n0);
+      float o[32];
+      tmem_ld32(tmem + lane_base + tc::COL_O + 32 * part, o);
+      tmem_wait_ld();
+      if (valid) {
+        T* orow = row_ptr(out, os, b, h, n) + 32 * part;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float o[32];
-        tmem_ld32(tmem + lane_base + tc::COL_O + 32 * c, o);
-        tmem_wait_ld();
-        if (valid) {
+        for (int i = 0; i < 32; i += 8) {
+          uint4 pk;
+          uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
+          if (r) {
+            const uint4 prev = *reinterpret_cast<const uint4*>(orow + i);
+            const T* pv = reinterpret_cast<const T*>(&prev);
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 pk;
-            uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
-            if (r) {
-              const uint4 prev = *reinterpret_cast<const uint4*>(orow + 32 * c + i);
-              const T* pv = reinterpret_cast<const T*>(&prev);
+            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(Elem<T>::load(pv + e) + o[i + e]);
+          } else {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(Elem<T>::load(pv + e) + o[i + e]);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(o[i + e]);
-            }
-            *reinterpret_cast<uint4*>(orow + 32 * c + i) = pk;
+            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(o[i + e]);
           }
+          *reinterpret_cast<uint4*>(orow + i) = pk;
         }
       }
     }
-    wait_mma();
-    if (tid == 0 && C::kQBufs == 1 && tile + 1 < ntiles && !*s_abort) issue_q(tile + 1);  // Q is free now
-    if (active) {  // clear this row of P for the next tile
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j)
-        *reinterpret_cast<uint16_t*>(sm + L::OFF_P + (pick[j] >> 6) * 16384 + sw128_offset(tid, pick[j] & 63)) = 0;
-    }
-    sync_all();
-    if (*s_abort) break;
   }
+  if (b_pending) wait_bar(bar_b, ph_b);
 
   // ---- chunk partials: TMEM lanes are slots here ----
   if (!__any_sync(0xffffffffu, *s_abort != 0)) {
     const size_t po = (size_t)bh * g.red_chunks + chunk;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const int m = 128 * hh + tid;
-      float s0[32], s1[32], wv[16];
-      tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh, s0);
-      tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh + 32, s1);
+      const int m = 128 * hh + row;
+      float s32[32], wv[16];
+      tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh + 32 * part, s32);
       tmem_ld16(tmem + lane_base + tc::COL_W + 16 * hh, wv);
       tmem_wait_ld();
       if (m < g.M) {
-        float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD);
+        float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * part);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(s0[4 * i], s0[4 * i + 1], s0[4 * i + 2], s0[4 * i + 3]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[8 + i] = make_float4(s1[4 * i], s1[4 * i + 1], s1[4 * i + 2], s1[4 * i + 3]);
-        fs.Wpart[po * g.M + m] = wv[0];
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
+        if (part == 0) fs.Wpart[po * g.M + m] = wv[0];
       }
     }
   }
-  // ---- wind down: wait (bounded) for copies still in flight, free TMEM ----
+  // ---- wind down: wait (bounded) for copies / MMAs still in flight, free TMEM ----
   if (tid == 0) {
     if (img_pending) tc::timed_wait(bar_img, 0);
-    if (q_pending0) tc::timed_wait(&bar_q[0], q_phase0);
-    if (q_pending1) tc::timed_wait(&bar_q[1], q_phase1);
-    if (*s_abort) tc::timed_wait(bar_mma, mma_phase);  // an MMA group whose completion was not seen
+    for (int i = 0; i < 2; ++i)
+      if (q_pending[i]) tc::timed_wait(&bar_q[i], q_phase[i]);
+    if (*s_abort) {  // groups whose completion was not observed
+      tc::timed_wait(bar_s, ph_s);
+      tc::timed_wait(bar_a, ph_a);
+      tc::timed_wait(bar_b, ph_b);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -586,8 +707,8 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
   }
   launch_load_slots<T>(g, p, sv, st);
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH("tc_images", k_tc_images<T>, g.BH, 256, 0, st, g, r, sv, images);
-    MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), kTile, tc::Layout<T>::kSmem, st, g, r,
+    MURM_LAUNCH("tc_images", k_tc_images<T>, dim3(g.BH, 8), 256, 0, st, g, r, sv, images);
+    MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
     if (r + 1 < g.R) launch_update_finalize(g, r, sv, fs, st);
   }
