@@ -86,7 +86,7 @@ struct Sizes {
   // offsets inside each block
   size_t sK, sV, sU, sW, sIdx, sw;
   size_t fS, fW, fImg;
-  size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq;
+  size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq, btab;
 };
 
 Sizes make_sizes(const Geom& g) {
@@ -115,6 +115,7 @@ Sizes make_sizes(const Geom& g) {
   z.bdVpart = take(BH * g.red_chunks * M * D * 4);
   z.bcoef = take(BH * N * 8 * 4);
   z.bdq = take(BH * N * D * 4);
+  z.btab = take(tc_bwd_tables_bytes(g));
   z.bwd_ws = o;
   return z;
 }
@@ -271,14 +272,18 @@ murm_status murm_slot_murmurate_bwd(const murm_bwd_args* a, void* stream) {
   bs.dKdir = reinterpret_cast<float*>(w + z.bdKdir); bs.dVdir = reinterpret_cast<float*>(w + z.bdVdir);
   bs.dKpart = reinterpret_cast<float*>(w + z.bdKpart); bs.dVpart = reinterpret_cast<float*>(w + z.bdVpart);
   bs.coef = reinterpret_cast<float*>(w + z.bcoef); bs.dq = reinterpret_cast<float*>(w + z.bdq);
+  bs.tables = reinterpret_cast<uint8_t*>(w + z.btab);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
+  const bool tc = tc_backward_supported(g, g.dtype, p);
   switch (a->shape.dtype) {
     case MURM_F32: e = bwd_simt<float>(g, p, sv, bs, st); break;
-    case MURM_F16: e = bwd_simt<__half>(g, p, sv, bs, st); break;
-    case MURM_BF16: e = bwd_simt<__nv_bfloat16>(g, p, sv, bs, st); break;
+    case MURM_F16: e = tc ? bwd_tc<__half>(g, p, sv, bs, st) : bwd_simt<__half>(g, p, sv, bs, st); break;
+    case MURM_BF16:
+      e = tc ? bwd_tc<__nv_bfloat16>(g, p, sv, bs, st) : bwd_simt<__nv_bfloat16>(g, p, sv, bs, st);
+      break;
   }
-  return cuda_status(e, "slot_murmurate backward launch");
+  return cuda_status(e, tc ? "slot_murmurate backward (tensor-core) launch" : "slot_murmurate backward launch");
 }
 
 }  // extern "C"

@@ -110,6 +110,7 @@ struct BwdScratch {
   float* dVpart;
   float* coef;   // [BH][N][8] scale * dlogit per pick
   float* dq;     // [BH][N][D] running dL/dq over rounds
+  uint8_t* tables;  // [BH][3][256][64] 16-bit K, V, dS of a round + [BH][256] fp32 dW (tensor-core path)
 };
 
 }  // namespace murm

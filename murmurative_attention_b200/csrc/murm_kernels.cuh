@@ -57,6 +57,11 @@ bool tc_forward_supported(const Geom& g, int dtype, const FwdPtrs& p);
 size_t tc_images_bytes(const Geom& g);
 template <typename T>
 cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdScratch& fs, cudaStream_t st);
+// Tensor-core backward (murm_tc_bwd.cu): same conditions as the forward.
+bool tc_backward_supported(const Geom& g, int dtype, const BwdPtrs& p);
+size_t tc_bwd_tables_bytes(const Geom& g);
+template <typename T>
+cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdScratch& bs, cudaStream_t st);
 // Device error word written by bounded waits in tensor-core kernels.
 cudaError_t read_and_clear_device_error(int* code, cudaStream_t st);
 

@@ -653,6 +653,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tc_tensor_map_encoder() { return get_encode(); }
+
 size_t tc_images_bytes(const Geom& g) {
   if (g.D != tc::kD) return 0;
   if (g.dtype == MURM_F16) return (size_t)g.BH * tc::Layout<__half>::kImages;

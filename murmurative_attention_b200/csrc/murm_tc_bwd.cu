@@ -1,0 +1,568 @@
+// murm_tc_bwd.cu — backward of the round loop for fp16/bf16, head_dim 64:
+// CUDA-core token math + tcgen05 slot scatters.
+//
+// Reverse-mode of reference.py:177-189 (autograd through reference.py:42-68,
+// 71-115, 118-135). For round r, with G = dL/d out (the same for every round
+// because out = sum of the rounds' attend outputs):
+//   dw_j = G . V[i_j] + q . dS[i_j] + dW[i_j]  (+ dL/d weights in the last round)
+//   da_j = w_j (dw_j - sum_k w_k dw_k)                       (softmax adjoint)
+//   dq  += sum_j w_j dS[i_j] + scale da_j K[i_j]
+//   dK_r = dKdir_r + sum over picks of scale da_j q          (slot scatter)
+//   dV_r = dVdir_r + sum over picks of w_j G                 (slot scatter)
+// with dS = dU / (W + eps), dW = -(dU . U) / (W + eps), dU = (1-alpha)(dK' + dV')
+// on slots that received picks, dK' = D^T dK_{r+1} (diffusion adjoint), and
+// dKdir = alpha dK' (or dK' on slots without picks).
+//
+// k_bwd_tokens_tc: one CTA per (batch, head) and token chunk, 8 warps. A warp
+// handles one token at a time with 2 head dims per lane; the slot tables K_r,
+// V_r, dS_r (16-bit) and dW_r sit in shared memory. The slot scatters are
+// dense tensor-core products over a 128 x 256 tile P that holds the 7 picks of
+// every token: dV += P^T . G with P = w, then dK += P^T . Q with P = scale da,
+// accumulated in TMEM over the chunk — deterministic, no atomics.
+// k_bwd_slots: finalize of round r (direct part + chunk partials, in chunk
+// order) fused with the per-slot adjoints of round r-1, warp per slot row.
+#include <cudaTypedefs.h>
+
+#include "murm_kernels.cuh"
+#include "murm_sm100.cuh"
+
+namespace murm {
+using namespace sm100;
+
+extern __device__ int g_device_error;
+
+namespace tcb {
+constexpr int kD = 64;
+constexpr int kSlotsPad = 256;
+constexpr int kThreads = 256;
+constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
+constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
+constexpr uint32_t kTables = 3 * kTable;
+constexpr uint32_t OFF_DW = kTables;                 // fp32 [256]
+constexpr uint32_t OFF_P = OFF_DW + 1024;            // 4 slot blocks x 16 KB (1024-aligned)
+constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;        // q tile, swizzled (MMA operand)
+constexpr uint32_t OFF_G = OFF_Q + 16384;            // grad_out tile, swizzled
+constexpr uint32_t OFF_COEF = OFF_G + 16384;         // fp32 [128][8]
+constexpr uint32_t OFF_MISC = OFF_COEF + kTile * 8 * 4;
+constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;
+static_assert(kSmem <= 232448, "shared memory budget");
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t COL_DV = 0, COL_DK = 128;
+enum : int { kErrWait = 8 };
+
+__device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 1000000000ull) return false;
+  }
+}
+
+template <typename T> struct Fmt;
+template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
+template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+
+template <typename T>
+__device__ __forceinline__ uint16_t bits(float x) {
+  T h;
+  Elem<T>::store(&h, x);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+// two consecutive 16-bit values -> float2
+template <typename T>
+__device__ __forceinline__ float2 load2(const void* p) {
+  const T* t = reinterpret_cast<const T*>(p);
+  return make_float2(Elem<T>::load(t), Elem<T>::load(t + 1));
+}
+
+// Sum each of v[0..7] over the 32 lanes; on return every lane holds all 8 sums.
+__device__ __forceinline__ void warp_sum8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  // transpose-reduce: halve the set of values per lane at each step
+#pragma unroll
+  for (int s = 16, n = 4; s >= 4; s >>= 1, n >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < n; ++k) {
+      const float send = upper ? v[k] : v[k + n];
+      const float keep = upper ? v[k + n] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  float x = v[0];
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  // lane l now holds the total of value index ((l>>4)&1)*4 + ((l>>3)&1)*2 + ((l>>2)&1)
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int src = ((j >> 2) & 1) * 16 + ((j >> 1) & 1) * 8 + (j & 1) * 4;
+    v[j] = __shfl_sync(0xffffffffu, x, src);
+  }
+}
+}  // namespace tcb
+
+// ---------------------------------------------------------------------------
+// Slot side: finalize round r (dK_r, dV_r) and, for r > 0, the adjoints of
+// round r-1 (dS, dW, direct parts) plus its 16-bit tables for the token kernel.
+// grid (BH, ceil(M/32)), 256 threads; warp per slot row, 2 dims per lane.
+// ---------------------------------------------------------------------------
+// Direct parts live in bs.dK[r & 1] / bs.dV[r & 1] (round parity): a block reads
+// its neighbours' rows of round r while they write round r-1.
+template <typename T>
+__global__ void __launch_bounds__(256) k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv,
+                                                   BwdScratch bs, uint8_t* tables, float* dWpad, T* gsk,
+                                                   Strides3 gsks, T* gsv, Strides3 gsvs) {
+  const float* dir_k = bs.dK[r & 1];
+  const float* dir_v = bs.dV[r & 1];
+  float* nxt_k = bs.dK[(r + 1) & 1];  // direct parts of round r-1
+  float* nxt_v = bs.dV[(r + 1) & 1];
+  __shared__ float2 skk[34][32];  // dK_r rows m0-1 .. m0+32, as float2 per lane
+  __shared__ float2 svv[34][32];
+  const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H;
+  const int m0 = blockIdx.y * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t MD = (size_t)g.M * g.D;
+  // 1. dK_r, dV_r for the block and its halo
+  for (int rr = warp; rr < 34; rr += 8) {
+    const int m = m0 - 1 + rr;
+    float2 k = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+    if (m >= 0 && m < g.M) {
+      const size_t e = bh * MD + (size_t)m * g.D + 2 * lane;
+      if (has_dir) {
+        k = *reinterpret_cast<const float2*>(dir_k + e);
+        v = *reinterpret_cast<const float2*>(dir_v + e);
+      }
+      if (has_part) {
+        for (int ch = 0; ch < g.red_chunks; ++ch) {
+          const size_t po = ((size_t)bh * g.red_chunks + ch) * MD + (size_t)m * g.D + 2 * lane;
+          const float2 a = *reinterpret_cast<const float2*>(bs.dKpart + po);
+          const float2 c = *reinterpret_cast<const float2*>(bs.dVpart + po);
+          k.x += a.x; k.y += a.y; v.x += c.x; v.y += c.y;
+        }
+      }
+    }
+    skk[rr][lane] = k;
+    svv[rr][lane] = v;
+  }
+  __syncthreads();
+  if (r == 0) {  // the slot gradients
+    for (int rr = 1 + warp; rr < 33; rr += 8) {
+      const int m = m0 - 1 + rr;
+      if (m >= g.M) break;
+      T* pk = row_ptr(gsk, gsks, b, h, m) + 2 * lane;
+      T* pv = row_ptr(gsv, gsvs, b, h, m) + 2 * lane;
+      Elem<T>::store(pk, skk[rr][lane].x);
+      Elem<T>::store(pk + 1, skk[rr][lane].y);
+      Elem<T>::store(pv, svv[rr][lane].x);
+      Elem<T>::store(pv + 1, svv[rr][lane].y);
+    }
+    return;
+  }
+  // 2. adjoints of round r-1 for slots of this block
+  const int rp = r - 1;
+  const float gm2 = -2.f * g.gamma;
+  uint8_t* tab = tables + (size_t)bh * tcb::kTables;
+  for (int rr = 1 + warp; rr < 33; rr += 8) {
+    const int m = m0 - 1 + rr;
+    if (m >= g.M) break;
+    const bool in_m = m > 0 && m < g.M - 1, in_l = m - 1 > 0, in_r = m + 1 < g.M - 1;
+    float2 ak = skk[rr][lane], av = svv[rr][lane];
+    if (in_m) {
+      ak.x = __fadd_rn(ak.x, __fmul_rn(gm2, ak.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(gm2, ak.y));
+      av.x = __fadd_rn(av.x, __fmul_rn(gm2, av.x)); av.y = __fadd_rn(av.y, __fmul_rn(gm2, av.y));
+    }
+    if (in_l) {
+      const float2 lk = skk[rr - 1][lane], lv = svv[rr - 1][lane];
+      ak.x = __fadd_rn(ak.x, __fmul_rn(g.gamma, lk.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(g.gamma, lk.y));
+      av.x = __fadd_rn(av.x, __fmul_rn(g.gamma, lv.x)); av.y = __fadd_rn(av.y, __fmul_rn(g.gamma, lv.y));
+    }
+    if (in_r) {
+      const float2 rk = skk[rr + 1][lane], rv = svv[rr + 1][lane];
+      ak.x = __fadd_rn(ak.x, __fmul_rn(g.gamma, rk.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(g.gamma, rk.y));
+      av.x = __fadd_rn(av.x, __fmul_rn(g.gamma, rv.x)); av.y = __fadd_rn(av.y, __fmul_rn(g.gamma, rv.y));
+    }
+    const float W = sv.W[((size_t)rp * g.BH + bh) * g.M + m];
+    const bool hit = W > 0.f;
+    const float den = __fadd_rn(W, kEmaEps);
+    float2 dU = make_float2(0.f, 0.f);
+    if (hit) {
+      dU.x = __fmul_rn(g.one_minus_alpha, __fadd_rn(ak.x, av.x));
+      dU.y = __fmul_rn(g.one_minus_alpha, __fadd_rn(ak.y, av.y));
+    }
+    const size_t st = ((size_t)rp * g.BH + bh) * MD + (size_t)m * g.D + 2 * lane;
+    const float2 U = *reinterpret_cast<const float2*>(sv.U + st);
+    float dot = fmaf(dU.x, U.x, dU.y * U.y);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const float2 dS = make_float2(__fdiv_rn(dU.x, den), __fdiv_rn(dU.y, den));
+    const size_t e = bh * MD + (size_t)m * g.D + 2 * lane;
+    *reinterpret_cast<float2*>(nxt_k + e) =
+        hit ? make_float2(__fmul_rn(g.alpha, ak.x), __fmul_rn(g.alpha, ak.y)) : ak;
+    *reinterpret_cast<float2*>(nxt_v + e) =
+        hit ? make_float2(__fmul_rn(g.alpha, av.x), __fmul_rn(g.alpha, av.y)) : av;
+    if (lane == 0) dWpad[(size_t)bh * tcb::kSlotsPad + m] = -__fdiv_rn(dot, den);
+    // 16-bit tables of round r-1 (row-major [256][64])
+    const float2 K = *reinterpret_cast<const float2*>(sv.K + st);
+    const float2 V = *reinterpret_cast<const float2*>(sv.V + st);
+    const uint32_t off = (uint32_t)m * 128 + 4 * lane;
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_K + off) = tcb::bits<T>(K.x) | ((uint32_t)tcb::bits<T>(K.y) << 16);
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_V + off) = tcb::bits<T>(V.x) | ((uint32_t)tcb::bits<T>(V.y) << 16);
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_DS + off) =
+        tcb::bits<T>(dS.x) | ((uint32_t)tcb::bits<T>(dS.y) << 16);
+  }
+}
+
+// Tables of the last round (no slot gradient flows into it): K, V; dS = 0, dW = 0.
+template <typename T>
+__global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8_t* tables, float* dWpad) {
+  const int bh = blockIdx.x;
+  const size_t st = ((size_t)(g.R - 1) * g.BH + bh) * g.M * g.D;
+  uint8_t* tab = tables + (size_t)bh * tcb::kTables;
+  for (int e = blockIdx.y * blockDim.x + threadIdx.x; e < tcb::kSlotsPad * 32; e += gridDim.y * blockDim.x) {
+    const int m = e >> 5, l = e & 31;
+    float2 K = make_float2(0.f, 0.f), V = K;
+    if (m < g.M) {
+      K = *reinterpret_cast<const float2*>(sv.K + st + (size_t)m * g.D + 2 * l);
+      V = *reinterpret_cast<const float2*>(sv.V + st + (size_t)m * g.D + 2 * l);
+    }
+    const uint32_t off = (uint32_t)m * 128 + 4 * l;
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_K + off) = tcb::bits<T>(K.x) | ((uint32_t)tcb::bits<T>(K.y) << 16);
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_V + off) = tcb::bits<T>(V.x) | ((uint32_t)tcb::bits<T>(V.y) << 16);
+    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_DS + off) = 0u;
+    if (l == 0) dWpad[(size_t)bh * tcb::kSlotsPad + m] = 0.f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Token side of round r
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(tcb::kThreads, 1)
+    k_bwd_tokens_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
+                    const T* q, Strides3 qs, const T* go, Strides3 gos, const float* gw, T* gq, Strides3 gqs,
+                    Saved sv, BwdScratch bs, const uint8_t* tables, const float* dWpad) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t s_base = smem_u32(sm);
+  uint64_t* bar_tab = reinterpret_cast<uint64_t*>(sm + tcb::OFF_MISC);
+  uint64_t* bar_qg = bar_tab + 1;
+  uint64_t* bar_mma = bar_tab + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + tcb::OFF_MISC + 64);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + tcb::OFF_MISC + 68);
+  const float* dWs = reinterpret_cast<const float*>(sm + tcb::OFF_DW);
+  float* coef = reinterpret_cast<float*>(sm + tcb::OFF_COEF);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
+  const int t_beg = chunk * g.red_chunk_tokens;
+  const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
+  const int ntiles = (t_end - t_beg + kTile - 1) / kTile;
+  const bool has_slot_grad = r < g.R - 1;
+  const bool first = (r == g.R - 1);
+  constexpr uint32_t ID_UPD = idesc_f16(tcb::Fmt<T>::v, 128, 64, 1, 1);
+
+  if (tid == 0) {
+    mbar_init(bar_tab, 1);
+    mbar_init(bar_qg, 1);
+    mbar_init(bar_mma, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  {
+    float4* p4 = reinterpret_cast<float4*>(sm + tcb::OFF_P);
+    for (int i = tid; i < 4 * 16384 / 16; i += tcb::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, tcb::kTmemCols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  uint32_t ph_qg = 0, ph_mma = 0;
+  bool tab_pending = false, qg_pending = false;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_tab, tcb::kTables + 1024);
+    bulk_g2s(sm, tables + (size_t)bh * tcb::kTables, tcb::kTables, bar_tab);
+    bulk_g2s(sm + tcb::OFF_DW, dWpad + (size_t)bh * tcb::kSlotsPad, 1024, bar_tab);
+    tab_pending = true;
+    mbar_arrive_expect_tx(bar_qg, 2 * 16384);
+    tma_load_4d(sm + tcb::OFF_Q, &qmap, 0, t_beg, h, b, bar_qg);
+    tma_load_4d(sm + tcb::OFF_G, &gmap, 0, t_beg, h, b, bar_qg);
+    qg_pending = true;
+  }
+  // every thread reads the tables: wait for them once
+  if (!tcb::timed_wait(bar_tab, 0)) {
+    atomicOr(&g_device_error, tcb::kErrWait);
+    *s_abort = 1;
+  } else if (tid == 0) {
+    tab_pending = false;
+  }
+  __syncthreads();
+
+  const uint8_t* tK = sm + tcb::OFF_K;
+  const uint8_t* tV = sm + tcb::OFF_V;
+  const uint8_t* tS = sm + tcb::OFF_DS;
+  const uint32_t a_p = s_base + tcb::OFF_P, a_q = s_base + tcb::OFF_Q, a_g = s_base + tcb::OFF_G;
+  auto p_entry = [&](int t, int m) -> uint16_t* {
+    return reinterpret_cast<uint16_t*>(sm + tcb::OFF_P + (m >> 6) * 16384 + sw128_offset(t, m & 63));
+  };
+  auto issue_scatter = [&](uint32_t a_b, uint32_t col, bool first_acc) {  // thread 0: D += P^T . B
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16(tmem + col + 64 * hh, smem_desc(a_p + 2 * hh * 16384 + kk * 2048, 16384, 1024, kSwizzle128B),
+                smem_desc(a_b + kk * 2048, 16384, 1024, kSwizzle128B), ID_UPD, (first_acc && kk == 0) ? 0u : 1u);
+  };
+  auto wait_mma = [&]() {
+    if (tcb::timed_wait(bar_mma, ph_mma)) ph_mma ^= 1;
+    else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+    tc_fence_after();
+  };
+
+  for (int tile = 0; tile < ntiles && !*s_abort; ++tile) {
+    const int n0 = t_beg + tile * kTile;
+    // ---- token math: warp per token ----
+    for (int t = warp; t < kTile; t += 8) {
+      const int n = n0 + t;
+      if (n >= t_end) break;
+      const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
+      const uint2 pk = reinterpret_cast<const uint2*>(sv.idx)[trow];
+      int ix[kTopK];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ix[j] = (pk.x >> (8 * j)) & 0xff;
+#pragma unroll
+      for (int j = 4; j < kTopK; ++j) ix[j] = (pk.y >> (8 * (j - 4))) & 0xff;
+      const float4 w0 = reinterpret_cast<const float4*>(sv.w + trow * 8)[0];
+      const float4 w1 = reinterpret_cast<const float4*>(sv.w + trow * 8)[1];
+      const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
+      const float2 qv = tcb::load2<T>(row_ptr(q, qs, b, h, n) + 2 * lane);
+      const float2 gv = tcb::load2<T>(row_ptr(go, gos, b, h, n) + 2 * lane);
+      float part[8];
+      float2 dsr[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        const float2 vv = tcb::load2<T>(tV + ix[j] * 128 + 4 * lane);
+        dsr[j] = tcb::load2<T>(tS + ix[j] * 128 + 4 * lane);
+        part[j] = fmaf(gv.x, vv.x, gv.y * vv.y);
+        if (has_slot_grad) part[j] = fmaf(qv.x, dsr[j].x, fmaf(qv.y, dsr[j].y, part[j]));
+      }
+      part[7] = 0.f;
+      tcb::warp_sum8(part);
+      float dw[kTopK], s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        dw[j] = part[j] + (has_slot_grad ? dWs[ix[j]] : 0.f);
+        if (gw && first) dw[j] += gw[((size_t)bh * g.N + n) * kTopK + j];
+        s = fmaf(w[j], dw[j], s);
+      }
+      float c[kTopK];
+      float2 dq = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        c[j] = g.scale * (w[j] * (dw[j] - s));
+        const float2 kv = tcb::load2<T>(tK + ix[j] * 128 + 4 * lane);
+        dq.x = fmaf(c[j], kv.x, dq.x);
+        dq.y = fmaf(c[j], kv.y, dq.y);
+        if (has_slot_grad) {
+          dq.x = fmaf(w[j], dsr[j].x, dq.x);
+          dq.y = fmaf(w[j], dsr[j].y, dq.y);
+        }
+      }
+      float2* acc = reinterpret_cast<float2*>(bs.dq + ((size_t)bh * g.N + n) * g.D) + lane;
+      if (!first) {
+        const float2 p = *acc;
+        dq.x += p.x;
+        dq.y += p.y;
+      }
+      if (r == 0) {
+        T* gr = row_ptr(gq, gqs, b, h, n) + 2 * lane;
+        Elem<T>::store(gr, dq.x);
+        Elem<T>::store(gr + 1, dq.y);
+      } else {
+        *acc = dq;
+      }
+      if (lane < kTopK) {  // this token's row of P (first product: weights) and its coefficients
+        float wl = 0.f, cl = 0.f;
+        int ml = 0;
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j)
+          if (lane == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
+        *p_entry(t, ml) = tcb::bits<T>(wl);
+        coef[t * 8 + lane] = cl;
+      }
+    }
+    // The scatters run as MMA phases over P: dV += P^T.G with P = w, then
+    // dK += P^T.Q with P = scale*da. For bf16 each weight goes in as two terms
+    // (hi = rn(x), lo = rn(x - hi)): bf16 alone would round them to 2^-9.
+    constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
+    bool ok = true;
+#pragma unroll 1
+    for (int ph = 0; ph < 2 * kTerms && ok; ++ph) {
+      const bool is_k = ph >= kTerms;   // dK phases use the coefficients, dV phases the weights
+      const bool lo = (ph % kTerms) == 1;
+      if (ph > 0) {  // rewrite this tile's P entries for the phase
+        for (int t = warp; t < kTile; t += 8) {
+          const int n = n0 + t;
+          if (n >= t_end) break;
+          if (lane < kTopK) {
+            const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
+            const int ml = sv.idx[trow * 8 + lane];
+            const float x = is_k ? coef[t * 8 + lane] : sv.w[trow * 8 + lane];
+            const uint16_t hb = tcb::bits<T>(x);
+            *p_entry(t, ml) = lo ? tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb))) : hb;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (*s_abort) { ok = false; break; }
+      if (tid == 0) {
+        bool go_on = true;
+        if (qg_pending) {
+          go_on = tcb::timed_wait(bar_qg, ph_qg);
+          if (go_on) { ph_qg ^= 1; qg_pending = false; }
+          else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+        }
+        if (go_on) {
+          tc_fence_after();
+          issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && (ph % kTerms) == 0);
+          mma_commit(bar_mma);
+        }
+      }
+      wait_mma();
+    }
+    if (*s_abort) break;
+    // clear P, fetch the next q/grad_out tiles
+    for (int t = warp; t < kTile; t += 8) {
+      const int n = n0 + t;
+      if (n >= t_end) break;
+      if (lane < kTopK) {
+        const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
+        *p_entry(t, sv.idx[trow * 8 + lane]) = 0;
+      }
+    }
+    if (tid == 0 && tile + 1 < ntiles && !*s_abort) {
+      mbar_arrive_expect_tx(bar_qg, 2 * 16384);
+      tma_load_4d(sm + tcb::OFF_Q, &qmap, 0, n0 + kTile, h, b, bar_qg);
+      tma_load_4d(sm + tcb::OFF_G, &gmap, 0, n0 + kTile, h, b, bar_qg);
+      qg_pending = true;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+
+  // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
+  if (!__any_sync(0xffffffffu, *s_abort != 0)) {
+    const int quad = warp & 3;
+    const uint32_t lb = (uint32_t)(32 * quad) << 16;
+    const bool is_k = warp >= 4;
+    float* dst_base = is_k ? bs.dKpart : bs.dVpart;
+    const size_t po = (size_t)bh * g.red_chunks + chunk;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int m = 128 * hh + 32 * quad + lane;
+      float a[32], c2[32];
+      const uint32_t col = (is_k ? tcb::COL_DK : tcb::COL_DV) + 64 * hh;
+      tmem_ld32(tmem + lb + col, a);
+      tmem_ld32(tmem + lb + col + 32, c2);
+      tmem_wait_ld();
+      if (m < g.M) {
+        float4* dst = reinterpret_cast<float4*>(dst_base + (po * g.M + m) * g.D);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[8 + i] = make_float4(c2[4 * i], c2[4 * i + 1], c2[4 * i + 2], c2[4 * i + 3]);
+      }
+    }
+  }
+  if (tid == 0) {
+    if (tab_pending) tcb::timed_wait(bar_tab, 0);
+    if (qg_pending) tcb::timed_wait(bar_qg, ph_qg);
+    if (*s_abort) tcb::timed_wait(bar_mma, ph_mma);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tcb::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tc_tensor_map_encoder();  // murm_tc.cu
+
+template <typename T>
+static bool make_rows_map(CUtensorMap* map, const Geom& g, const void* base, Strides3 st) {
+  auto encode = tc_tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t esz = sizeof(T);
+  cuuint64_t dims[4] = {(cuuint64_t)g.D, (cuuint64_t)g.N, (cuuint64_t)g.H, (cuuint64_t)g.B};
+  cuuint64_t strides[3] = {(cuuint64_t)st.s[2] * esz, (cuuint64_t)st.s[1] * esz,
+                           (cuuint64_t)(st.s[0] ? st.s[0] : 1) * esz};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      tcb::Fmt<T>::v == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_backward_supported(const Geom& g, int dtype, const BwdPtrs& p) {
+  if (dtype != MURM_F16 && dtype != MURM_BF16) return false;
+  if (g.D != tcb::kD || g.R < 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((p.qs.s[i] % 8) || (p.gos.s[i] % 8)) return false;
+  if ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.go)) & 15) return false;
+  const char* force = getenv("MURM_FORCE_SIMT");
+  return !(force && force[0] == '1');
+}
+
+size_t tc_bwd_tables_bytes(const Geom& g) {
+  if (g.D != tcb::kD || g.dtype == MURM_F32) return 0;
+  return (size_t)g.BH * (tcb::kTables + tcb::kSlotsPad * 4);
+}
+
+template <typename T>
+cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdScratch& bs, cudaStream_t st) {
+  CUtensorMap qmap, gmap;
+  if (!make_rows_map<T>(&qmap, g, p.q, p.qs) || !make_rows_map<T>(&gmap, g, p.go, p.gos))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_bwd_tokens_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcb::kSmem);
+    attr = true;
+  }
+  uint8_t* tables = bs.tables;
+  float* dWpad = reinterpret_cast<float*>(tables + (size_t)g.BH * tcb::kTables);
+  const int slot_blocks = (g.M + 31) / 32;
+  MURM_LAUNCH("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, 4), 256, 0, st, g, sv, tables, dWpad);
+  for (int r = g.R - 1; r >= 0; --r) {
+    MURM_LAUNCH("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
+                qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,
+                static_cast<T*>(p.gq), p.gqs, sv, bs, tables, dWpad);
+    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), 256, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
+                sv, bs, tables, dWpad, static_cast<T*>(p.gsk), p.gsks, static_cast<T*>(p.gsv), p.gsvs);
+  }
+  return cudaGetLastError();
+}
+
+template cudaError_t bwd_tc<__half>(const Geom&, const BwdPtrs&, const Saved&, const BwdScratch&, cudaStream_t);
+template cudaError_t bwd_tc<__nv_bfloat16>(const Geom&, const BwdPtrs&, const Saved&, const BwdScratch&,
+                                           cudaStream_t);
+
+}  // namespace murm
