@@ -409,16 +409,29 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       tc::merge8_desc(&lst[0], &lst[8], all8);
       thr = all8[kTopK - 1];
       const bool bounded = thr > -INFINITY;
-      int cnt = 0;
+      int cc[4];  // candidates per 32-column chunk (masked columns are -inf)
 #pragma unroll
-      for (int i = 0; i < 128; ++i) cnt += (bounded && v[i] >= thr) ? 1 : 0;  // masked columns are -inf
+      for (int c = 0; c < 4; ++c) {
+        int x = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x += (bounded && v[32 * c + i] >= thr) ? 1 : 0;
+        cc[c] = x;
+      }
+      const int cnt = cc[0] + cc[1] + cc[2] + cc[3];
       if (cnt && valid) {
-        int k = atomicAdd(&row_cnt[row], cnt);  // order-free: Top7Ord
+        int k[4];
+        k[0] = atomicAdd(&row_cnt[row], cnt);  // order-free: Top7Ord
+        k[1] = k[0] + cc[0];
+        k[2] = k[1] + cc[1];
+        k[3] = k[2] + cc[2];
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const bool c = v[i] >= thr;
-          if (c && k < tc::kCand) cand[k * kTile] = make_float2(v[i], __int_as_float(col0 + i));
-          k += c ? 1 : 0;
+        for (int i = 0; i < 32; ++i) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {  // four independent append chains
+            const bool hit = v[32 * c + i] >= thr;
+            if (hit && k[c] < tc::kCand) cand[k[c] * kTile] = make_float2(v[32 * c + i], __int_as_float(col0 + 32 * c + i));
+            k[c] += hit ? 1 : 0;
+          }
         }
       }
     }
@@ -434,9 +447,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       const bool exact_scan = valid && (!(thr > -INFINITY) || total > tc::kCand);
       tc::Top7Ord top;
       top.init();
-      float masked_raw[kTopK];
+      // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
+      float mraw[kTopK];
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) masked_raw[j] = 0.f;
+      for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
       if (!exact_scan) {
         for (int e = 0; e < total; ++e) {
           const float2 cd = cand[e * kTile];
@@ -445,18 +459,22 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
       if (__any_sync(0xffffffffu, exact_scan)) {
         // exact full scan (rows with fewer than 7 finite group maxima, or many candidates)
+#pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float w32[32];
           tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, w32);
           tmem_wait_ld();
-          if (exact_scan) {
+          if (exact_scan) {  // rare path: kept compact (not unrolled)
+#pragma unroll 1
             for (int i = 0; i < 32; ++i) {
               const int m = 32 * c + i;
-              if (m >= g.M) break;
               if (m < lim) {
                 top.offer(rank_key(w32[i]), m);
-              } else {
-                if (m - lim < kTopK) masked_raw[m - lim] = w32[i];
+              } else if (m < g.M) {
+                if (m - lim < kTopK) {
+#pragma unroll
+                  for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[i] : mraw[j];
+                }
                 top.offer(kNegInfKey, m);
               }
             }
@@ -469,8 +487,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         pick[j] = valid ? top.i[j] : 0;
         // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
         const uint32_t kk = top.k[j];
-        const float s = (pick[j] < lim) ? __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk)
-                                        : masked_raw[min(max(pick[j] - lim, 0), kTopK - 1)];
+        float s = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
+        if (pick[j] >= lim) {
+#pragma unroll
+          for (int k2 = 0; k2 < kTopK; ++k2) s = (pick[j] == lim + k2) ? mraw[k2] : s;
+        }
         wgt[j] = s * g.scale;
         mx = fmaxf(mx, wgt[j]);
       }
@@ -574,25 +595,24 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     }
     // ---- output: out (+)= O, 32 columns per thread ----
     if (!__any_sync(0xffffffffu, *s_abort != 0)) {
+      T* orow = row_ptr(out, os, b, h, valid ? n : n0) + 32 * part;
+      uint4 prev[4];
+      if (r && valid) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) prev[i] = reinterpret_cast<const uint4*>(orow)[i];  // before the TMEM read
+      }
       float o[32];
       tmem_ld32(tmem + lane_base + tc::COL_O + 32 * part, o);
       tmem_wait_ld();
       if (valid) {
-        T* orow = row_ptr(out, os, b, h, n) + 32 * part;
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
+        for (int i = 0; i < 4; ++i) {
           uint4 pk;
           uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
-          if (r) {
-            const uint4 prev = *reinterpret_cast<const uint4*>(orow + i);
-            const T* pv = reinterpret_cast<const T*>(&prev);
+          const T* pv = reinterpret_cast<const T*>(&prev[i]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(Elem<T>::load(pv + e) + o[i + e]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>(o[i + e]);
-          }
-          *reinterpret_cast<uint4*>(orow + i) = pk;
+          for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>((r ? Elem<T>::load(pv + e) : 0.f) + o[8 * i + e]);
+          reinterpret_cast<uint4*>(orow)[i] = pk;
         }
       }
     }

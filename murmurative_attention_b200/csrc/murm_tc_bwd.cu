@@ -42,8 +42,11 @@ constexpr uint32_t OFF_DW = kTables;                 // fp32 [256]
 constexpr uint32_t OFF_P = OFF_DW + 1024;            // 4 slot blocks x 16 KB (1024-aligned)
 constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;        // q tile, swizzled (MMA operand)
 constexpr uint32_t OFF_G = OFF_Q + 16384;            // grad_out tile, swizzled
-constexpr uint32_t OFF_COEF = OFF_G + 16384;         // fp32 [128][8]
-constexpr uint32_t OFF_MISC = OFF_COEF + kTile * 8 * 4;
+constexpr uint32_t OFF_COEF = OFF_G + 16384;         // fp32 [128][8] scale*da per pick
+constexpr uint32_t OFF_TW = OFF_COEF + kTile * 8 * 4;  // fp32 [128][8] weights of the tile's tokens
+constexpr uint32_t OFF_TGW = OFF_TW + kTile * 8 * 4;   // fp32 [128][8] dL/d weights (last round)
+constexpr uint32_t OFF_TIX = OFF_TGW + kTile * 8 * 4;  // u8 [128][8] picks
+constexpr uint32_t OFF_MISC = OFF_TIX + kTile * 8;
 constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 256;
@@ -329,22 +332,47 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
 
   for (int tile = 0; tile < ntiles && !*s_abort; ++tile) {
     const int n0 = t_beg + tile * kTile;
-    // ---- token math: warp per token ----
+    // ---- the tile's picks, weights (and last-round weight gradients) into shared memory ----
+    float* tw = reinterpret_cast<float*>(sm + tcb::OFF_TW);
+    float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
+    uint8_t* tix = sm + tcb::OFF_TIX;
+    {
+      const int nt = min(kTile, t_end - n0);
+      const size_t trow0 = ((size_t)r * g.BH + bh) * g.N + n0;
+      if (tid < nt) reinterpret_cast<uint2*>(tix)[tid] = reinterpret_cast<const uint2*>(sv.idx)[trow0 + tid];
+      if ((tid >> 1) < nt) reinterpret_cast<float4*>(tw)[tid] = reinterpret_cast<const float4*>(sv.w + trow0 * 8)[tid];
+      if (gw && first) {
+        const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
+        for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
+      }
+    }
+    if (tid == 0 && qg_pending) {  // q / grad_out tiles (read below and by the MMAs)
+      if (tcb::timed_wait(bar_qg, ph_qg)) { ph_qg ^= 1; qg_pending = false; }
+      else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+    }
+    __syncthreads();
+    if (*s_abort) break;
+    // ---- token math: warp per token, 2 head dims per lane ----
+    const uint8_t* sq = sm + tcb::OFF_Q;
+    const uint8_t* sgo = sm + tcb::OFF_G;
     for (int t = warp; t < kTile; t += 8) {
       const int n = n0 + t;
       if (n >= t_end) break;
-      const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
-      const uint2 pk = reinterpret_cast<const uint2*>(sv.idx)[trow];
+      float2* acc = reinterpret_cast<float2*>(bs.dq + ((size_t)bh * g.N + n) * g.D) + lane;
+      const float2 prev = first ? make_float2(0.f, 0.f) : *acc;  // issued early, used at the end
+      const uint2 pk = reinterpret_cast<const uint2*>(tix)[t];
       int ix[kTopK];
 #pragma unroll
       for (int j = 0; j < 4; ++j) ix[j] = (pk.x >> (8 * j)) & 0xff;
 #pragma unroll
       for (int j = 4; j < kTopK; ++j) ix[j] = (pk.y >> (8 * (j - 4))) & 0xff;
-      const float4 w0 = reinterpret_cast<const float4*>(sv.w + trow * 8)[0];
-      const float4 w1 = reinterpret_cast<const float4*>(sv.w + trow * 8)[1];
+      const float4 w0 = reinterpret_cast<const float4*>(tw + t * 8)[0];
+      const float4 w1 = reinterpret_cast<const float4*>(tw + t * 8)[1];
       const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
-      const float2 qv = tcb::load2<T>(row_ptr(q, qs, b, h, n) + 2 * lane);
-      const float2 gv = tcb::load2<T>(row_ptr(go, gos, b, h, n) + 2 * lane);
+      // swizzled 128-byte rows of the TMA tiles: dims 2*lane, 2*lane+1
+      const uint32_t rq = (uint32_t)t * 128 + ((((uint32_t)lane >> 2) ^ (t & 7)) << 4) + (lane & 3) * 4;
+      const float2 qv = tcb::load2<T>(sq + rq);
+      const float2 gv = tcb::load2<T>(sgo + rq);
       float part[8];
       float2 dsr[kTopK];
 #pragma unroll
@@ -360,11 +388,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         dw[j] = part[j] + (has_slot_grad ? dWs[ix[j]] : 0.f);
-        if (gw && first) dw[j] += gw[((size_t)bh * g.N + n) * kTopK + j];
+        if (gw && first) dw[j] += tgw[t * 8 + j];
         s = fmaf(w[j], dw[j], s);
       }
       float c[kTopK];
-      float2 dq = make_float2(0.f, 0.f);
+      float2 dq = prev;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         c[j] = g.scale * (w[j] * (dw[j] - s));
@@ -375,12 +403,6 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
           dq.x = fmaf(w[j], dsr[j].x, dq.x);
           dq.y = fmaf(w[j], dsr[j].y, dq.y);
         }
-      }
-      float2* acc = reinterpret_cast<float2*>(bs.dq + ((size_t)bh * g.N + n) * g.D) + lane;
-      if (!first) {
-        const float2 p = *acc;
-        dq.x += p.x;
-        dq.y += p.y;
       }
       if (r == 0) {
         T* gr = row_ptr(gq, gqs, b, h, n) + 2 * lane;
@@ -413,9 +435,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
           const int n = n0 + t;
           if (n >= t_end) break;
           if (lane < kTopK) {
-            const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
-            const int ml = sv.idx[trow * 8 + lane];
-            const float x = is_k ? coef[t * 8 + lane] : sv.w[trow * 8 + lane];
+            const int ml = tix[t * 8 + lane];
+            const float x = is_k ? coef[t * 8 + lane] : tw[t * 8 + lane];
             const uint16_t hb = tcb::bits<T>(x);
             *p_entry(t, ml) = lo ? tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb))) : hb;
           }
@@ -427,17 +448,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       tc_fence_after();
       if (*s_abort) { ok = false; break; }
       if (tid == 0) {
-        bool go_on = true;
-        if (qg_pending) {
-          go_on = tcb::timed_wait(bar_qg, ph_qg);
-          if (go_on) { ph_qg ^= 1; qg_pending = false; }
-          else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
-        }
-        if (go_on) {
-          tc_fence_after();
-          issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && (ph % kTerms) == 0);
-          mma_commit(bar_mma);
-        }
+        issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && (ph % kTerms) == 0);
+        mma_commit(bar_mma);
       }
       wait_mma();
     }
@@ -446,10 +458,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     for (int t = warp; t < kTile; t += 8) {
       const int n = n0 + t;
       if (n >= t_end) break;
-      if (lane < kTopK) {
-        const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
-        *p_entry(t, sv.idx[trow * 8 + lane]) = 0;
-      }
+      if (lane < kTopK) *p_entry(t, tix[t * 8 + lane]) = 0;
     }
     if (tid == 0 && tile + 1 < ntiles && !*s_abort) {
       mbar_arrive_expect_tx(bar_qg, 2 * 16384);
