@@ -6,10 +6,11 @@
 //      terms (K = K_1 + K_2 (+ K_3) + O(2^-22..2^-24 |K|): two fp16 terms, three
 //      bf16 terms), so the scores carry fp32-level precision; the N x M scores
 //      never leave the SM.
-//   2. top-7 per token, exact, ties to the lowest slot (thread = TMEM lane =
-//      token): a group-max pass bounds the 7th score from below, the few
-//      scores above the bound are compacted to shared memory and ranked
-//      exactly; rows where the bound is not finite take an exact full scan.
+//   2. top-7 per token, exact, ties to the lowest slot (two threads per token
+//      row, 128 slot columns each): the 7th largest of 32 group maxima (groups
+//      of 8 slots at stride 16) bounds the 7th score from below, the few scores
+//      above the bound are compacted to shared memory and ranked exactly; rows
+//      where the bound is not finite take an exact full scan.
 //   3. softmax over the 7 picks (reference.py:61-63) in fp32.
 //   4. the picks' weights w are written into a zeroed 128 x 256 tile P in shared
 //      memory as two 16-bit terms, first w_hi = rn(w) and then w_lo = rn(w - w_hi):
@@ -381,12 +382,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i) v[i] = (col0 + i < lim) ? v[i] : -INFINITY;
       }
+      // 16 groups of 8 slots at stride 16: diffusion makes neighbouring slots alike, so
+      // contiguous groups would cluster the top scores and weaken the bound below.
       float ga[8], gb[8], top8[8];
 #pragma unroll
       for (int gq = 0; gq < 16; ++gq) {
-        float x = v[8 * gq];
+        float x = v[gq];
 #pragma unroll
-        for (int i = 1; i < 8; ++i) x = fmaxf(x, v[8 * gq + i]);
+        for (int i = 1; i < 8; ++i) x = fmaxf(x, v[gq + 16 * i]);
         if (gq < 8) ga[gq] = x; else gb[gq - 8] = x;
       }
       tc::sort8_desc(ga);
