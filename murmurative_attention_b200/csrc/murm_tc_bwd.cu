@@ -34,7 +34,8 @@ extern __device__ int g_device_error;
 namespace tcb {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const int nt = min(kTile, t_end - n0);
       const size_t trow0 = ((size_t)r * g.BH + bh) * g.N + n0;
       if (tid < nt) reinterpret_cast<uint2*>(tix)[tid] = reinterpret_cast<const uint2*>(sv.idx)[trow0 + tid];
-      if ((tid >> 1) < nt) reinterpret_cast<float4*>(tw)[tid] = reinterpret_cast<const float4*>(sv.w + trow0 * 8)[tid];
+      if (tid < 2 * nt) reinterpret_cast<float4*>(tw)[tid] = reinterpret_cast<const float4*>(sv.w + trow0 * 8)[tid];
       if (gw && first) {
         const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
         for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
@@ -355,7 +356,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     // ---- token math: warp per token, 2 head dims per lane ----
     const uint8_t* sq = sm + tcb::OFF_Q;
     const uint8_t* sgo = sm + tcb::OFF_G;
-    for (int t = warp; t < kTile; t += 8) {
+    for (int t = warp; t < kTile; t += tcb::kWarps) {
       const int n = n0 + t;
       if (n >= t_end) break;
       float2* acc = reinterpret_cast<float2*>(bs.dq + ((size_t)bh * g.N + n) * g.D) + lane;
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const bool is_k = ph >= kTerms;   // dK phases use the coefficients, dV phases the weights
       const bool lo = (ph % kTerms) == 1;
       if (ph > 0) {  // rewrite this tile's P entries for the phase
-        for (int t = warp; t < kTile; t += 8) {
+        for (int t = warp; t < kTile; t += tcb::kWarps) {
           const int n = n0 + t;
           if (n >= t_end) break;
           if (lane < kTopK) {
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     }
     if (*s_abort) break;
     // clear P, fetch the next q/grad_out tiles
-    for (int t = warp; t < kTile; t += 8) {
+    for (int t = warp; t < kTile; t += tcb::kWarps) {
       const int n = n0 + t;
       if (n >= t_end) break;
       if (lane < kTopK) *p_entry(t, tix[t * 8 + lane]) = 0;
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   }
 
   // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
-  if (!__any_sync(0xffffffffu, *s_abort != 0)) {
+  if (warp < 8 && !__any_sync(0xffffffffu, *s_abort != 0)) {
     const int quad = warp & 3;
     const uint32_t lb = (uint32_t)(32 * quad) << 16;
     const bool is_k = warp >= 4;
