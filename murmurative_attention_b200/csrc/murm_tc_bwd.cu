@@ -84,6 +84,36 @@ __device__ __forceinline__ float2 load2(const void* p) {
   return make_float2(Elem<T>::load(t), Elem<T>::load(t + 1));
 }
 
+// 8 consecutive 16-bit values (16 bytes, aligned) -> 8 floats
+template <typename T>
+__device__ __forceinline__ void load8(const void* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = Elem<T>::load(t + i);
+}
+
+// Within each group of 8 lanes, sum each of v[0..7] over the group; on return
+// every lane of the group holds all 8 sums.
+__device__ __forceinline__ void group8_sum8(float (&v)[8]) {
+  const int c = threadIdx.x & 7;
+#pragma unroll
+  for (int s = 4, n = 4; s >= 1; s >>= 1, n >>= 1) {
+    const bool upper = (c & s) != 0;
+#pragma unroll
+    for (int k = 0; k < n; ++k) {
+      const float send = upper ? v[k] : v[k + n];
+      const float keep = upper ? v[k + n] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  // lane c of the group now holds the total of value index c
+  const float x = v[0];
+  const int base = threadIdx.x & 24;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, x, base + j);
+}
+
 // Sum each of v[0..7] over the 32 lanes; on return every lane holds all 8 sums.
 __device__ __forceinline__ void warp_sum8(float (&v)[8]) {
   const int lane = threadIdx.x & 31;
@@ -353,14 +383,18 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     }
     __syncthreads();
     if (*s_abort) break;
-    // ---- token math: warp per token, 2 head dims per lane ----
+    // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp ----
     const uint8_t* sq = sm + tcb::OFF_Q;
     const uint8_t* sgo = sm + tcb::OFF_G;
-    for (int t = warp; t < kTile; t += tcb::kWarps) {
+    const int grp = lane >> 3, c8 = lane & 7;
+    for (int t0 = 4 * warp; t0 < kTile; t0 += 4 * tcb::kWarps) {
+      const int t = t0 + grp;
       const int n = n0 + t;
-      if (n >= t_end) break;
-      float2* acc = reinterpret_cast<float2*>(bs.dq + ((size_t)bh * g.N + n) * g.D) + lane;
-      const float2 prev = first ? make_float2(0.f, 0.f) : *acc;  // issued early, used at the end
+      if (n0 + t0 >= t_end) break;        // warp-uniform
+      const bool live = n < t_end;          // group-uniform
+      float4* acc = reinterpret_cast<float4*>(bs.dq + ((size_t)bh * g.N + (live ? n : n0)) * g.D + 8 * c8);
+      float4 prev0 = make_float4(0.f, 0.f, 0.f, 0.f), prev1 = prev0;
+      if (!first && live) { prev0 = acc[0]; prev1 = acc[1]; }  // issued early, used at the end
       const uint2 pk = reinterpret_cast<const uint2*>(tix)[t];
       int ix[kTopK];
 #pragma unroll
@@ -370,21 +404,29 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const float4 w0 = reinterpret_cast<const float4*>(tw + t * 8)[0];
       const float4 w1 = reinterpret_cast<const float4*>(tw + t * 8)[1];
       const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
-      // swizzled 128-byte rows of the TMA tiles: dims 2*lane, 2*lane+1
-      const uint32_t rq = (uint32_t)t * 128 + ((((uint32_t)lane >> 2) ^ (t & 7)) << 4) + (lane & 3) * 4;
-      const float2 qv = tcb::load2<T>(sq + rq);
-      const float2 gv = tcb::load2<T>(sgo + rq);
+      // swizzled 128-byte rows of the TMA tiles: 16-byte chunk c8 of row t
+      const uint32_t rq = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
+      float qv[8], gv[8];
+      tcb::load8<T>(sq + rq, qv);
+      tcb::load8<T>(sgo + rq, gv);
       float part[8];
-      float2 dsr[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        const float2 vv = tcb::load2<T>(tV + ix[j] * 128 + 4 * lane);
-        dsr[j] = tcb::load2<T>(tS + ix[j] * 128 + 4 * lane);
-        part[j] = fmaf(gv.x, vv.x, gv.y * vv.y);
-        if (has_slot_grad) part[j] = fmaf(qv.x, dsr[j].x, fmaf(qv.y, dsr[j].y, part[j]));
+        float vv[8];
+        tcb::load8<T>(tV + ix[j] * 128 + 16 * c8, vv);
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = fmaf(gv[i], vv[i], a);
+        if (has_slot_grad) {
+          float ds[8];
+          tcb::load8<T>(tS + ix[j] * 128 + 16 * c8, ds);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) a = fmaf(qv[i], ds[i], a);
+        }
+        part[j] = a;
       }
       part[7] = 0.f;
-      tcb::warp_sum8(part);
+      tcb::group8_sum8(part);
       float dw[kTopK], s = 0.f;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
@@ -393,33 +435,41 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         s = fmaf(w[j], dw[j], s);
       }
       float c[kTopK];
-      float2 dq = prev;
+      float dq[8] = {prev0.x, prev0.y, prev0.z, prev0.w, prev1.x, prev1.y, prev1.z, prev1.w};
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         c[j] = g.scale * (w[j] * (dw[j] - s));
-        const float2 kv = tcb::load2<T>(tK + ix[j] * 128 + 4 * lane);
-        dq.x = fmaf(c[j], kv.x, dq.x);
-        dq.y = fmaf(c[j], kv.y, dq.y);
+        float kv[8];
+        tcb::load8<T>(tK + ix[j] * 128 + 16 * c8, kv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dq[i] = fmaf(c[j], kv[i], dq[i]);
         if (has_slot_grad) {
-          dq.x = fmaf(w[j], dsr[j].x, dq.x);
-          dq.y = fmaf(w[j], dsr[j].y, dq.y);
+          float ds[8];
+          tcb::load8<T>(tS + ix[j] * 128 + 16 * c8, ds);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dq[i] = fmaf(w[j], ds[i], dq[i]);
         }
       }
-      if (r == 0) {
-        T* gr = row_ptr(gq, gqs, b, h, n) + 2 * lane;
-        Elem<T>::store(gr, dq.x);
-        Elem<T>::store(gr + 1, dq.y);
-      } else {
-        *acc = dq;
-      }
-      if (lane < kTopK) {  // this token's row of P (first product: weights) and its coefficients
-        float wl = 0.f, cl = 0.f;
-        int ml = 0;
+      if (live) {
+        if (r == 0) {
+          uint4 o;
+          uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j)
-          if (lane == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
-        *p_entry(t, ml) = tcb::bits<T>(wl);
-        coef[t * 8 + lane] = cl;
+          for (int i = 0; i < 8; ++i) oh[i] = tcb::bits<T>(dq[i]);
+          *reinterpret_cast<uint4*>(row_ptr(gq, gqs, b, h, n) + 8 * c8) = o;
+        } else {
+          acc[0] = make_float4(dq[0], dq[1], dq[2], dq[3]);
+          acc[1] = make_float4(dq[4], dq[5], dq[6], dq[7]);
+        }
+        if (c8 < kTopK) {  // this token's row of P (first product: weights) and its coefficients
+          float wl = 0.f, cl = 0.f;
+          int ml = 0;
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j)
+            if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
+          *p_entry(t, ml) = tcb::bits<T>(wl);
+          coef[t * 8 + c8] = cl;
+        }
       }
     }
     // The scatters run as MMA phases over P: dV += P^T.G with P = w, then
@@ -536,8 +586,9 @@ bool tc_backward_supported(const Geom& g, int dtype, const BwdPtrs& p) {
   if (dtype != MURM_F16 && dtype != MURM_BF16) return false;
   if (g.D != tcb::kD || g.R < 1) return false;
   for (int i = 0; i < 3; ++i)
-    if ((p.qs.s[i] % 8) || (p.gos.s[i] % 8)) return false;
-  if ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.go)) & 15) return false;
+    if ((p.qs.s[i] % 8) || (p.gos.s[i] % 8) || (p.gqs.s[i] % 8)) return false;
+  if ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.go) | reinterpret_cast<uintptr_t>(p.gq)) & 15)
+    return false;
   const char* force = getenv("MURM_FORCE_SIMT");
   return !(force && force[0] == '1');
 }
