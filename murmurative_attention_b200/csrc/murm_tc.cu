@@ -161,45 +161,130 @@ struct Top7Ord {
 }  // namespace tc
 
 // ---------------------------------------------------------------------------
-// Operand images of one round, laid out exactly as the kernel's shared-memory
-// tiles (swizzled rows of 128 B): the key terms K_1..K_s and V in the dtype.
+// Slot-side kernels of the tensor-core path: warp per slot row (2 dims per
+// lane, coalesced), and they also write the next round's operand images.
 // ---------------------------------------------------------------------------
+namespace tc {
+// Write this lane's two columns of slot row m into the operand images.
 template <typename T>
-__global__ void __launch_bounds__(256) k_tc_images(Geom g, int r, Saved sv, uint8_t* images) {
-  constexpr int S = tc::Cfg<T>::kSplits;
-  const int bh = blockIdx.x;
-  const size_t st = ((size_t)r * g.BH + bh) * g.M * tc::kD;
+__device__ __forceinline__ void put_images(uint8_t* base, int m, int lane, float2 k, float2 v) {
+  const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)lane >> 2) ^ (m & 7)) << 4) + (lane & 3) * 4;
+#pragma unroll
+  for (int s = 0; s < Cfg<T>::kSplits; ++s) {
+    const uint16_t a = to_bits<T>(k.x), b = to_bits<T>(k.y);
+    *reinterpret_cast<uint32_t*>(base + s * kImg + off) = a | ((uint32_t)b << 16);
+    k.x -= from_bits<T>(a);  // exact in fp32: the next term carries the residual
+    k.y -= from_bits<T>(b);
+  }
+  *reinterpret_cast<uint32_t*>(base + Layout<T>::OFF_V + off) = to_bits<T>(v.x) | ((uint32_t)to_bits<T>(v.y) << 16);
+}
+}  // namespace tc
+
+// Round-0 state: slot tables (dtype, strided; batch stride 0 broadcasts) -> fp32 state + images.
+// grid (BH, 8): block y covers 32 slot rows (rows >= M write zero images).
+template <typename T>
+__global__ void __launch_bounds__(256) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv, Strides3 svs,
+                                                 Saved sv, uint8_t* images) {
+  const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
-  // thread -> (slot row, 8-column chunk): coalesced 16-byte stores
-  for (int e = blockIdx.y * blockDim.x + threadIdx.x; e < tc::kSlotsPad * 8; e += gridDim.y * blockDim.x) {
-    const int m = e >> 3, c8 = e & 7;
-    float k[8], v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { k[i] = 0.f; v[i] = 0.f; }
+  for (int m = blockIdx.y * 32 + warp; m < blockIdx.y * 32 + 32; m += 8) {
+    float2 k = make_float2(0.f, 0.f), v = k;
     if (m < g.M) {
-      const float4* kp = reinterpret_cast<const float4*>(sv.K + st + (size_t)m * tc::kD + 8 * c8);
-      const float4* vp = reinterpret_cast<const float4*>(sv.V + st + (size_t)m * tc::kD + 8 * c8);
-      const float4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
-      k[0] = k0.x; k[1] = k0.y; k[2] = k0.z; k[3] = k0.w; k[4] = k1.x; k[5] = k1.y; k[6] = k1.z; k[7] = k1.w;
-      v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w; v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+      const T* pk = row_ptr(sk, sks, b, h, m) + 2 * lane;
+      const T* pv = row_ptr(svv, svs, b, h, m) + 2 * lane;
+      k = make_float2(Elem<T>::load(pk), Elem<T>::load(pk + 1));
+      v = make_float2(Elem<T>::load(pv), Elem<T>::load(pv + 1));
+      const size_t e = (size_t)bh * g.M * tc::kD + (size_t)m * tc::kD + 2 * lane;
+      *reinterpret_cast<float2*>(sv.K + e) = k;
+      *reinterpret_cast<float2*>(sv.V + e) = v;
     }
-    const uint32_t off = sm100::sw128_offset(m, 8 * c8);  // 16-byte chunk start
+    tc::put_images<T>(base, m, lane, k, v);
+  }
+}
+
+// Finalize round r: combine the chunk partials in chunk order, EMA (reference.py:105-113)
+// and diffusion (reference.py:128-133) -> state entering round r+1, U_r, W_r and
+// the images of round r+1. grid (BH, 8), warp per slot row, halo rows recomputed.
+template <typename T>
+__global__ void __launch_bounds__(256) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
+  __shared__ float2 kn[34][32];
+  __shared__ float2 vn[34][32];
+  const int bh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * 32;
+  const size_t MD = (size_t)g.M * tc::kD;
+  const size_t cur = ((size_t)r * g.BH + bh) * MD;
+  for (int rr = warp; rr < 34; rr += 8) {
+    const int m = m0 - 1 + rr;
+    float2 k = make_float2(0.f, 0.f), v = k;
+    if (m >= 0 && m < g.M) {
+      float2 S = make_float2(0.f, 0.f);
+      float W = 0.f;
+      int ch = 0;
+      for (; ch + 4 <= g.red_chunks; ch += 4) {  // four loads in flight, added in chunk order
+        float2 a[4];
+        float wv[4];
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      uint4 pk;
-      uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
+        for (int u = 0; u < 4; ++u) {
+          const size_t po = (size_t)bh * g.red_chunks + ch + u;
+          a[u] = *reinterpret_cast<const float2*>(fs.Spart + (po * g.M + m) * tc::kD + 2 * lane);
+          wv[u] = fs.Wpart[po * g.M + m];
+        }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        ph[i] = tc::to_bits<T>(k[i]);
-        k[i] -= tc::from_bits<T>(ph[i]);  // exact in fp32: the next term carries the residual
+        for (int u = 0; u < 4; ++u) {
+          S.x = __fadd_rn(S.x, a[u].x);
+          S.y = __fadd_rn(S.y, a[u].y);
+          W = __fadd_rn(W, wv[u]);
+        }
       }
-      *reinterpret_cast<uint4*>(base + s * tc::kImg + off) = pk;
+      for (; ch < g.red_chunks; ++ch) {
+        const size_t po = (size_t)bh * g.red_chunks + ch;
+        const float2 a = *reinterpret_cast<const float2*>(fs.Spart + (po * g.M + m) * tc::kD + 2 * lane);
+        S.x = __fadd_rn(S.x, a.x);
+        S.y = __fadd_rn(S.y, a.y);
+        W = __fadd_rn(W, fs.Wpart[po * g.M + m]);
+      }
+      const bool hit = W > 0.f;
+      const float den = __fadd_rn(W, kEmaEps);
+      const float2 U = make_float2(__fdiv_rn(S.x, den), __fdiv_rn(S.y, den));
+      const size_t e = cur + (size_t)m * tc::kD + 2 * lane;
+      k = *reinterpret_cast<const float2*>(sv.K + e);
+      v = *reinterpret_cast<const float2*>(sv.V + e);
+      if (rr >= 1 && rr <= 32) {  // this block's rows record U and W
+        *reinterpret_cast<float2*>(sv.U + e) = U;
+        if (lane == 0) sv.W[((size_t)r * g.BH + bh) * g.M + m] = W;
+      }
+      if (hit) {
+        const float dx = __fmul_rn(g.one_minus_alpha, U.x), dy = __fmul_rn(g.one_minus_alpha, U.y);
+        k = make_float2(__fadd_rn(__fmul_rn(g.alpha, k.x), dx), __fadd_rn(__fmul_rn(g.alpha, k.y), dy));
+        v = make_float2(__fadd_rn(__fmul_rn(g.alpha, v.x), dx), __fadd_rn(__fmul_rn(g.alpha, v.y), dy));
+      }
     }
-    uint4 pv;
-    uint16_t* pvh = reinterpret_cast<uint16_t*>(&pv);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) pvh[i] = tc::to_bits<T>(v[i]);
-    *reinterpret_cast<uint4*>(base + tc::Layout<T>::OFF_V + off) = pv;
+    kn[rr][lane] = k;
+    vn[rr][lane] = v;
+  }
+  __syncthreads();
+  uint8_t* base = fs.images + (size_t)bh * tc::Layout<T>::kImages;
+  const size_t nxt = ((size_t)(r + 1) * g.BH + bh) * MD;
+  for (int rr = 1 + warp; rr < 33; rr += 8) {
+    const int m = m0 - 1 + rr;
+    float2 k = make_float2(0.f, 0.f), v = k;
+    if (m < g.M) {
+      k = kn[rr][lane];
+      v = vn[rr][lane];
+      if (m > 0 && m < g.M - 1) {
+        const float2 kl = kn[rr - 1][lane], kr = kn[rr + 1][lane], vl = vn[rr - 1][lane], vr = vn[rr + 1][lane];
+        const float2 tk = make_float2(__fsub_rn(__fadd_rn(kl.x, kr.x), __fmul_rn(2.f, k.x)),
+                                      __fsub_rn(__fadd_rn(kl.y, kr.y), __fmul_rn(2.f, k.y)));
+        const float2 tv = make_float2(__fsub_rn(__fadd_rn(vl.x, vr.x), __fmul_rn(2.f, v.x)),
+                                      __fsub_rn(__fadd_rn(vl.y, vr.y), __fmul_rn(2.f, v.y)));
+        k = make_float2(__fadd_rn(k.x, __fmul_rn(g.gamma, tk.x)), __fadd_rn(k.y, __fmul_rn(g.gamma, tk.y)));
+        v = make_float2(__fadd_rn(v.x, __fmul_rn(g.gamma, tv.x)), __fadd_rn(v.y, __fmul_rn(g.gamma, tv.y)));
+      }
+      const size_t e = nxt + (size_t)m * tc::kD + 2 * lane;
+      *reinterpret_cast<float2*>(sv.K + e) = k;
+      *reinterpret_cast<float2*>(sv.V + e) = v;
+    }
+    tc::put_images<T>(base, m, lane, k, v);  // rows >= M: zero
   }
 }
 
@@ -730,12 +815,12 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
     cudaFuncSetAttribute(k_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Layout<T>::kSmem);
     attr = true;
   }
-  launch_load_slots<T>(g, p, sv, st);
+  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, 8), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
+              static_cast<const T*>(p.sv), p.svs, sv, images);
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH("tc_images", k_tc_images<T>, dim3(g.BH, 8), 256, 0, st, g, r, sv, images);
     MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
-    if (r + 1 < g.R) launch_update_finalize(g, r, sv, fs, st);
+    if (r + 1 < g.R) MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, 8), 256, 0, st, g, r, sv, fs);
   }
   return cudaGetLastError();
 }

@@ -171,7 +171,19 @@ __global__ void __launch_bounds__(256) k_bwd_slots(Geom g, int r, int has_dir, i
         v = *reinterpret_cast<const float2*>(dir_v + e);
       }
       if (has_part) {
-        for (int ch = 0; ch < g.red_chunks; ++ch) {
+        int ch = 0;
+        for (; ch + 4 <= g.red_chunks; ch += 4) {  // four loads in flight, added in chunk order
+          float2 a[4], c[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const size_t po = ((size_t)bh * g.red_chunks + ch + u) * MD + (size_t)m * g.D + 2 * lane;
+            a[u] = *reinterpret_cast<const float2*>(bs.dKpart + po);
+            c[u] = *reinterpret_cast<const float2*>(bs.dVpart + po);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) { k.x += a[u].x; k.y += a[u].y; v.x += c[u].x; v.y += c[u].y; }
+        }
+        for (; ch < g.red_chunks; ++ch) {
           const size_t po = ((size_t)bh * g.red_chunks + ch) * MD + (size_t)m * g.D + 2 * lane;
           const float2 a = *reinterpret_cast<const float2*>(bs.dKpart + po);
           const float2 c = *reinterpret_cast<const float2*>(bs.dVpart + po);
