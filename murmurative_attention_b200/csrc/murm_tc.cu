@@ -42,7 +42,6 @@ constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
 constexpr int kThreads = 256;    // 2 warps per TMEM lane quadrant
 constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
-constexpr int kCand = 16;        // candidate list per row (16 never exceeded in 2e5 random rows)
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: scores | slot sums S (2 halves) | weight sums W (2 halves) | exchange | attend output O
@@ -73,9 +72,8 @@ template <typename T> struct Layout {
   static constexpr uint32_t OFF_P = OFF_V + kImg;
   static constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;
   static constexpr uint32_t OFF_ONES = OFF_Q + Cfg<T>::kQBufs * kQBytes;
-  static constexpr uint32_t OFF_CAND = OFF_ONES + 512;
-  static constexpr uint32_t OFF_CNT = OFF_CAND + kTile * kCand * 8;
-  static constexpr uint32_t OFF_MISC = OFF_CNT + 2 * kTile * 4;
+  static constexpr uint32_t OFF_XCH = OFF_ONES + 512;  // [7][kThreads] packed ranks: per-thread top-7 lists
+  static constexpr uint32_t OFF_MISC = OFF_XCH + kTopK * kThreads * 8;
   static constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
 };
@@ -131,32 +129,60 @@ __device__ __forceinline__ void merge8_desc(const float* A, const float* B, floa
       }
 }
 
-// Top-7 under the total order (score key descending, slot ascending): the
-// result does not depend on the order in which candidates are offered.
-struct Top7Ord {
-  uint32_t k[kTopK];
-  int i[kTopK];
-  __device__ __forceinline__ void init() {
+// A rank packs (score key, slot) into 64 bits so that larger means earlier in
+// the order "score descending, lower slot first on ties": key in the high
+// word, the complement of the slot in the low word. Rank 0 is below every
+// real entry.
+__device__ __forceinline__ uint64_t pack_rank(uint32_t key, int slot) {
+  return ((uint64_t)key << 32) | (uint32_t)~slot;
+}
+__device__ __forceinline__ int rank_slot(uint64_t r) { return (int)~(uint32_t)r; }
+__device__ __forceinline__ uint32_t rank_score_key(uint64_t r) { return (uint32_t)(r >> 32); }
+__device__ __forceinline__ uint64_t max64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+__device__ __forceinline__ uint64_t min64(uint64_t a, uint64_t b) { return a > b ? b : a; }
+
+// Insert (key xk, slot xs) into a list of 7 kept in rank order (branch-free).
+// Offers must come in ascending slot order: then an equal key never displaces
+// an earlier entry, and comparing keys alone gives the exact rank order.
+__device__ __forceinline__ void offer7_asc(uint32_t (&k)[kTopK], int (&sl)[kTopK], uint32_t xk, int xs) {
+  bool gt[kTopK];
 #pragma unroll
-    for (int j = 0; j < kTopK; ++j) { k[j] = 0u; i[j] = 0x7FFFFFFF; }
-  }
-  static __device__ __forceinline__ bool better(uint32_t ka, int ia, uint32_t kb, int ib) {
-    return ka > kb || (ka == kb && ia < ib);
-  }
-  __device__ __forceinline__ void offer(uint32_t key, int idx) {
-    if (!better(key, idx, k[kTopK - 1], i[kTopK - 1])) return;
-    bool done = false;
+  for (int j = 0; j < kTopK; ++j) gt[j] = xk > k[j];
 #pragma unroll
-    for (int j = kTopK - 1; j > 0; --j) {
-      const bool shift = !done && better(key, idx, k[j - 1], i[j - 1]);
-      const bool place = !done && !shift;
-      k[j] = shift ? k[j - 1] : (place ? key : k[j]);
-      i[j] = shift ? i[j - 1] : (place ? idx : i[j]);
-      done = done || place;
-    }
-    if (!done) { k[0] = key; i[0] = idx; }
+  for (int j = kTopK - 1; j >= 1; --j) {
+    k[j] = gt[j - 1] ? k[j - 1] : (gt[j] ? xk : k[j]);
+    sl[j] = gt[j - 1] ? sl[j - 1] : (gt[j] ? xs : sl[j]);
   }
-};
+  k[0] = gt[0] ? xk : k[0];
+  sl[0] = gt[0] ? xs : sl[0];
+}
+// Best 8 (descending) of two descending lists of 8 ranks: bitonic merge.
+__device__ __forceinline__ void merge8_rank(const uint64_t (&A)[8], const uint64_t (&B)[8], uint64_t (&c)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = max64(A[i], B[7 - i]);
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((i & s) == 0) {
+        const uint64_t x = c[i], y = c[i + s];
+        c[i] = max64(x, y);
+        c[i + s] = min64(x, y);
+      }
+}
+// x[b] for a run-time b in [0, 32) over 32 values held in registers (select tree).
+__device__ __forceinline__ float pick32(const float* x, int b) {
+  float t[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) t[j] = (b & 1) ? x[2 * j + 1] : x[2 * j];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) t[j] = (b & 2) ? t[2 * j + 1] : t[2 * j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) t[j] = (b & 4) ? t[2 * j + 1] : t[2 * j];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) t[j] = (b & 8) ? t[2 * j + 1] : t[2 * j];
+  return (b & 16) ? t[1] : t[0];
+}
 
 }  // namespace tc
 
@@ -312,14 +338,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint64_t* bar_b = bar_img + 5;  // MMA_B done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 64);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 68);
-  int* row_cnt2 = reinterpret_cast<int*>(sm + L::OFF_CNT);  // [2][128], by tile parity
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int row = tid & (kTile - 1);  // token row within the tile == TMEM lane
   const int part = tid >> 7;          // which 128 of the 256 slot columns this thread scans
   const int quadrant = warp & 3;
-  // candidate e of row r at [e][r]: a warp's rows touch consecutive words (no bank conflicts)
-  float2* cand = reinterpret_cast<float2*>(sm + L::OFF_CAND) + row;
+  // entry j of thread t's top-8 list at [j][t]: a warp touches consecutive words (no bank conflicts)
+  uint64_t* xch = reinterpret_cast<uint64_t*>(sm + L::OFF_XCH);
   const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
   const int t_beg = chunk * g.red_chunk_tokens;
   const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
@@ -345,7 +370,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     for (int i = tid; i < 4 * 16384 / 16; i += tc::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint16_t* ones = reinterpret_cast<uint16_t*>(sm + L::OFF_ONES);
     ones[tid] = C::one();  // 256 x 16-bit
-    if (tid < 2 * kTile) row_cnt2[tid] = 0;
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tc::kTmemCols);
@@ -441,7 +465,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     const int n0 = t_beg + tile * kTile;
     const int n = n0 + row;
     const bool valid = n < t_end;
-    int* row_cnt = row_cnt2 + (tile & 1) * kTile;
 
     // ---- scores of this tile ----
     wait_bar(bar_s, ph_s);
@@ -487,8 +510,18 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tc::quadrant_sync(quadrant);
     tc_fence_after();
 
-    // pass 2: threshold = 7th largest group maximum of the row; scores >= it are candidates
+    // pass 2: threshold = 7th largest group maximum of the row. The row's top 7 are among its
+    // scores >= it; each thread ranks its own (a handful) into a top-8 list straight from
+    // registers: bit masks per 32 columns, then one select-tree read per set bit.
     float thr = -INFINITY;
+    bool exact_scan = false;  // same for both threads of a row
+    uint32_t tkey[kTopK];     // this thread's best 7, in rank order (key 0 = empty)
+    int tslot[kTopK];
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      tkey[j] = 0u;
+      tslot[j] = 0;
+    }
     if (!aborting) {
       float lst[16];
       tmem_ld16(tmem + lane_base + tc::COL_X, lst);
@@ -496,57 +529,60 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       float all8[8];
       tc::merge8_desc(&lst[0], &lst[8], all8);
       thr = all8[kTopK - 1];
-      const bool bounded = thr > -INFINITY;
-      int cc[4];  // candidates per 32-column chunk (masked columns are -inf)
+      // rows with fewer than 7 finite group maxima (causal rows near the start) scan exactly
+      exact_scan = valid && !(thr > -INFINITY);
+      const bool scan = valid && !exact_scan;
+      uint32_t msk[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        int x = 0;
+        uint32_t a = 0, b2 = 0;  // two independent chains
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x += (bounded && v[32 * c + i] >= thr) ? 1 : 0;
-        cc[c] = x;
+        for (int i = 0; i < 16; ++i) {
+          a |= (v[32 * c + i] >= thr) ? (1u << i) : 0u;
+          b2 |= (v[32 * c + 16 + i] >= thr) ? (1u << (16 + i)) : 0u;
+        }
+        msk[c] = scan ? (a | b2) : 0u;
       }
-      const int cnt = cc[0] + cc[1] + cc[2] + cc[3];
-      if (cnt && valid) {
-        int k[4];
-        k[0] = atomicAdd(&row_cnt[row], cnt);  // order-free: Top7Ord
-        k[1] = k[0] + cc[0];
-        k[2] = k[1] + cc[1];
-        k[3] = k[2] + cc[2];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {  // four independent append chains
-            const bool hit = v[32 * c + i] >= thr;
-            if (hit && k[c] < tc::kCand) cand[k[c] * kTile] = make_float2(v[32 * c + i], __int_as_float(col0 + 32 * c + i));
-            k[c] += hit ? 1 : 0;
-          }
+      for (int c = 0; c < 4; ++c) {
+        while (__any_sync(0xffffffffu, msk[c] != 0)) {
+          // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
+          const int bit = __ffs(msk[c]) - 1;
+          const uint32_t key = rank_key(tc::pick32(&v[32 * c], bit & 31));
+          tc::offer7_asc(tkey, tslot, msk[c] ? key : 0u, col0 + 32 * c + bit);
+          msk[c] &= msk[c] - 1;
         }
       }
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) xch[j * tc::kThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
     }
-    tc_fence_before();
     tc::quadrant_sync(quadrant);
-    tc_fence_after();
 
-    // pass 3 (both threads of a row, redundantly): exact top-7 and softmax
+    // pass 3 (both threads of a row, redundantly): merge the two lists, softmax
     int pick[kTopK];
     float wgt[kTopK];
     if (!aborting) {
-      const int total = row_cnt[row];
-      const bool exact_scan = valid && (!(thr > -INFINITY) || total > tc::kCand);
-      tc::Top7Ord top;
-      top.init();
+      if (!exact_scan) {
+        uint64_t other[8], mine[8], top[8];
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) {
+          other[j] = xch[j * tc::kThreads + (tid ^ kTile)];
+          mine[j] = tc::pack_rank(tkey[j], tslot[j]);
+        }
+        other[7] = mine[7] = 0;
+        tc::merge8_rank(mine, other, top);
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) {
+          tkey[j] = tc::rank_score_key(top[j]);
+          tslot[j] = tc::rank_slot(top[j]);
+        }
+      }
       // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
       float mraw[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
-      if (!exact_scan) {
-        for (int e = 0; e < total; ++e) {
-          const float2 cd = cand[e * kTile];
-          top.offer(rank_key(cd.x), __float_as_int(cd.y));
-        }
-      }
       if (__any_sync(0xffffffffu, exact_scan)) {
-        // exact full scan (rows with fewer than 7 finite group maxima, or many candidates)
+        // exact full scan of the row's 256 columns from TMEM
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float w32[32];
@@ -557,13 +593,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const int m = 32 * c + i;
               if (m < lim) {
-                top.offer(rank_key(w32[i]), m);
+                tc::offer7_asc(tkey, tslot, rank_key(w32[i]), m);
               } else if (m < g.M) {
                 if (m - lim < kTopK) {
 #pragma unroll
                   for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[i] : mraw[j];
                 }
-                top.offer(kNegInfKey, m);
+                tc::offer7_asc(tkey, tslot, kNegInfKey, m);
               }
             }
           }
@@ -572,9 +608,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        pick[j] = valid ? top.i[j] : 0;
+        pick[j] = valid ? tslot[j] : 0;
         // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
-        const uint32_t kk = top.k[j];
+        const uint32_t kk = tkey[j];
         float s = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
         if (pick[j] >= lim) {
 #pragma unroll
@@ -599,7 +635,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       b_pending = false;
     }
     if (!aborting && part == 0) {
-      row_cnt2[((tile + 1) & 1) * kTile + row] = 0;  // next tile's counter
 #pragma unroll
       for (int j = 0; j < kTopK; ++j)
         if (old_pick[j] >= 0) *p_entry(old_pick[j]) = 0;
