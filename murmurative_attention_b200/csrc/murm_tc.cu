@@ -54,11 +54,34 @@ enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
 __device__ __forceinline__ void quadrant_sync(int quadrant) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(32 * kParts) : "memory");
 }
+// Named barrier 5 over the whole CTA: warp 0 (the MMA issuer) waits, the others only arrive.
+constexpr int kBarIssue = 5;
+__device__ __forceinline__ void issue_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kBarIssue), "n"(kThreads) : "memory");
+}
+__device__ __forceinline__ void issue_arrive() {
+  asm volatile("bar.arrive %0, %1;" ::"n"(kBarIssue), "n"(kThreads) : "memory");
+}
+
+// Shared-memory matrix descriptor kept as two 32-bit words. The low word holds the
+// start address (>> 4, bits 0-13) and the leading offset; adding a byte offset >> 4
+// to it moves the start (shared addresses stay below 256 KB, so no carry leaves the
+// 14-bit field). One add per MMA instead of re-encoding the whole descriptor.
+struct SDesc {
+  uint32_t lo, hi;
+  __device__ __forceinline__ uint64_t at(uint32_t byte_off) const {
+    return ((uint64_t)hi << 32) | (uint32_t)(lo + (byte_off >> 4));
+  }
+};
+__device__ __forceinline__ SDesc sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  const uint64_t d = smem_desc(saddr, lbo, sbo, layout);
+  return SDesc{(uint32_t)d, (uint32_t)(d >> 32)};
+}
 
 template <typename T> struct Cfg;
 template <> struct Cfg<__half> {
   static constexpr uint32_t fmt = 0;
-  static constexpr int kSplits = 2, kQBufs = 2;
+  static constexpr int kSplits = 2, kQBufs = 3;
   static __device__ __forceinline__ uint16_t one() { return 0x3C00u; }
 };
 template <> struct Cfg<__nv_bfloat16> {
@@ -332,10 +355,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t s_base = smem_u32(sm);
   uint64_t* bar_img = reinterpret_cast<uint64_t*>(sm + L::OFF_MISC);
-  uint64_t* bar_q = bar_img + 1;  // [2]
-  uint64_t* bar_s = bar_img + 3;  // SELECT done
-  uint64_t* bar_a = bar_img + 4;  // MMA_A done
-  uint64_t* bar_b = bar_img + 5;  // MMA_B done
+  uint64_t* bar_q = bar_img + 1;  // [3], one per Q buffer
+  uint64_t* bar_s = bar_img + 4;  // SELECT done
+  uint64_t* bar_a = bar_img + 5;  // MMA_A done
+  uint64_t* bar_b = bar_img + 6;  // MMA_B done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 64);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 68);
 
@@ -357,8 +380,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // ---- set-up: barriers, zeroed P, ones, counters, TMEM ----
   if (tid == 0) {
     mbar_init(bar_img, 1);
-    mbar_init(&bar_q[0], 1);
-    mbar_init(&bar_q[1], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_q[i], 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_b, 1);
@@ -387,8 +409,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // mbarrier phases (every thread tracks them; waits never fall two phases behind)
   uint32_t ph_s = 0, ph_a = 0, ph_b = 0;
   // thread 0's bookkeeping of asynchronous copies
-  bool img_pending = false, q_pending[2] = {false, false};
-  uint32_t q_phase[2] = {0, 0};
+  bool img_pending = false, q_pending[3] = {false, false, false};
+  uint32_t q_phase[3] = {0, 0, 0};
 
   auto fail = [&](int code) {
     atomicOr(&g_device_error, code);
@@ -399,7 +421,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     else fail(tc::kErrMmaWait);
     tc_fence_after();
   };
-  auto q_slot = [&](int tile_idx) { return (C::kQBufs == 2) ? (tile_idx & 1) : 0; };
+  auto q_slot = [&](int tile_idx) { return tile_idx % C::kQBufs; };
   auto issue_q = [&](int tile_idx) {  // thread 0
     const int bs = q_slot(tile_idx);
     mbar_arrive_expect_tx(&bar_q[bs], tc::kQBytes);
@@ -416,27 +438,34 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     q_pending[bs] = false;
     return true;
   };
+  // operand descriptors (start addresses moved per MMA by SDesc::at)
+  const tc::SDesc d_qk = tc::sdesc(s_base + L::OFF_Q, 16, 1024, kSwizzle128B);      // Q, K-major (SELECT A)
+  const tc::SDesc d_qmn = tc::sdesc(s_base + L::OFF_Q, 16384, 1024, kSwizzle128B);  // Q, MN-major (update B)
+  const tc::SDesc d_key = tc::sdesc(s_base, 16, 1024, kSwizzle128B);                // key terms (SELECT B)
+  const tc::SDesc d_pk = tc::sdesc(a_p, 16, 1024, kSwizzle128B);                    // P, K-major (attend A)
+  const tc::SDesc d_pmn = tc::sdesc(a_p, 16384, 1024, kSwizzle128B);                // P, MN-major (update A)
+  const tc::SDesc d_v = tc::sdesc(a_v, 16384, 1024, kSwizzle128B);                  // V (attend B)
+  const uint64_t d_ones = smem_desc(a_ones, 256, 128, kSwizzleNone);
   auto issue_select = [&](int tile_idx) {  // thread 0
-    const uint32_t a_q = s_base + L::OFF_Q + q_slot(tile_idx) * tc::kQBytes;
+    const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
     tc_fence_after();
 #pragma unroll
     for (int s = 0; s < C::kSplits; ++s)
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        mma_f16(tmem + tc::COL_S, smem_desc(a_q + k * 32, 16, 1024, kSwizzle128B),
-                smem_desc(s_base + s * tc::kImg + k * 32, 16, 1024, kSwizzle128B), ID_SEL, (s | k) != 0);
+        mma_f16(tmem + tc::COL_S, d_qk.at(q_off + k * 32), d_key.at(s * tc::kImg + k * 32), ID_SEL, (s | k) != 0);
     mma_commit(bar_s);
   };
   auto issue_update = [&](int tile_idx, bool first) {  // thread 0: S += P^T.Q, W += P^T.1
-    const uint32_t a_q = s_base + L::OFF_Q + q_slot(tile_idx) * tc::kQBytes;
+    const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t a = smem_desc(a_p + 2 * hh * 16384 + kk * 2048, 16384, 1024, kSwizzle128B);
+        const uint64_t a = d_pmn.at(2 * hh * 16384 + kk * 2048);
         const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-        mma_f16(tmem + tc::COL_U + 64 * hh, a, smem_desc(a_q + kk * 2048, 16384, 1024, kSwizzle128B), ID_UPD, acc);
-        mma_f16(tmem + tc::COL_W + 16 * hh, a, smem_desc(a_ones, 256, 128, kSwizzleNone), ID_W, acc);
+        mma_f16(tmem + tc::COL_U + 64 * hh, a, d_qmn.at(q_off + kk * 2048), ID_UPD, acc);
+        mma_f16(tmem + tc::COL_W + 16 * hh, a, d_ones, ID_W, acc);
       }
     }
   };
@@ -450,7 +479,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
     img_pending = true;
     issue_q(0);
-    if (C::kQBufs == 2 && ntiles > 1) issue_q(1);
+    for (int i = 1; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
     if (!tc::timed_wait(bar_img, 0)) fail(tc::kErrImgWait);
     else img_pending = false;
     if (!*s_abort && wait_q(0)) issue_select(0);
@@ -468,12 +497,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 
     // ---- scores of this tile ----
     wait_bar(bar_s, ph_s);
-    if (tid == 0 && C::kQBufs == 2 && tile >= 1 && tile + 1 < ntiles && !*s_abort) {
-      // the next tile's Q buffer was read last by MMA_B(i-1), which follows SELECT(i)
-      wait_bar(bar_b, ph_b);
-      b_pending = false;
-      issue_q(tile + 1);
-    }
     const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
     const int lim = g.causal ? min(g.M, n + 1) : g.M;               // columns >= lim score -inf
     const int col0 = 128 * part;
@@ -511,7 +534,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tc_fence_after();
 
     // pass 2: threshold = 7th largest group maximum of the row. The row's top 7 are among its
-    // scores >= it; each thread ranks its own (a handful) into a top-8 list straight from
+    // scores >= it; each thread ranks its own (a handful) into a top-7 list straight from
     // registers: bit masks per 32 columns, then one select-tree read per set bit.
     float thr = -INFINITY;
     bool exact_scan = false;  // same for both threads of a row
@@ -633,6 +656,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     if (b_pending) {
       wait_bar(bar_b, ph_b);
       b_pending = false;
+      // buffer of tile i-1+kQBufs was read last by MMA_B(i-1)
+      if (tid == 0 && C::kQBufs > 1 && tile - 1 + C::kQBufs < ntiles && !*s_abort) issue_q(tile - 1 + C::kQBufs);
     }
     if (!aborting && part == 0) {
 #pragma unroll
@@ -645,19 +670,18 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       fence_proxy_async_smem();
     }
     tc_fence_before();
-    __syncthreads();
+    const int stop = __syncthreads_or(*s_abort != 0);  // one decision for all threads
     tc_fence_after();
-    if (*s_abort) break;
+    if (stop) break;
 
     // ---- MMA_A(i), then SELECT(i+1) ----
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < 16; ++kk)
-        mma_f16(tmem + tc::COL_O, smem_desc(a_p + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                smem_desc(a_v + kk * 2048, 16384, 1024, kSwizzle128B), ID_ATT, kk != 0);
+        mma_f16(tmem + tc::COL_O, d_pk.at((kk >> 2) * 16384 + (kk & 3) * 32), d_v.at(kk * 2048), ID_ATT, kk != 0);
       issue_update(tile, tile == 0);
       mma_commit(bar_a);
-      if (C::kQBufs == 2 && tile + 1 < ntiles && wait_q(tile + 1)) issue_select(tile + 1);
+      if (C::kQBufs > 1 && tile + 1 < ntiles && wait_q(tile + 1)) issue_select(tile + 1);
     }
     // round records, by the row's second thread (off the tensor-core path)
     if (!aborting && valid && part == 1) {
@@ -697,10 +721,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) old_pick[j] = valid ? pick[j] : -1;
     }
+    // only the issuing warp waits for the second weight term; the others go on to the output
     tc_fence_before();
-    __syncthreads();
+    if (warp == 0) tc::issue_sync(); else tc::issue_arrive();
     tc_fence_after();
-    if (*s_abort) break;
     // ---- MMA_B(i) ----
     if (tid == 0) {
       issue_update(tile, false);
@@ -763,7 +787,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // ---- wind down: wait (bounded) for copies / MMAs still in flight, free TMEM ----
   if (tid == 0) {
     if (img_pending) tc::timed_wait(bar_img, 0);
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 3; ++i)
       if (q_pending[i]) tc::timed_wait(&bar_q[i], q_phase[i]);
     if (*s_abort) {  // groups whose completion was not observed
       tc::timed_wait(bar_s, ph_s);
