@@ -373,46 +373,103 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     tc_fence_after();
   };
 
-  for (int tile = 0; tile < ntiles && !*s_abort; ++tile) {
+  // Scatter phases over P (128 tokens x 256 slots, one term per phase):
+  //   fp16: dV += P^T.G (P = w) during the token math, then dK += P^T.Q (P = scale*da);
+  //   bf16: weights and coefficients go in as two terms each (hi = rn(x), lo = rn(x - hi)),
+  //         since bf16 alone rounds them to 2^-9: dV_hi during the math, then dV_lo, dK_hi, dK_lo.
+  constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
+  auto hi_bits = [](float x) -> uint16_t { return tcb::bits<T>(x); };
+  auto lo_bits = [](float x) -> uint16_t {
+    const uint16_t hb = tcb::bits<T>(x);
+    return tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb)));
+  };
+  float* tw = reinterpret_cast<float*>(sm + tcb::OFF_TW);
+  float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
+  uint8_t* tix = sm + tcb::OFF_TIX;
+  // records of a tile, one token per thread (threads 0..127), fetched a tile ahead
+  uint2 rix = make_uint2(0u, 0u);
+  float4 rw0 = make_float4(0.f, 0.f, 0.f, 0.f), rw1 = rw0;
+  auto fetch_recs = [&](int tile_idx) {
+    const int nn0 = t_beg + tile_idx * kTile;
+    if (tid < min(kTile, t_end - nn0)) {
+      const size_t trow = ((size_t)r * g.BH + bh) * g.N + nn0 + tid;
+      rix = reinterpret_cast<const uint2*>(sv.idx)[trow];
+      rw0 = reinterpret_cast<const float4*>(sv.w + trow * 8)[0];
+      rw1 = reinterpret_cast<const float4*>(sv.w + trow * 8)[1];
+    }
+  };
+  auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
+  fetch_recs(0);
+  uint2 old_ix = make_uint2(0u, 0u);  // thread t's token row of P in the previous tile
+  bool old_live = false;
+
+  for (int tile = 0; tile < ntiles; ++tile) {
     const int n0 = t_beg + tile * kTile;
-    // ---- the tile's picks, weights (and last-round weight gradients) into shared memory ----
-    float* tw = reinterpret_cast<float*>(sm + tcb::OFF_TW);
-    float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
-    uint8_t* tix = sm + tcb::OFF_TIX;
-    {
-      const int nt = min(kTile, t_end - n0);
-      const size_t trow0 = ((size_t)r * g.BH + bh) * g.N + n0;
-      if (tid < nt) reinterpret_cast<uint2*>(tix)[tid] = reinterpret_cast<const uint2*>(sv.idx)[trow0 + tid];
-      if (tid < 2 * nt) reinterpret_cast<float4*>(tw)[tid] = reinterpret_cast<const float4*>(sv.w + trow0 * 8)[tid];
-      if (gw && first) {
-        const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
-        for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
+    const int nt = min(kTile, t_end - n0);
+    // ---- records into shared memory; P rows: clear the previous tile's entries, then w ----
+    if (tid < kTile) {
+      if (old_live) {
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(old_ix, j)) = 0;
       }
+      old_live = tid < nt;
+      if (old_live) {
+        reinterpret_cast<uint2*>(tix)[tid] = rix;
+        reinterpret_cast<float4*>(tw)[2 * tid] = rw0;
+        reinterpret_cast<float4*>(tw)[2 * tid + 1] = rw1;
+        const float wv[kTopK] = {rw0.x, rw0.y, rw0.z, rw0.w, rw1.x, rw1.y, rw1.z};
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(rix, j)) = hi_bits(wv[j]);
+        old_ix = rix;
+      }
+    }
+    if (gw && first) {
+      const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
+      for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
     }
     if (tid == 0 && qg_pending) {  // q / grad_out tiles (read below and by the MMAs)
       if (tcb::timed_wait(bar_qg, ph_qg)) { ph_qg ^= 1; qg_pending = false; }
       else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
     }
-    __syncthreads();
-    if (*s_abort) break;
-    // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp ----
+    fence_proxy_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(*s_abort != 0)) break;  // one decision for all threads
+    tc_fence_after();
+    if (tid == 0) {  // dV (first term) runs during the token math
+      issue_scatter(a_g, tcb::COL_DV, tile == 0);
+      mma_commit(bar_mma);
+    }
+    if (tile + 1 < ntiles) fetch_recs(tile + 1);
+
+    // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp, 2 passes ----
     const uint8_t* sq = sm + tcb::OFF_Q;
     const uint8_t* sgo = sm + tcb::OFF_G;
     const int grp = lane >> 3, c8 = lane & 7;
-    for (int t0 = 4 * warp; t0 < kTile; t0 += 4 * tcb::kWarps) {
+    constexpr int kPasses = kTile / (4 * tcb::kWarps);
+    static_assert(kPasses * 4 * tcb::kWarps == kTile, "token passes");
+    float4 prev[kPasses][2];  // dq of earlier rounds, fetched before the math
+#pragma unroll
+    for (int it = 0; it < kPasses; ++it) {
+      const int t = 4 * warp + it * 4 * tcb::kWarps + grp;
+      prev[it][0] = prev[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!first && t < nt) {
+        const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n0 + t) * g.D + 8 * c8);
+        prev[it][0] = acc[0];
+        prev[it][1] = acc[1];
+      }
+    }
+    bool p_free = false;  // has this thread seen the first scatter complete?
+#pragma unroll
+    for (int it = 0; it < kPasses; ++it) {
+      const int t0 = 4 * warp + it * 4 * tcb::kWarps;
+      if (t0 >= nt) break;                 // warp-uniform
       const int t = t0 + grp;
-      const int n = n0 + t;
-      if (n0 + t0 >= t_end) break;        // warp-uniform
-      const bool live = n < t_end;          // group-uniform
-      float4* acc = reinterpret_cast<float4*>(bs.dq + ((size_t)bh * g.N + (live ? n : n0)) * g.D + 8 * c8);
-      float4 prev0 = make_float4(0.f, 0.f, 0.f, 0.f), prev1 = prev0;
-      if (!first && live) { prev0 = acc[0]; prev1 = acc[1]; }  // issued early, used at the end
+      const bool live = t < nt;            // group-uniform
+      const int n = n0 + (live ? t : 0);
       const uint2 pk = reinterpret_cast<const uint2*>(tix)[t];
       int ix[kTopK];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) ix[j] = (pk.x >> (8 * j)) & 0xff;
-#pragma unroll
-      for (int j = 4; j < kTopK; ++j) ix[j] = (pk.y >> (8 * (j - 4))) & 0xff;
+      for (int j = 0; j < kTopK; ++j) ix[j] = pick_of(pk, j);
       const float4 w0 = reinterpret_cast<const float4*>(tw + t * 8)[0];
       const float4 w1 = reinterpret_cast<const float4*>(tw + t * 8)[1];
       const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
@@ -421,6 +478,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       float qv[8], gv[8];
       tcb::load8<T>(sq + rq, qv);
       tcb::load8<T>(sgo + rq, gv);
+      float dq[8] = {prev[it][0].x, prev[it][0].y, prev[it][0].z, prev[it][0].w,
+                     prev[it][1].x, prev[it][1].y, prev[it][1].z, prev[it][1].w};
       float part[8];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
@@ -429,11 +488,14 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         float a = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) a = fmaf(gv[i], vv[i], a);
-        if (has_slot_grad) {
+        if (has_slot_grad) {  // dS[i_j] enters both dw_j and dq
           float ds[8];
           tcb::load8<T>(tS + ix[j] * 128 + 16 * c8, ds);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) a = fmaf(qv[i], ds[i], a);
+          for (int i = 0; i < 8; ++i) {
+            a = fmaf(qv[i], ds[i], a);
+            dq[i] = fmaf(w[j], ds[i], dq[i]);
+          }
         }
         part[j] = a;
       }
@@ -447,7 +509,6 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         s = fmaf(w[j], dw[j], s);
       }
       float c[kTopK];
-      float dq[8] = {prev0.x, prev0.y, prev0.z, prev0.w, prev1.x, prev1.y, prev1.z, prev1.w};
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         c[j] = g.scale * (w[j] * (dw[j] - s));
@@ -455,12 +516,6 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         tcb::load8<T>(tK + ix[j] * 128 + 16 * c8, kv);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dq[i] = fmaf(c[j], kv[i], dq[i]);
-        if (has_slot_grad) {
-          float ds[8];
-          tcb::load8<T>(tS + ix[j] * 128 + 16 * c8, ds);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dq[i] = fmaf(w[j], ds[i], dq[i]);
-        }
       }
       if (live) {
         if (r == 0) {
@@ -470,69 +525,62 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
           for (int i = 0; i < 8; ++i) oh[i] = tcb::bits<T>(dq[i]);
           *reinterpret_cast<uint4*>(row_ptr(gq, gqs, b, h, n) + 8 * c8) = o;
         } else {
+          float4* acc = reinterpret_cast<float4*>(bs.dq + ((size_t)bh * g.N + n) * g.D + 8 * c8);
           acc[0] = make_float4(dq[0], dq[1], dq[2], dq[3]);
           acc[1] = make_float4(dq[4], dq[5], dq[6], dq[7]);
         }
-        if (c8 < kTopK) {  // this token's row of P (first product: weights) and its coefficients
-          float wl = 0.f, cl = 0.f;
-          int ml = 0;
+      }
+      // this token's P entries take the next phase's values once the first scatter is done
+      if (!p_free) {
+        wait_mma();
+        p_free = true;
+      }
+      if (live && c8 < kTopK) {
+        float wl = 0.f, cl = 0.f;
+        int ml = 0;
 #pragma unroll
-          for (int j = 0; j < kTopK; ++j)
-            if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
-          *p_entry(t, ml) = tcb::bits<T>(wl);
-          coef[t * 8 + c8] = cl;
-        }
+        for (int j = 0; j < kTopK; ++j)
+          if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
+        coef[t * 8 + c8] = cl;
+        *p_entry(t, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
       }
     }
-    // The scatters run as MMA phases over P: dV += P^T.G with P = w, then
-    // dK += P^T.Q with P = scale*da. For bf16 each weight goes in as two terms
-    // (hi = rn(x), lo = rn(x - hi)): bf16 alone would round them to 2^-9.
-    constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
-    bool ok = true;
+    if (!p_free) wait_mma();  // warps without tokens in this tile
+
+    // ---- remaining scatter phases: fp16 dK; bf16 dV_lo, dK_hi, dK_lo ----
+    bool stop = false;
 #pragma unroll 1
-    for (int ph = 0; ph < 2 * kTerms && ok; ++ph) {
-      const bool is_k = ph >= kTerms;   // dK phases use the coefficients, dV phases the weights
-      const bool lo = (ph % kTerms) == 1;
-      if (ph > 0) {  // rewrite this tile's P entries for the phase
-        for (int t = warp; t < kTile; t += tcb::kWarps) {
-          const int n = n0 + t;
-          if (n >= t_end) break;
-          if (lane < kTopK) {
-            const int ml = tix[t * 8 + lane];
-            const float x = is_k ? coef[t * 8 + lane] : tw[t * 8 + lane];
-            const uint16_t hb = tcb::bits<T>(x);
-            *p_entry(t, ml) = lo ? tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb))) : hb;
+    for (int ph = 1; ph < 2 * kTerms; ++ph) {
+      const bool is_k = ph >= kTerms;
+      if (ph >= 2) {  // bf16: rewrite P with the coefficient terms (thread per token)
+        if (tid < nt) {
+          const uint2 pk = reinterpret_cast<const uint2*>(tix)[tid];
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            const float x = coef[tid * 8 + j];
+            *p_entry(tid, pick_of(pk, j)) = (ph == 2) ? hi_bits(x) : lo_bits(x);
           }
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      __syncthreads();
+      stop = __syncthreads_or(*s_abort != 0);
       tc_fence_after();
-      if (*s_abort) { ok = false; break; }
+      if (stop) break;
       if (tid == 0) {
-        issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && (ph % kTerms) == 0);
+        issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
         mma_commit(bar_mma);
       }
       wait_mma();
     }
-    if (*s_abort) break;
-    // clear P, fetch the next q/grad_out tiles
-    for (int t = warp; t < kTile; t += tcb::kWarps) {
-      const int n = n0 + t;
-      if (n >= t_end) break;
-      if (lane < kTopK) *p_entry(t, tix[t * 8 + lane]) = 0;
-    }
+    if (stop) break;
+    // q / grad_out tiles are free: fetch the next ones
     if (tid == 0 && tile + 1 < ntiles && !*s_abort) {
       mbar_arrive_expect_tx(bar_qg, 2 * 16384);
       tma_load_4d(sm + tcb::OFF_Q, &qmap, 0, n0 + kTile, h, b, bar_qg);
       tma_load_4d(sm + tcb::OFF_G, &gmap, 0, n0 + kTile, h, b, bar_qg);
       qg_pending = true;
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
   }
 
   // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
