@@ -40,7 +40,9 @@ __device__ int g_device_error;  // set by a bounded wait that expired; read by m
 namespace tc {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kThreads = 256;    // 2 warps per TMEM lane quadrant
+constexpr int kRowThreads = 256;               // 2 warps per TMEM lane quadrant
+constexpr int kIssuerWarp = kRowThreads / 32;   // one more warp: its lane 0 issues MMAs and copies
+constexpr int kThreads = kRowThreads + 32;
 constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
@@ -54,13 +56,16 @@ enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
 __device__ __forceinline__ void quadrant_sync(int quadrant) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(32 * kParts) : "memory");
 }
-// Named barrier 5 over the whole CTA: warp 0 (the MMA issuer) waits, the others only arrive.
-constexpr int kBarIssue = 5;
-__device__ __forceinline__ void issue_sync() {
-  asm volatile("bar.sync %0, %1;" ::"n"(kBarIssue), "n"(kThreads) : "memory");
+// Named barriers over the whole CTA that the issuer warp waits on and the row
+// warps only arrive at: the tile's first (5) and second (6) weight terms are in P.
+constexpr int kBarPhi = 5, kBarPlo = 6;
+template <int kId>
+__device__ __forceinline__ void issuer_wait() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kThreads) : "memory");
 }
-__device__ __forceinline__ void issue_arrive() {
-  asm volatile("bar.arrive %0, %1;" ::"n"(kBarIssue), "n"(kThreads) : "memory");
+template <int kId>
+__device__ __forceinline__ void rows_arrive() {
+  asm volatile("bar.arrive %0, %1;" ::"n"(kId), "n"(kThreads) : "memory");
 }
 
 // Shared-memory matrix descriptor kept as two 32-bit words. The low word holds the
@@ -95,8 +100,8 @@ template <typename T> struct Layout {
   static constexpr uint32_t OFF_P = OFF_V + kImg;
   static constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;
   static constexpr uint32_t OFF_ONES = OFF_Q + Cfg<T>::kQBufs * kQBytes;
-  static constexpr uint32_t OFF_XCH = OFF_ONES + 512;  // [7][kThreads] packed ranks: per-thread top-7 lists
-  static constexpr uint32_t OFF_MISC = OFF_XCH + kTopK * kThreads * 8;
+  static constexpr uint32_t OFF_XCH = OFF_ONES + 512;  // [7][kRowThreads] packed ranks: per-thread top-7 lists
+  static constexpr uint32_t OFF_MISC = OFF_XCH + kTopK * kRowThreads * 8;
   static constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
 };
@@ -338,12 +343,14 @@ __global__ void __launch_bounds__(256) k_tc_finalize(Geom g, int r, Saved sv, Fw
 }
 
 // ---------------------------------------------------------------------------
-// The forward round kernel (256 threads: thread = (token row, half of the slots))
+// The forward round kernel: 8 row warps (thread = token row x half of the slots)
+// and one issuer warp whose lane 0 issues every MMA and copy, so the row warps
+// never stall behind the tensor-core queue.
 //
 // Tensor-core order per tile i:  MMA_A(i) = {O = P_hi.V, S += P_hi^T.Q, W += P_hi^T.1},
 // then SELECT(i+1) (scores of the next tile), then MMA_B(i) = {S += P_lo^T.Q,
-// W += P_lo^T.1}. SELECT(i+1) runs while the CUDA cores write the second
-// weight term and the output of tile i; MMA_B(i) runs while they rank tile i+1.
+// W += P_lo^T.1}. SELECT(i+1) runs while the row warps write the second weight
+// term and the output of tile i; MMA_B(i) runs while they rank tile i+1.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(tc::kThreads, 1)
@@ -362,11 +369,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 64);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 68);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool issuer_warp = warp == tc::kIssuerWarp;
   const int row = tid & (kTile - 1);  // token row within the tile == TMEM lane
-  const int part = tid >> 7;          // which 128 of the 256 slot columns this thread scans
+  const int part = (tid >> 7) & 1;    // which 128 of the 256 slot columns this thread scans
   const int quadrant = warp & 3;
-  // entry j of thread t's top-8 list at [j][t]: a warp touches consecutive words (no bank conflicts)
+  // entry j of thread t's top-7 list at [j][t]: a warp touches consecutive words (no bank conflicts)
   uint64_t* xch = reinterpret_cast<uint64_t*>(sm + L::OFF_XCH);
   const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
   const int t_beg = chunk * g.red_chunk_tokens;
@@ -377,7 +385,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   constexpr uint32_t ID_UPD = idesc_f16(C::fmt, 128, 64, 1, 1);
   constexpr uint32_t ID_W = idesc_f16(C::fmt, 128, 16, 1, 0);
 
-  // ---- set-up: barriers, zeroed P, ones, counters, TMEM ----
+  // ---- set-up: barriers, zeroed P, ones, TMEM ----
   if (tid == 0) {
     mbar_init(bar_img, 1);
     for (int i = 0; i < 3; ++i) mbar_init(&bar_q[i], 1);
@@ -391,7 +399,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     float4* p4 = reinterpret_cast<float4*>(sm + L::OFF_P);
     for (int i = tid; i < 4 * 16384 / 16; i += tc::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint16_t* ones = reinterpret_cast<uint16_t*>(sm + L::OFF_ONES);
-    ones[tid] = C::one();  // 256 x 16-bit
+    if (tid < 256) ones[tid] = C::one();  // 256 x 16-bit
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tc::kTmemCols);
@@ -406,9 +414,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
   const bool last_round = (r == g.R - 1);
 
-  // mbarrier phases (every thread tracks them; waits never fall two phases behind)
+  // mbarrier phases of the row threads (each waits every phase once)
   uint32_t ph_s = 0, ph_a = 0, ph_b = 0;
-  // thread 0's bookkeeping of asynchronous copies
+  // the issuer's bookkeeping of asynchronous copies
   bool img_pending = false, q_pending[3] = {false, false, false};
   uint32_t q_phase[3] = {0, 0, 0};
 
@@ -422,13 +430,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tc_fence_after();
   };
   auto q_slot = [&](int tile_idx) { return tile_idx % C::kQBufs; };
-  auto issue_q = [&](int tile_idx) {  // thread 0
+  auto issue_q = [&](int tile_idx) {  // issuer
     const int bs = q_slot(tile_idx);
     mbar_arrive_expect_tx(&bar_q[bs], tc::kQBytes);
     tma_load_4d(sm + L::OFF_Q + bs * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bs]);
     q_pending[bs] = true;
   };
-  auto wait_q = [&](int tile_idx) -> bool {  // thread 0
+  auto wait_q = [&](int tile_idx) -> bool {  // issuer
     const int bs = q_slot(tile_idx);
     if (!tc::timed_wait(&bar_q[bs], q_phase[bs])) {
       fail(tc::kErrQWait);
@@ -446,7 +454,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const tc::SDesc d_pmn = tc::sdesc(a_p, 16384, 1024, kSwizzle128B);                // P, MN-major (update A)
   const tc::SDesc d_v = tc::sdesc(a_v, 16384, 1024, kSwizzle128B);                  // V (attend B)
   const uint64_t d_ones = smem_desc(a_ones, 256, 128, kSwizzleNone);
-  auto issue_select = [&](int tile_idx) {  // thread 0
+  auto issue_select = [&](int tile_idx) {  // issuer
     const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
     tc_fence_after();
 #pragma unroll
@@ -456,7 +464,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         mma_f16(tmem + tc::COL_S, d_qk.at(q_off + k * 32), d_key.at(s * tc::kImg + k * 32), ID_SEL, (s | k) != 0);
     mma_commit(bar_s);
   };
-  auto issue_update = [&](int tile_idx, bool first) {  // thread 0: S += P^T.Q, W += P^T.1
+  auto issue_update = [&](int tile_idx, bool first) {  // issuer: S += P^T.Q, W += P^T.1
     const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -473,327 +481,395 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     return reinterpret_cast<uint16_t*>(sm + L::OFF_P + (m >> 6) * 16384 + sw128_offset(row, m & 63));
   };
 
-  // ---- prologue: operand images, first token tile(s), first SELECT ----
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_img, L::kImages);
-    bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
-    img_pending = true;
-    issue_q(0);
-    for (int i = 1; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
-    if (!tc::timed_wait(bar_img, 0)) fail(tc::kErrImgWait);
-    else img_pending = false;
-    if (!*s_abort && wait_q(0)) issue_select(0);
-  }
-
-  int old_pick[kTopK];  // this row's picks in the previous tile (their P entries are still set)
-#pragma unroll
-  for (int j = 0; j < kTopK; ++j) old_pick[j] = -1;
-  bool b_pending = false;  // an MMA_B whose completion this thread has not waited for
-
-  for (int tile = 0; tile < ntiles; ++tile) {
-    const int n0 = t_beg + tile * kTile;
-    const int n = n0 + row;
-    const bool valid = n < t_end;
-
-    // ---- scores of this tile ----
-    wait_bar(bar_s, ph_s);
-    const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
-    const int lim = g.causal ? min(g.M, n + 1) : g.M;               // columns >= lim score -inf
-    const int col0 = 128 * part;
-    const bool mask_warp = __any_sync(0xffffffffu, lim < col0 + 128);
-
-    // pass 1: this thread's 128 scores (kept in registers), 16 group maxima, top 8 published in TMEM
-    float v[128];
-    if (!aborting) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tmem + lane_base + tc::COL_S + col0 + 32 * c, *reinterpret_cast<float(*)[32]>(&v[32 * c]));
-      tmem_wait_ld();
-      if (mask_warp) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) v[i] = (col0 + i < lim) ? v[i] : -INFINITY;
+  // fp16 (three Q buffers) runs SELECT(i+1) ahead of MMA_A(i): the row warps rank tile i+1
+  // while MMA_A(i) runs, then finish tile i (second weight term, output). bf16 has one Q
+  // buffer, so SELECT(i+1) waits for MMA_B(i) and the row warps finish tile i first.
+  constexpr bool kEarlySelect = C::kQBufs >= 3;
+  if (issuer_warp) {
+    // ================= issuer warp =================
+    uint32_t n_s = 0, n_a = 0, n_b = 0;  // commits per barrier (for the wind-down)
+    if (lane == 0) {  // prologue: operand images, first token tiles, first SELECT
+      mbar_arrive_expect_tx(bar_img, L::kImages);
+      bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
+      img_pending = true;
+      for (int i = 0; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
+      if (!tc::timed_wait(bar_img, 0)) fail(tc::kErrImgWait);
+      else img_pending = false;
+      if (ntiles > 0 && !*s_abort && wait_q(0)) {
+        issue_select(0);
+        ++n_s;
       }
-      // 16 groups of 8 slots at stride 16: diffusion makes neighbouring slots alike, so
-      // contiguous groups would cluster the top scores and weaken the bound below.
-      float ga[8], gb[8], top8[8];
-#pragma unroll
-      for (int gq = 0; gq < 16; ++gq) {
-        float x = v[gq];
-#pragma unroll
-        for (int i = 1; i < 8; ++i) x = fmaxf(x, v[gq + 16 * i]);
-        if (gq < 8) ga[gq] = x; else gb[gq - 8] = x;
-      }
-      tc::sort8_desc(ga);
-      tc::sort8_desc(gb);
-      tc::merge8_desc(ga, gb, top8);
-      tmem_st8(tmem + lane_base + tc::COL_X + 8 * part, top8);
-      tmem_wait_st();
     }
-    tc_fence_before();
-    tc::quadrant_sync(quadrant);
-    tc_fence_after();
-
-    // pass 2: threshold = 7th largest group maximum of the row. The row's top 7 are among its
-    // scores >= it; each thread ranks its own (a handful) into a top-7 list straight from
-    // registers: bit masks per 32 columns, then one select-tree read per set bit.
-    float thr = -INFINITY;
-    bool exact_scan = false;  // same for both threads of a row
-    uint32_t tkey[kTopK];     // this thread's best 7, in rank order (key 0 = empty)
-    int tslot[kTopK];
-#pragma unroll
-    for (int j = 0; j < kTopK; ++j) {
-      tkey[j] = 0u;
-      tslot[j] = 0;
-    }
-    if (!aborting) {
-      float lst[16];
-      tmem_ld16(tmem + lane_base + tc::COL_X, lst);
-      tmem_wait_ld();
-      float all8[8];
-      tc::merge8_desc(&lst[0], &lst[8], all8);
-      thr = all8[kTopK - 1];
-      // rows with fewer than 7 finite group maxima (causal rows near the start) scan exactly
-      exact_scan = valid && !(thr > -INFINITY);
-      const bool scan = valid && !exact_scan;
-      uint32_t msk[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t a = 0, b2 = 0;  // two independent chains
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          a |= (v[32 * c + i] >= thr) ? (1u << i) : 0u;
-          b2 |= (v[32 * c + 16 + i] >= thr) ? (1u << (16 + i)) : 0u;
-        }
-        msk[c] = scan ? (a | b2) : 0u;
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        while (__any_sync(0xffffffffu, msk[c] != 0)) {
-          // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
-          const int bit = __ffs(msk[c]) - 1;
-          const uint32_t key = rank_key(tc::pick32(&v[32 * c], bit & 31));
-          tc::offer7_asc(tkey, tslot, msk[c] ? key : 0u, col0 + 32 * c + bit);
-          msk[c] &= msk[c] - 1;
+    __syncwarp();
+    uint32_t ph_b_own = 0;  // MMA_B phases this lane waits for itself (one Q buffer)
+    auto mma_b = [&](int tile_idx) {  // ---- MMA_B(tile_idx) ----
+      tc::issuer_wait<tc::kBarPlo>();
+      if (lane == 0 && !*s_abort) {
+        tc_fence_after();
+        issue_update(tile_idx, false);
+        mma_commit(bar_b);
+        ++n_b;
+        if (!kEarlySelect && tile_idx + 1 < ntiles) {  // one Q buffer: free once MMA_B is done
+          if (tc::timed_wait(bar_b, ph_b_own)) ph_b_own ^= 1; else fail(tc::kErrMmaWait);
+          tc_fence_after();
+          issue_q(tile_idx + 1);
+          if (wait_q(tile_idx + 1)) {
+            issue_select(tile_idx + 1);
+            ++n_s;
+          }
         }
       }
+      __syncwarp();
+    };
+    for (int tile = 0; tile < ntiles; ++tile) {
+      if (kEarlySelect && tile > 0) mma_b(tile - 1);
+      tc::issuer_wait<tc::kBarPhi>();
+      if (lane == 0 && !*s_abort) {
+        tc_fence_after();
+        if (kEarlySelect && tile + 1 < ntiles && wait_q(tile + 1)) {  // SELECT(i+1) first
+          issue_select(tile + 1);
+          ++n_s;
+        }
+        // ---- MMA_A(i) ----
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) xch[j * tc::kThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
+        for (int kk = 0; kk < 16; ++kk)
+          mma_f16(tmem + tc::COL_O, d_pk.at((kk >> 2) * 16384 + (kk & 3) * 32), d_v.at(kk * 2048), ID_ATT, kk != 0);
+        issue_update(tile, tile == 0);
+        mma_commit(bar_a);
+        ++n_a;
+        // the row warps saw MMA_B(i-1) complete before writing P: its Q buffer is free
+        if (C::kQBufs > 1 && tile >= 1 && tile - 1 + C::kQBufs < ntiles) issue_q(tile - 1 + C::kQBufs);
+      }
+      __syncwarp();
+      if (!kEarlySelect) mma_b(tile);
     }
-    tc::quadrant_sync(quadrant);
-
-    // pass 3 (both threads of a row, redundantly): merge the two lists, softmax
+    if (kEarlySelect && ntiles > 0) mma_b(ntiles - 1);
+    if (lane == 0) {  // every committed group completes before TMEM is freed (bounded waits)
+      if (n_s) tc::timed_wait(bar_s, (n_s - 1) & 1);
+      if (n_a) tc::timed_wait(bar_a, (n_a - 1) & 1);
+      if (n_b) tc::timed_wait(bar_b, (n_b - 1) & 1);
+    }
+  } else {
+    // ================= row warps =================
+    // A tile's state kept for its completion (second weight term, records, output)
     int pick[kTopK];
     float wgt[kTopK];
-    if (!aborting) {
-      if (!exact_scan) {
-        uint64_t other[8], mine[8], top[8];
+    bool done_valid = false;      // the tile being completed has a valid row here
+    int old_pick[kTopK];          // picks whose P entries are set
+    uint4 prev[4];                // this thread's 32 output columns from earlier rounds
+    T* orow = out;
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) {
-          other[j] = xch[j * tc::kThreads + (tid ^ kTile)];
-          mine[j] = tc::pack_rank(tkey[j], tslot[j]);
+    for (int j = 0; j < kTopK; ++j) {
+      old_pick[j] = -1;
+      pick[j] = 0;
+      wgt[j] = 0.f;
+    }
+    // wait on an mbarrier unless the kernel is already giving up
+    auto wait_live = [&](uint64_t* bar, uint32_t& ph) {
+      if (!*s_abort) wait_bar(bar, ph);
+    };
+    // second weight term and output of the tile whose P_hi MMA_A has consumed
+    auto complete = [&]() {
+      wait_live(bar_a, ph_a);
+      const bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
+      if (ok && part == 0) {
+        if (done_valid) {
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            const uint16_t hb = tc::to_bits<T>(wgt[j]);
+            *p_entry(pick[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
+          }
         }
-        other[7] = mine[7] = 0;
-        tc::merge8_rank(mine, other, top);
+        fence_proxy_async_smem();
+      }
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) {
-          tkey[j] = tc::rank_score_key(top[j]);
-          tslot[j] = tc::rank_slot(top[j]);
+      for (int j = 0; j < kTopK; ++j) old_pick[j] = done_valid ? pick[j] : -1;
+      tc_fence_before();
+      tc::rows_arrive<tc::kBarPlo>();  // MMA_B may start
+      // ---- output: out (+)= O, 32 columns per thread ----
+      if (ok) {
+        float o[32];
+        tmem_ld32(tmem + lane_base + tc::COL_O + 32 * part, o);
+        tmem_wait_ld();
+        if (done_valid) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 pk;
+            uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
+            const T* pv = reinterpret_cast<const T*>(&prev[i]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>((r ? Elem<T>::load(pv + e) : 0.f) + o[8 * i + e]);
+            reinterpret_cast<uint4*>(orow)[i] = pk;
+          }
         }
       }
-      // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
-      float mraw[kTopK];
+      tc_fence_before();  // the output's TMEM reads come before the next MMA_A
+    };
+
+    for (int tile = 0; tile < ntiles; ++tile) {
+      const int n0 = t_beg + tile * kTile;
+      const int n = n0 + row;
+      const bool valid = n < t_end;
+
+      // ---- scores of this tile ----
+      wait_live(bar_s, ph_s);
+      const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
+      const int lim = g.causal ? min(g.M, n + 1) : g.M;               // columns >= lim score -inf
+      const int col0 = 128 * part;
+      const bool mask_warp = __any_sync(0xffffffffu, lim < col0 + 128);
+
+      // pass 1: 16 group maxima of this thread's 128 scores, top 8 published in TMEM.
+      // Groups of 8 slots at stride 16: diffusion makes neighbouring slots alike, so
+      // contiguous groups would cluster the top scores and weaken the bound below.
+      auto load2 = [&](int c, float (&x0)[32], float (&x1)[32]) {  // chunks c, c+1 of this thread's half, masked
+        tmem_ld32(tmem + lane_base + tc::COL_S + col0 + 32 * c, x0);
+        tmem_ld32(tmem + lane_base + tc::COL_S + col0 + 32 * c + 32, x1);
+        tmem_wait_ld();
+        if (mask_warp) {
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
-      if (__any_sync(0xffffffffu, exact_scan)) {
-        // exact full scan of the row's 256 columns from TMEM
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          float w32[32];
-          tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, w32);
-          tmem_wait_ld();
-          if (exact_scan) {  // rare path: kept compact (not unrolled)
-#pragma unroll 1
-            for (int i = 0; i < 32; ++i) {
-              const int m = 32 * c + i;
-              if (m < lim) {
-                tc::offer7_asc(tkey, tslot, rank_key(w32[i]), m);
-              } else if (m < g.M) {
-                if (m - lim < kTopK) {
+          for (int i = 0; i < 32; ++i) {
+            x0[i] = (col0 + 32 * c + i < lim) ? x0[i] : -INFINITY;
+            x1[i] = (col0 + 32 * c + 32 + i < lim) ? x1[i] : -INFINITY;
+          }
+        }
+      };
+      if (!aborting) {
+        float gm[16];
 #pragma unroll
-                  for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[i] : mraw[j];
+        for (int c = 0; c < 4; c += 2) {
+          float x0[32], x1[32];
+          load2(c, x0, x1);
+#pragma unroll
+          for (int gq = 0; gq < 16; ++gq) {
+            const float y = fmaxf(fmaxf(x0[gq], x0[gq + 16]), fmaxf(x1[gq], x1[gq + 16]));
+            gm[gq] = c ? fmaxf(gm[gq], y) : y;
+          }
+        }
+        float ga[8], gb[8], top8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ga[j] = gm[j];
+          gb[j] = gm[8 + j];
+        }
+        tc::sort8_desc(ga);
+        tc::sort8_desc(gb);
+        tc::merge8_desc(ga, gb, top8);
+        tmem_st8(tmem + lane_base + tc::COL_X + 8 * part, top8);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      tc::quadrant_sync(quadrant);
+      tc_fence_after();
+
+      // pass 2: threshold = 7th largest group maximum of the row. The row's top 7 are among its
+      // scores >= it; each thread ranks its own (a handful) into a top-7 list: the scores come
+      // back from TMEM 64 at a time, bit masks per 32 columns, one select-tree read per set bit.
+      float thr = -INFINITY;
+      bool exact_scan = false;  // same for both threads of a row
+      uint32_t tkey[kTopK];     // this thread's best 7, in rank order (key 0 = empty)
+      int tslot[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        tkey[j] = 0u;
+        tslot[j] = 0;
+      }
+      if (!aborting) {
+        float lst[16];
+        tmem_ld16(tmem + lane_base + tc::COL_X, lst);
+        tmem_wait_ld();
+        float all8[8];
+        tc::merge8_desc(&lst[0], &lst[8], all8);
+        thr = all8[kTopK - 1];
+        // rows with fewer than 7 finite group maxima (causal rows near the start) scan exactly
+        exact_scan = valid && !(thr > -INFINITY);
+        const bool scan = valid && !exact_scan;
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+          float x[2][32];
+          load2(c, x[0], x[1]);
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            uint32_t a = 0, b2 = 0;  // two independent chains
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              a |= (x[k][i] >= thr) ? (1u << i) : 0u;
+              b2 |= (x[k][16 + i] >= thr) ? (1u << (16 + i)) : 0u;
+            }
+            uint32_t msk = scan ? (a | b2) : 0u;
+            while (__any_sync(0xffffffffu, msk != 0)) {
+              // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
+              const int bit = __ffs(msk) - 1;
+              const uint32_t key = rank_key(tc::pick32(x[k], bit & 31));
+              tc::offer7_asc(tkey, tslot, msk ? key : 0u, col0 + 32 * (c + k) + bit);
+              msk &= msk - 1;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) xch[j * tc::kRowThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
+      }
+      tc::quadrant_sync(quadrant);
+
+      // the previous tile: second weight term and output, while this tile's scores wait in TMEM
+      if (kEarlySelect && tile > 0) complete();
+
+      // pass 3 (both threads of a row, redundantly): merge the two lists, softmax
+      int npick[kTopK];
+      float nwgt[kTopK];
+      if (!aborting) {
+        if (!exact_scan) {
+          uint64_t other[8], mine[8], top[8];
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            other[j] = xch[j * tc::kRowThreads + (tid ^ kTile)];
+            mine[j] = tc::pack_rank(tkey[j], tslot[j]);
+          }
+          other[7] = mine[7] = 0;
+          tc::merge8_rank(mine, other, top);
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            tkey[j] = tc::rank_score_key(top[j]);
+            tslot[j] = tc::rank_slot(top[j]);
+          }
+        }
+        // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
+        float mraw[kTopK];
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
+        if (__any_sync(0xffffffffu, exact_scan)) {
+          // exact full scan of the row's 256 columns from TMEM
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            float w32[32];
+            tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, w32);
+            tmem_wait_ld();
+            if (exact_scan) {  // rare path: kept compact (not unrolled)
+#pragma unroll 1
+              for (int i = 0; i < 32; ++i) {
+                const int m = 32 * c + i;
+                if (m < lim) {
+                  tc::offer7_asc(tkey, tslot, rank_key(w32[i]), m);
+                } else if (m < g.M) {
+                  if (m - lim < kTopK) {
+#pragma unroll
+                    for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[i] : mraw[j];
+                  }
+                  tc::offer7_asc(tkey, tslot, kNegInfKey, m);
                 }
-                tc::offer7_asc(tkey, tslot, kNegInfKey, m);
               }
             }
           }
         }
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        pick[j] = valid ? tslot[j] : 0;
-        // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
-        const uint32_t kk = tkey[j];
-        float s = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
-        if (pick[j] >= lim) {
-#pragma unroll
-          for (int k2 = 0; k2 < kTopK; ++k2) s = (pick[j] == lim + k2) ? mraw[k2] : s;
-        }
-        wgt[j] = s * g.scale;
-        mx = fmaxf(mx, wgt[j]);
-      }
-      float sum = 0.f;
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        wgt[j] = expf(wgt[j] - mx);
-        sum += wgt[j];
-      }
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) wgt[j] = wgt[j] / sum;
-    }
-
-    // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
-    if (b_pending) {
-      wait_bar(bar_b, ph_b);
-      b_pending = false;
-      // buffer of tile i-1+kQBufs was read last by MMA_B(i-1)
-      if (tid == 0 && C::kQBufs > 1 && tile - 1 + C::kQBufs < ntiles && !*s_abort) issue_q(tile - 1 + C::kQBufs);
-    }
-    if (!aborting && part == 0) {
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j)
-        if (old_pick[j] >= 0) *p_entry(old_pick[j]) = 0;
-      if (valid) {
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) *p_entry(pick[j]) = tc::to_bits<T>(wgt[j]);
-      }
-      fence_proxy_async_smem();
-    }
-    tc_fence_before();
-    const int stop = __syncthreads_or(*s_abort != 0);  // one decision for all threads
-    tc_fence_after();
-    if (stop) break;
-
-    // ---- MMA_A(i), then SELECT(i+1) ----
-    if (tid == 0) {
-#pragma unroll
-      for (int kk = 0; kk < 16; ++kk)
-        mma_f16(tmem + tc::COL_O, d_pk.at((kk >> 2) * 16384 + (kk & 3) * 32), d_v.at(kk * 2048), ID_ATT, kk != 0);
-      issue_update(tile, tile == 0);
-      mma_commit(bar_a);
-      if (C::kQBufs > 1 && tile + 1 < ntiles && wait_q(tile + 1)) issue_select(tile + 1);
-    }
-    // round records, by the row's second thread (off the tensor-core path)
-    if (!aborting && valid && part == 1) {
-      const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) lo |= (uint32_t)pick[j] << (8 * j);
-#pragma unroll
-      for (int j = 4; j < kTopK; ++j) hi |= (uint32_t)pick[j] << (8 * (j - 4));
-      reinterpret_cast<uint2*>(sv.idx)[trow] = make_uint2(lo, hi);
-      float4* wrow = reinterpret_cast<float4*>(sv.w + trow * 8);
-      wrow[0] = make_float4(wgt[0], wgt[1], wgt[2], wgt[3]);
-      wrow[1] = make_float4(wgt[4], wgt[5], wgt[6], 0.f);
-      if (last_round) {
-        const size_t o7 = ((size_t)bh * g.N + n) * kTopK;
-        if (indices) {
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) indices[o7 + j] = pick[j];
-        }
-        if (weights) {
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) weights[o7 + j] = wgt[j];
-        }
-      }
-    }
-    wait_bar(bar_a, ph_a);
-    // second weight term
-    if (!aborting && part == 0) {
-      if (valid) {
+        float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
-          const uint16_t hb = tc::to_bits<T>(wgt[j]);
-          *p_entry(pick[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
-        }
-      }
-      fence_proxy_async_smem();
+          npick[j] = valid ? tslot[j] : 0;
+          // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
+          const uint32_t kk = tkey[j];
+          float sc = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
+          if (npick[j] >= lim) {
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) old_pick[j] = valid ? pick[j] : -1;
-    }
-    // only the issuing warp waits for the second weight term; the others go on to the output
-    tc_fence_before();
-    if (warp == 0) tc::issue_sync(); else tc::issue_arrive();
-    tc_fence_after();
-    // ---- MMA_B(i) ----
-    if (tid == 0) {
-      issue_update(tile, false);
-      mma_commit(bar_b);
-      if (C::kQBufs == 1 && tile + 1 < ntiles) {  // one Q buffer: it is free once MMA_B(i) is done
-        if (tc::timed_wait(bar_b, ph_b)) ph_b ^= 1; else fail(tc::kErrMmaWait);
-        tc_fence_after();
-        issue_q(tile + 1);
-        if (wait_q(tile + 1)) issue_select(tile + 1);
+            for (int k2 = 0; k2 < kTopK; ++k2) sc = (npick[j] == lim + k2) ? mraw[k2] : sc;
+          }
+          nwgt[j] = sc * g.scale;
+          mx = fmaxf(mx, nwgt[j]);
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) {
+          nwgt[j] = expf(nwgt[j] - mx);
+          sum += nwgt[j];
+        }
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) nwgt[j] = nwgt[j] / sum;
       } else {
-        b_pending = true;
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) {
+          npick[j] = 0;
+          nwgt[j] = 0.f;
+        }
       }
-    } else {
-      b_pending = true;
+
+      // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
+      if (tile > 0) wait_live(bar_b, ph_b);
+      if (!aborting && part == 0) {
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j)
+          if (old_pick[j] >= 0) *p_entry(old_pick[j]) = 0;
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) *p_entry(npick[j]) = tc::to_bits<T>(nwgt[j]);
+        }
+        fence_proxy_async_smem();
+      }
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        old_pick[j] = (valid && !aborting) ? npick[j] : -1;
+        pick[j] = npick[j];
+        wgt[j] = nwgt[j];
+      }
+      done_valid = valid && !aborting;
+      orow = row_ptr(out, os, b, h, valid ? n : n0) + 32 * part;
+      if (r && done_valid) {  // read early; added in the output
+#pragma unroll
+        for (int i = 0; i < 4; ++i) prev[i] = reinterpret_cast<const uint4*>(orow)[i];
+      }
+      tc_fence_before();
+      tc::rows_arrive<tc::kBarPhi>();  // MMA_A(i) may start; this tile's score reads are done
+
+      // round records, by the row's second thread (off the tensor-core path)
+      if (done_valid && part == 1) {
+        const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lo |= (uint32_t)pick[j] << (8 * j);
+#pragma unroll
+        for (int j = 4; j < kTopK; ++j) hi |= (uint32_t)pick[j] << (8 * (j - 4));
+        reinterpret_cast<uint2*>(sv.idx)[trow] = make_uint2(lo, hi);
+        float4* wrow = reinterpret_cast<float4*>(sv.w + trow * 8);
+        wrow[0] = make_float4(wgt[0], wgt[1], wgt[2], wgt[3]);
+        wrow[1] = make_float4(wgt[4], wgt[5], wgt[6], 0.f);
+        if (last_round) {
+          const size_t o7 = ((size_t)bh * g.N + n) * kTopK;
+          if (indices) {
+#pragma unroll
+            for (int j = 0; j < kTopK; ++j) indices[o7 + j] = pick[j];
+          }
+          if (weights) {
+#pragma unroll
+            for (int j = 0; j < kTopK; ++j) weights[o7 + j] = wgt[j];
+          }
+        }
+      }
+      if (!kEarlySelect) complete();
     }
-    // ---- output: out (+)= O, 32 columns per thread ----
+    if (kEarlySelect && ntiles > 0) complete();
+    if (ntiles > 0) wait_live(bar_b, ph_b);
+
+    // ---- chunk partials: TMEM lanes are slots here ----
     if (!__any_sync(0xffffffffu, *s_abort != 0)) {
-      T* orow = row_ptr(out, os, b, h, valid ? n : n0) + 32 * part;
-      uint4 prev[4];
-      if (r && valid) {
+      const size_t po = (size_t)bh * g.red_chunks + chunk;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) prev[i] = reinterpret_cast<const uint4*>(orow)[i];  // before the TMEM read
-      }
-      float o[32];
-      tmem_ld32(tmem + lane_base + tc::COL_O + 32 * part, o);
-      tmem_wait_ld();
-      if (valid) {
+      for (int hh = 0; hh < 2; ++hh) {
+        const int m = 128 * hh + row;
+        float s32[32], wv[16];
+        tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh + 32 * part, s32);
+        tmem_ld16(tmem + lane_base + tc::COL_W + 16 * hh, wv);
+        tmem_wait_ld();
+        if (m < g.M) {
+          float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * part);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 pk;
-          uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
-          const T* pv = reinterpret_cast<const T*>(&prev[i]);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>((r ? Elem<T>::load(pv + e) : 0.f) + o[8 * i + e]);
-          reinterpret_cast<uint4*>(orow)[i] = pk;
+          for (int i = 0; i < 8; ++i) dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
+          if (part == 0) fs.Wpart[po * g.M + m] = wv[0];
         }
       }
     }
   }
-  if (b_pending) wait_bar(bar_b, ph_b);
-
-  // ---- chunk partials: TMEM lanes are slots here ----
-  if (!__any_sync(0xffffffffu, *s_abort != 0)) {
-    const size_t po = (size_t)bh * g.red_chunks + chunk;
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int m = 128 * hh + row;
-      float s32[32], wv[16];
-      tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh + 32 * part, s32);
-      tmem_ld16(tmem + lane_base + tc::COL_W + 16 * hh, wv);
-      tmem_wait_ld();
-      if (m < g.M) {
-        float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * part);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
-        if (part == 0) fs.Wpart[po * g.M + m] = wv[0];
-      }
-    }
-  }
-  // ---- wind down: wait (bounded) for copies / MMAs still in flight, free TMEM ----
-  if (tid == 0) {
+  // ---- wind down: wait (bounded) for copies still in flight, free TMEM ----
+  if (issuer_warp && lane == 0) {
     if (img_pending) tc::timed_wait(bar_img, 0);
     for (int i = 0; i < 3; ++i)
       if (q_pending[i]) tc::timed_wait(&bar_q[i], q_phase[i]);
-    if (*s_abort) {  // groups whose completion was not observed
-      tc::timed_wait(bar_s, ph_s);
-      tc::timed_wait(bar_a, ph_a);
-      tc::timed_wait(bar_b, ph_b);
-    }
   }
   tc_fence_before();
   __syncthreads();

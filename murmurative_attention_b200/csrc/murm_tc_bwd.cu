@@ -34,15 +34,16 @@ extern __device__ int g_device_error;
 namespace tcb {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kThreads = 512;
-constexpr int kWarps = kThreads / 32;
+constexpr int kMathWarps = 16;                   // token math
+constexpr int kThreads = 32 * (kMathWarps + 1);  // + one warp whose lane 0 issues the MMAs and copies
+constexpr int kIssuer = 32 * kMathWarps;
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
 constexpr uint32_t OFF_DW = kTables;                 // fp32 [256]
 constexpr uint32_t OFF_P = OFF_DW + 1024;            // 4 slot blocks x 16 KB (1024-aligned)
-constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;        // q tile, swizzled (MMA operand)
-constexpr uint32_t OFF_G = OFF_Q + 16384;            // grad_out tile, swizzled
+constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;        // 2 q tiles (tile parity), swizzled (MMA operand)
+constexpr uint32_t OFF_G = OFF_Q + 2 * 16384;        // grad_out tile, swizzled
 constexpr uint32_t OFF_COEF = OFF_G + 16384;         // fp32 [128][8] scale*da per pick
 constexpr uint32_t OFF_TW = OFF_COEF + kTile * 8 * 4;  // fp32 [128][8] weights of the tile's tokens
 constexpr uint32_t OFF_TGW = OFF_TW + kTile * 8 * 4;   // fp32 [128][8] dL/d weights (last round)
@@ -295,8 +296,9 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t s_base = smem_u32(sm);
   uint64_t* bar_tab = reinterpret_cast<uint64_t*>(sm + tcb::OFF_MISC);
-  uint64_t* bar_qg = bar_tab + 1;
-  uint64_t* bar_mma = bar_tab + 2;
+  uint64_t* bar_q = bar_tab + 1;  // [2], by tile parity
+  uint64_t* bar_g = bar_tab + 3;
+  uint64_t* bar_mma = bar_tab + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + tcb::OFF_MISC + 64);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + tcb::OFF_MISC + 68);
   const float* dWs = reinterpret_cast<const float*>(sm + tcb::OFF_DW);
@@ -311,9 +313,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const bool first = (r == g.R - 1);
   constexpr uint32_t ID_UPD = idesc_f16(tcb::Fmt<T>::v, 128, 64, 1, 1);
 
-  if (tid == 0) {
+  if (tid == tcb::kIssuer) {
     mbar_init(bar_tab, 1);
-    mbar_init(bar_qg, 1);
+    mbar_init(&bar_q[0], 1);
+    mbar_init(&bar_q[1], 1);
+    mbar_init(bar_g, 1);
     mbar_init(bar_mma, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -331,23 +335,35 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  uint32_t ph_qg = 0, ph_mma = 0;
-  bool tab_pending = false, qg_pending = false;
-  if (tid == 0) {
+  uint32_t ph_mma = 0;
+  // the issuer's bookkeeping of asynchronous copies
+  uint32_t ph_q[2] = {0, 0}, ph_g = 0;
+  bool tab_pending = false, q_pending[2] = {false, false}, g_pending = false;
+  auto load_q = [&](int tile_idx) {  // issuer
+    const int bsl = tile_idx & 1;
+    mbar_arrive_expect_tx(&bar_q[bsl], 16384);
+    tma_load_4d(sm + tcb::OFF_Q + bsl * 16384, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bsl]);
+    q_pending[bsl] = true;
+  };
+  auto load_g = [&](int tile_idx) {  // issuer
+    mbar_arrive_expect_tx(bar_g, 16384);
+    tma_load_4d(sm + tcb::OFF_G, &gmap, 0, t_beg + tile_idx * kTile, h, b, bar_g);
+    g_pending = true;
+  };
+  if (tid == tcb::kIssuer) {
     mbar_arrive_expect_tx(bar_tab, tcb::kTables + 1024);
     bulk_g2s(sm, tables + (size_t)bh * tcb::kTables, tcb::kTables, bar_tab);
     bulk_g2s(sm + tcb::OFF_DW, dWpad + (size_t)bh * tcb::kSlotsPad, 1024, bar_tab);
     tab_pending = true;
-    mbar_arrive_expect_tx(bar_qg, 2 * 16384);
-    tma_load_4d(sm + tcb::OFF_Q, &qmap, 0, t_beg, h, b, bar_qg);
-    tma_load_4d(sm + tcb::OFF_G, &gmap, 0, t_beg, h, b, bar_qg);
-    qg_pending = true;
+    load_q(0);
+    load_g(0);
+    if (ntiles > 1) load_q(1);
   }
   // every thread reads the tables: wait for them once
   if (!tcb::timed_wait(bar_tab, 0)) {
     atomicOr(&g_device_error, tcb::kErrWait);
     *s_abort = 1;
-  } else if (tid == 0) {
+  } else if (tid == tcb::kIssuer) {
     tab_pending = false;
   }
   __syncthreads();
@@ -355,7 +371,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const uint8_t* tK = sm + tcb::OFF_K;
   const uint8_t* tV = sm + tcb::OFF_V;
   const uint8_t* tS = sm + tcb::OFF_DS;
-  const uint32_t a_p = s_base + tcb::OFF_P, a_q = s_base + tcb::OFF_Q, a_g = s_base + tcb::OFF_G;
+  const uint32_t a_p = s_base + tcb::OFF_P, a_g = s_base + tcb::OFF_G;
   auto p_entry = [&](int t, int m) -> uint16_t* {
     return reinterpret_cast<uint16_t*>(sm + tcb::OFF_P + (m >> 6) * 16384 + sw128_offset(t, m & 63));
   };
@@ -427,32 +443,41 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
       for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
     }
-    if (tid == 0 && qg_pending) {  // q / grad_out tiles (read below and by the MMAs)
-      if (tcb::timed_wait(bar_qg, ph_qg)) { ph_qg ^= 1; qg_pending = false; }
-      else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+    if (tid == tcb::kIssuer) {  // q / grad_out tiles (read below and by the MMAs)
+      const int bsl = tile & 1;
+      if (q_pending[bsl]) {
+        if (tcb::timed_wait(&bar_q[bsl], ph_q[bsl])) { ph_q[bsl] ^= 1; q_pending[bsl] = false; }
+        else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+      }
+      if (g_pending) {
+        if (tcb::timed_wait(bar_g, ph_g)) { ph_g ^= 1; g_pending = false; }
+        else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     if (__syncthreads_or(*s_abort != 0)) break;  // one decision for all threads
     tc_fence_after();
-    if (tid == 0) {  // dV (first term) runs during the token math
+    if (tid == tcb::kIssuer) {  // dV (first term) runs during the token math
       issue_scatter(a_g, tcb::COL_DV, tile == 0);
       mma_commit(bar_mma);
     }
     if (tile + 1 < ntiles) fetch_recs(tile + 1);
 
     // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp, 2 passes ----
-    const uint8_t* sq = sm + tcb::OFF_Q;
+    const uint32_t a_q = s_base + tcb::OFF_Q + (tile & 1) * 16384;
+    const uint8_t* sq = sm + tcb::OFF_Q + (tile & 1) * 16384;
     const uint8_t* sgo = sm + tcb::OFF_G;
     const int grp = lane >> 3, c8 = lane & 7;
-    constexpr int kPasses = kTile / (4 * tcb::kWarps);
-    static_assert(kPasses * 4 * tcb::kWarps == kTile, "token passes");
+    constexpr int kPasses = kTile / (4 * tcb::kMathWarps);
+    static_assert(kPasses * 4 * tcb::kMathWarps == kTile, "token passes");
+    const bool math_warp = warp < tcb::kMathWarps;
     float4 prev[kPasses][2];  // dq of earlier rounds, fetched before the math
 #pragma unroll
     for (int it = 0; it < kPasses; ++it) {
-      const int t = 4 * warp + it * 4 * tcb::kWarps + grp;
+      const int t = 4 * warp + it * 4 * tcb::kMathWarps + grp;
       prev[it][0] = prev[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (!first && t < nt) {
+      if (math_warp && !first && t < nt) {
         const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n0 + t) * g.D + 8 * c8);
         prev[it][0] = acc[0];
         prev[it][1] = acc[1];
@@ -461,8 +486,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     bool p_free = false;  // has this thread seen the first scatter complete?
 #pragma unroll
     for (int it = 0; it < kPasses; ++it) {
-      const int t0 = 4 * warp + it * 4 * tcb::kWarps;
-      if (t0 >= nt) break;                 // warp-uniform
+      const int t0 = 4 * warp + it * 4 * tcb::kMathWarps;
+      if (!math_warp || t0 >= nt) break;   // warp-uniform
       const int t = t0 + grp;
       const bool live = t < nt;            // group-uniform
       const int n = n0 + (live ? t : 0);
@@ -545,7 +570,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         *p_entry(t, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
       }
     }
-    if (!p_free) wait_mma();  // warps without tokens in this tile
+    if (!p_free) wait_mma();  // warps without tokens in this tile, and the issuer
 
     // ---- remaining scatter phases: fp16 dK; bf16 dV_lo, dK_hi, dK_lo ----
     bool stop = false;
@@ -567,20 +592,17 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       stop = __syncthreads_or(*s_abort != 0);
       tc_fence_after();
       if (stop) break;
-      if (tid == 0) {
+      if (tid == tcb::kIssuer) {
+        // the math and the dV phases are done with the grad_out tile: fetch the next one
+        if (ph == kTerms && tile + 1 < ntiles) load_g(tile + 1);
         issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
         mma_commit(bar_mma);
       }
       wait_mma();
     }
     if (stop) break;
-    // q / grad_out tiles are free: fetch the next ones
-    if (tid == 0 && tile + 1 < ntiles && !*s_abort) {
-      mbar_arrive_expect_tx(bar_qg, 2 * 16384);
-      tma_load_4d(sm + tcb::OFF_Q, &qmap, 0, n0 + kTile, h, b, bar_qg);
-      tma_load_4d(sm + tcb::OFF_G, &gmap, 0, n0 + kTile, h, b, bar_qg);
-      qg_pending = true;
-    }
+    // this q buffer is free: fetch the tile after next into it
+    if (tid == tcb::kIssuer && tile + 2 < ntiles && !*s_abort) load_q(tile + 2);
   }
 
   // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
@@ -607,9 +629,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       }
     }
   }
-  if (tid == 0) {
+  if (tid == tcb::kIssuer) {
     if (tab_pending) tcb::timed_wait(bar_tab, 0);
-    if (qg_pending) tcb::timed_wait(bar_qg, ph_qg);
+    for (int i = 0; i < 2; ++i)
+      if (q_pending[i]) tcb::timed_wait(&bar_q[i], ph_q[i]);
+    if (g_pending) tcb::timed_wait(bar_g, ph_g);
     if (*s_abort) tcb::timed_wait(bar_mma, ph_mma);
   }
   tc_fence_before();
