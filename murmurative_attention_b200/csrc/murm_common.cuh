@@ -19,6 +19,9 @@ constexpr int kTopK = MURM_TOP_K;  // reference.py:38 hard-codes k = 7
 constexpr int kMaxSlots = 256;     // indices are stored as one byte per pick
 constexpr float kEmaEps = 1e-8f;   // reference.py:106-107
 constexpr int kTile = 128;         // tokens per tile (one thread or TMEM lane each)
+constexpr int kSlotRows = 16;              // slot rows per block of the slot-side kernels
+constexpr int kSlotHalo = kSlotRows + 2;   // plus one diffusion halo row on each side: a warp each
+constexpr int kSlotBlocks = 256 / kSlotRows;  // covers the 256 padded slot rows of the operand images
 
 // ---------------------------------------------------------------------------
 // Element types

@@ -235,13 +235,14 @@ __device__ __forceinline__ void put_images(uint8_t* base, int m, int lane, float
 }  // namespace tc
 
 // Round-0 state: slot tables (dtype, strided; batch stride 0 broadcasts) -> fp32 state + images.
-// grid (BH, 8): block y covers 32 slot rows (rows >= M write zero images).
+// grid (BH, 256/16): block y covers 16 slot rows, a warp each (rows >= M write zero images).
 template <typename T>
-__global__ void __launch_bounds__(256) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv, Strides3 svs,
-                                                 Saved sv, uint8_t* images) {
+__global__ void __launch_bounds__(32 * kSlotRows) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv,
+                                                            Strides3 svs, Saved sv, uint8_t* images) {
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
-  for (int m = blockIdx.y * 32 + warp; m < blockIdx.y * 32 + 32; m += 8) {
+  {
+    const int m = blockIdx.y * kSlotRows + warp;
     float2 k = make_float2(0.f, 0.f), v = k;
     if (m < g.M) {
       const T* pk = row_ptr(sk, sks, b, h, m) + 2 * lane;
@@ -258,52 +259,48 @@ __global__ void __launch_bounds__(256) k_tc_load(Geom g, const T* sk, Strides3 s
 
 // Finalize round r: combine the chunk partials in chunk order, EMA (reference.py:105-113)
 // and diffusion (reference.py:128-133) -> state entering round r+1, U_r, W_r and
-// the images of round r+1. grid (BH, 8), warp per slot row, halo rows recomputed.
+// the images of round r+1. grid (BH, M/16): a block owns 16 slot rows and recomputes
+// one halo row on each side; one warp per row, every chunk load of a row in flight at once.
 template <typename T>
-__global__ void __launch_bounds__(256) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
-  __shared__ float2 kn[34][32];
-  __shared__ float2 vn[34][32];
+__global__ void __launch_bounds__(32 * kSlotHalo) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
+  __shared__ float2 kn[kSlotHalo][32];
+  __shared__ float2 vn[kSlotHalo][32];
   const int bh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * 32;
+  const int m0 = blockIdx.y * kSlotRows;
   const size_t MD = (size_t)g.M * tc::kD;
   const size_t cur = ((size_t)r * g.BH + bh) * MD;
-  for (int rr = warp; rr < 34; rr += 8) {
+  {
+    const int rr = warp;  // one row per warp: rows m0-1 .. m0+16
     const int m = m0 - 1 + rr;
     float2 k = make_float2(0.f, 0.f), v = k;
     if (m >= 0 && m < g.M) {
+      const size_t e = cur + (size_t)m * tc::kD + 2 * lane;
+      k = *reinterpret_cast<const float2*>(sv.K + e);
+      v = *reinterpret_cast<const float2*>(sv.V + e);
       float2 S = make_float2(0.f, 0.f);
       float W = 0.f;
-      int ch = 0;
-      for (; ch + 4 <= g.red_chunks; ch += 4) {  // four loads in flight, added in chunk order
-        float2 a[4];
-        float wv[4];
+      for (int ch = 0; ch < g.red_chunks; ch += 8) {  // eight loads in flight, added in chunk order
+        float2 a[8];
+        float wv[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const size_t po = (size_t)bh * g.red_chunks + ch + u;
+        for (int u = 0; u < 8; ++u) {
+          const size_t po = (size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1);
           a[u] = *reinterpret_cast<const float2*>(fs.Spart + (po * g.M + m) * tc::kD + 2 * lane);
           wv[u] = fs.Wpart[po * g.M + m];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          S.x = __fadd_rn(S.x, a[u].x);
-          S.y = __fadd_rn(S.y, a[u].y);
-          W = __fadd_rn(W, wv[u]);
+        for (int u = 0; u < 8; ++u) {
+          if (ch + u < g.red_chunks) {
+            S.x = __fadd_rn(S.x, a[u].x);
+            S.y = __fadd_rn(S.y, a[u].y);
+            W = __fadd_rn(W, wv[u]);
+          }
         }
-      }
-      for (; ch < g.red_chunks; ++ch) {
-        const size_t po = (size_t)bh * g.red_chunks + ch;
-        const float2 a = *reinterpret_cast<const float2*>(fs.Spart + (po * g.M + m) * tc::kD + 2 * lane);
-        S.x = __fadd_rn(S.x, a.x);
-        S.y = __fadd_rn(S.y, a.y);
-        W = __fadd_rn(W, fs.Wpart[po * g.M + m]);
       }
       const bool hit = W > 0.f;
       const float den = __fadd_rn(W, kEmaEps);
       const float2 U = make_float2(__fdiv_rn(S.x, den), __fdiv_rn(S.y, den));
-      const size_t e = cur + (size_t)m * tc::kD + 2 * lane;
-      k = *reinterpret_cast<const float2*>(sv.K + e);
-      v = *reinterpret_cast<const float2*>(sv.V + e);
-      if (rr >= 1 && rr <= 32) {  // this block's rows record U and W
+      if (rr >= 1 && rr <= kSlotRows) {  // this block's rows record U and W
         *reinterpret_cast<float2*>(sv.U + e) = U;
         if (lane == 0) sv.W[((size_t)r * g.BH + bh) * g.M + m] = W;
       }
@@ -317,29 +314,29 @@ __global__ void __launch_bounds__(256) k_tc_finalize(Geom g, int r, Saved sv, Fw
     vn[rr][lane] = v;
   }
   __syncthreads();
+  if (warp < 1 || warp > kSlotRows) return;
   uint8_t* base = fs.images + (size_t)bh * tc::Layout<T>::kImages;
   const size_t nxt = ((size_t)(r + 1) * g.BH + bh) * MD;
-  for (int rr = 1 + warp; rr < 33; rr += 8) {
-    const int m = m0 - 1 + rr;
-    float2 k = make_float2(0.f, 0.f), v = k;
-    if (m < g.M) {
-      k = kn[rr][lane];
-      v = vn[rr][lane];
-      if (m > 0 && m < g.M - 1) {
-        const float2 kl = kn[rr - 1][lane], kr = kn[rr + 1][lane], vl = vn[rr - 1][lane], vr = vn[rr + 1][lane];
-        const float2 tk = make_float2(__fsub_rn(__fadd_rn(kl.x, kr.x), __fmul_rn(2.f, k.x)),
-                                      __fsub_rn(__fadd_rn(kl.y, kr.y), __fmul_rn(2.f, k.y)));
-        const float2 tv = make_float2(__fsub_rn(__fadd_rn(vl.x, vr.x), __fmul_rn(2.f, v.x)),
-                                      __fsub_rn(__fadd_rn(vl.y, vr.y), __fmul_rn(2.f, v.y)));
-        k = make_float2(__fadd_rn(k.x, __fmul_rn(g.gamma, tk.x)), __fadd_rn(k.y, __fmul_rn(g.gamma, tk.y)));
-        v = make_float2(__fadd_rn(v.x, __fmul_rn(g.gamma, tv.x)), __fadd_rn(v.y, __fmul_rn(g.gamma, tv.y)));
-      }
-      const size_t e = nxt + (size_t)m * tc::kD + 2 * lane;
-      *reinterpret_cast<float2*>(sv.K + e) = k;
-      *reinterpret_cast<float2*>(sv.V + e) = v;
+  const int rr = warp;
+  const int m = m0 - 1 + rr;
+  float2 k = make_float2(0.f, 0.f), v = k;
+  if (m < g.M) {
+    k = kn[rr][lane];
+    v = vn[rr][lane];
+    if (m > 0 && m < g.M - 1) {
+      const float2 kl = kn[rr - 1][lane], kr = kn[rr + 1][lane], vl = vn[rr - 1][lane], vr = vn[rr + 1][lane];
+      const float2 tk = make_float2(__fsub_rn(__fadd_rn(kl.x, kr.x), __fmul_rn(2.f, k.x)),
+                                    __fsub_rn(__fadd_rn(kl.y, kr.y), __fmul_rn(2.f, k.y)));
+      const float2 tv = make_float2(__fsub_rn(__fadd_rn(vl.x, vr.x), __fmul_rn(2.f, v.x)),
+                                    __fsub_rn(__fadd_rn(vl.y, vr.y), __fmul_rn(2.f, v.y)));
+      k = make_float2(__fadd_rn(k.x, __fmul_rn(g.gamma, tk.x)), __fadd_rn(k.y, __fmul_rn(g.gamma, tk.y)));
+      v = make_float2(__fadd_rn(v.x, __fmul_rn(g.gamma, tv.x)), __fadd_rn(v.y, __fmul_rn(g.gamma, tv.y)));
     }
-    tc::put_images<T>(base, m, lane, k, v);  // rows >= M: zero
+    const size_t e = nxt + (size_t)m * tc::kD + 2 * lane;
+    *reinterpret_cast<float2*>(sv.K + e) = k;
+    *reinterpret_cast<float2*>(sv.V + e) = v;
   }
+  tc::put_images<T>(base, m, lane, k, v);  // rows >= M: zero
 }
 
 // ---------------------------------------------------------------------------
@@ -950,12 +947,13 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
     cudaFuncSetAttribute(k_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Layout<T>::kSmem);
     attr = true;
   }
-  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, 8), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
+  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), 32 * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
               static_cast<const T*>(p.sv), p.svs, sv, images);
   for (int r = 0; r < g.R; ++r) {
     MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
-    if (r + 1 < g.R) MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, 8), 256, 0, st, g, r, sv, fs);
+    if (r + 1 < g.R)
+      MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), 32 * kSlotHalo, 0, st, g, r, sv, fs);
   }
   return cudaGetLastError();
 }

@@ -34,9 +34,9 @@ extern __device__ int g_device_error;
 namespace tcb {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kMathWarps = 16;                   // token math
-constexpr int kThreads = 32 * (kMathWarps + 1);  // + one warp whose lane 0 issues the MMAs and copies
-constexpr int kIssuer = 32 * kMathWarps;
+constexpr int kMathWarps = 16;              // token math
+constexpr int kThreads = 32 * kMathWarps;
+constexpr int kIssuer = 0;                  // the thread that issues the MMAs and copies
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
@@ -149,20 +149,21 @@ __device__ __forceinline__ void warp_sum8(float (&v)[8]) {
 // Direct parts live in bs.dK[r & 1] / bs.dV[r & 1] (round parity): a block reads
 // its neighbours' rows of round r while they write round r-1.
 template <typename T>
-__global__ void __launch_bounds__(256) k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv,
-                                                   BwdScratch bs, uint8_t* tables, float* dWpad, T* gsk,
-                                                   Strides3 gsks, T* gsv, Strides3 gsvs) {
+__global__ void __launch_bounds__(32 * kSlotHalo) k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv,
+                                                             BwdScratch bs, uint8_t* tables, float* dWpad, T* gsk,
+                                                             Strides3 gsks, T* gsv, Strides3 gsvs) {
   const float* dir_k = bs.dK[r & 1];
   const float* dir_v = bs.dV[r & 1];
   float* nxt_k = bs.dK[(r + 1) & 1];  // direct parts of round r-1
   float* nxt_v = bs.dV[(r + 1) & 1];
-  __shared__ float2 skk[34][32];  // dK_r rows m0-1 .. m0+32, as float2 per lane
-  __shared__ float2 svv[34][32];
+  __shared__ float2 skk[kSlotHalo][32];  // dK_r rows m0-1 .. m0+16, as float2 per lane
+  __shared__ float2 svv[kSlotHalo][32];
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H;
-  const int m0 = blockIdx.y * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kSlotRows, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t MD = (size_t)g.M * g.D;
-  // 1. dK_r, dV_r for the block and its halo
-  for (int rr = warp; rr < 34; rr += 8) {
+  // 1. dK_r, dV_r for the block and its halo: one row per warp, every chunk load in flight at once
+  {
+    const int rr = warp;
     const int m = m0 - 1 + rr;
     float2 k = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
     if (m >= 0 && m < g.M) {
@@ -172,23 +173,18 @@ __global__ void __launch_bounds__(256) k_bwd_slots(Geom g, int r, int has_dir, i
         v = *reinterpret_cast<const float2*>(dir_v + e);
       }
       if (has_part) {
-        int ch = 0;
-        for (; ch + 4 <= g.red_chunks; ch += 4) {  // four loads in flight, added in chunk order
-          float2 a[4], c[4];
+        for (int ch = 0; ch < g.red_chunks; ch += 8) {  // added in chunk order
+          float2 a[8], c[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const size_t po = ((size_t)bh * g.red_chunks + ch + u) * MD + (size_t)m * g.D + 2 * lane;
+          for (int u = 0; u < 8; ++u) {
+            const size_t po = ((size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1)) * MD + (size_t)m * g.D + 2 * lane;
             a[u] = *reinterpret_cast<const float2*>(bs.dKpart + po);
             c[u] = *reinterpret_cast<const float2*>(bs.dVpart + po);
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) { k.x += a[u].x; k.y += a[u].y; v.x += c[u].x; v.y += c[u].y; }
-        }
-        for (; ch < g.red_chunks; ++ch) {
-          const size_t po = ((size_t)bh * g.red_chunks + ch) * MD + (size_t)m * g.D + 2 * lane;
-          const float2 a = *reinterpret_cast<const float2*>(bs.dKpart + po);
-          const float2 c = *reinterpret_cast<const float2*>(bs.dVpart + po);
-          k.x += a.x; k.y += a.y; v.x += c.x; v.y += c.y;
+          for (int u = 0; u < 8; ++u) {
+            if (ch + u < g.red_chunks) { k.x += a[u].x; k.y += a[u].y; v.x += c[u].x; v.y += c[u].y; }
+          }
         }
       }
     }
@@ -196,26 +192,24 @@ __global__ void __launch_bounds__(256) k_bwd_slots(Geom g, int r, int has_dir, i
     svv[rr][lane] = v;
   }
   __syncthreads();
+  if (warp < 1 || warp > kSlotRows) return;
+  const int rr = warp;
+  const int m = m0 - 1 + rr;
+  if (m >= g.M) return;
   if (r == 0) {  // the slot gradients
-    for (int rr = 1 + warp; rr < 33; rr += 8) {
-      const int m = m0 - 1 + rr;
-      if (m >= g.M) break;
-      T* pk = row_ptr(gsk, gsks, b, h, m) + 2 * lane;
-      T* pv = row_ptr(gsv, gsvs, b, h, m) + 2 * lane;
-      Elem<T>::store(pk, skk[rr][lane].x);
-      Elem<T>::store(pk + 1, skk[rr][lane].y);
-      Elem<T>::store(pv, svv[rr][lane].x);
-      Elem<T>::store(pv + 1, svv[rr][lane].y);
-    }
+    T* pk = row_ptr(gsk, gsks, b, h, m) + 2 * lane;
+    T* pv = row_ptr(gsv, gsvs, b, h, m) + 2 * lane;
+    Elem<T>::store(pk, skk[rr][lane].x);
+    Elem<T>::store(pk + 1, skk[rr][lane].y);
+    Elem<T>::store(pv, svv[rr][lane].x);
+    Elem<T>::store(pv + 1, svv[rr][lane].y);
     return;
   }
   // 2. adjoints of round r-1 for slots of this block
   const int rp = r - 1;
   const float gm2 = -2.f * g.gamma;
   uint8_t* tab = tables + (size_t)bh * tcb::kTables;
-  for (int rr = 1 + warp; rr < 33; rr += 8) {
-    const int m = m0 - 1 + rr;
-    if (m >= g.M) break;
+  {
     const bool in_m = m > 0 && m < g.M - 1, in_l = m - 1 > 0, in_r = m + 1 < g.M - 1;
     float2 ak = skk[rr][lane], av = svv[rr][lane];
     if (in_m) {
@@ -694,13 +688,13 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
   }
   uint8_t* tables = bs.tables;
   float* dWpad = reinterpret_cast<float*>(tables + (size_t)g.BH * tcb::kTables);
-  const int slot_blocks = (g.M + 31) / 32;
-  MURM_LAUNCH("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, 4), 256, 0, st, g, sv, tables, dWpad);
+  const int slot_blocks = (g.M + kSlotRows - 1) / kSlotRows;
+  MURM_LAUNCH("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad);
   for (int r = g.R - 1; r >= 0; --r) {
     MURM_LAUNCH("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
                 qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,
                 static_cast<T*>(p.gq), p.gqs, sv, bs, tables, dWpad);
-    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), 256, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
+    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), 32 * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
                 sv, bs, tables, dWpad, static_cast<T*>(p.gsk), p.gsks, static_cast<T*>(p.gsv), p.gsvs);
   }
   return cudaGetLastError();
