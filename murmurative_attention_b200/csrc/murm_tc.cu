@@ -57,8 +57,9 @@ __device__ __forceinline__ void quadrant_sync(int quadrant) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(32 * kParts) : "memory");
 }
 // Named barriers over the whole CTA that the issuer warp waits on and the row
-// warps only arrive at: the tile's first (5) and second (6) weight terms are in P.
-constexpr int kBarPhi = 5, kBarPlo = 6;
+// warps only arrive at: the tile's first (5) and second (6) weight terms are in P;
+// the row warps are done reading the tile's scores (7).
+constexpr int kBarPhi = 5, kBarPlo = 6, kBarSfree = 7;
 template <int kId>
 __device__ __forceinline__ void issuer_wait() {
   asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kThreads) : "memory");
@@ -519,14 +520,21 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       __syncwarp();
     };
     for (int tile = 0; tile < ntiles; ++tile) {
-      if (kEarlySelect && tile > 0) mma_b(tile - 1);
+      if (kEarlySelect) {
+        if (tile > 0) mma_b(tile - 1);
+        tc::issuer_wait<tc::kBarSfree>();  // the scores of tile i are read: SELECT(i+1)
+        if (lane == 0 && !*s_abort && tile + 1 < ntiles) {
+          tc_fence_after();
+          if (wait_q(tile + 1)) {
+            issue_select(tile + 1);
+            ++n_s;
+          }
+        }
+        __syncwarp();
+      }
       tc::issuer_wait<tc::kBarPhi>();
       if (lane == 0 && !*s_abort) {
         tc_fence_after();
-        if (kEarlySelect && tile + 1 < ntiles && wait_q(tile + 1)) {  // SELECT(i+1) first
-          issue_select(tile + 1);
-          ++n_s;
-        }
         // ---- MMA_A(i) ----
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk)
@@ -670,6 +678,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         tkey[j] = 0u;
         tslot[j] = 0;
       }
+      bool scan = false;
       if (!aborting) {
         float lst[16];
         tmem_ld16(tmem + lane_base + tc::COL_X, lst);
@@ -679,40 +688,46 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         thr = all8[kTopK - 1];
         // rows with fewer than 7 finite group maxima (causal rows near the start) scan exactly
         exact_scan = valid && !(thr > -INFINITY);
-        const bool scan = valid && !exact_scan;
+        scan = valid && !exact_scan;
+      }
+      auto rank_chunks = [&](int c) {  // columns 32c .. 32c+63 of this thread's half
+        float x[2][32];
+        load2(c, x[0], x[1]);
 #pragma unroll
-        for (int c = 0; c < 4; c += 2) {
-          float x[2][32];
-          load2(c, x[0], x[1]);
+        for (int k = 0; k < 2; ++k) {
+          uint32_t a = 0, b2 = 0;  // two independent chains
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            uint32_t a = 0, b2 = 0;  // two independent chains
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              a |= (x[k][i] >= thr) ? (1u << i) : 0u;
-              b2 |= (x[k][16 + i] >= thr) ? (1u << (16 + i)) : 0u;
-            }
-            uint32_t msk = scan ? (a | b2) : 0u;
-            while (__any_sync(0xffffffffu, msk != 0)) {
-              // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
-              const int bit = __ffs(msk) - 1;
-              const uint32_t key = rank_key(tc::pick32(x[k], bit & 31));
-              tc::offer7_asc(tkey, tslot, msk ? key : 0u, col0 + 32 * (c + k) + bit);
-              msk &= msk - 1;
-            }
+          for (int i = 0; i < 16; ++i) {
+            a |= (x[k][i] >= thr) ? (1u << i) : 0u;
+            b2 |= (x[k][16 + i] >= thr) ? (1u << (16 + i)) : 0u;
+          }
+          uint32_t msk = scan ? (a | b2) : 0u;
+          while (__any_sync(0xffffffffu, msk != 0)) {
+            // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
+            const int bit = __ffs(msk) - 1;
+            const uint32_t key = rank_key(tc::pick32(x[k], bit & 31));
+            tc::offer7_asc(tkey, tslot, msk ? key : 0u, col0 + 32 * (c + k) + bit);
+            msk &= msk - 1;
           }
         }
+      };
+      if (!aborting) rank_chunks(0);
+      // the previous tile: second weight term and output (its MMA_A is done by now; MMA_B then
+      // runs under the rest of the ranking)
+      if (kEarlySelect && tile > 0) complete();
+      if (!aborting) {
+        rank_chunks(2);
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) xch[j * tc::kRowThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
       }
       tc::quadrant_sync(quadrant);
 
-      // the previous tile: second weight term and output, while this tile's scores wait in TMEM
-      if (kEarlySelect && tile > 0) complete();
-
       // pass 3 (both threads of a row, redundantly): merge the two lists, softmax
       int npick[kTopK];
       float nwgt[kTopK];
+      float mraw[kTopK];  // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
       if (!aborting) {
         if (!exact_scan) {
           uint64_t other[8], mine[8], top[8];
@@ -729,10 +744,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             tslot[j] = tc::rank_slot(top[j]);
           }
         }
-        // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
-        float mraw[kTopK];
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
         if (__any_sync(0xffffffffu, exact_scan)) {
           // exact full scan of the row's 256 columns from TMEM
 #pragma unroll 1
@@ -757,6 +768,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             }
           }
         }
+      }
+      if (kEarlySelect) {
+        tc_fence_before();
+        tc::rows_arrive<tc::kBarSfree>();  // SELECT(i+1) may overwrite the scores
+      }
+      if (!aborting) {
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
