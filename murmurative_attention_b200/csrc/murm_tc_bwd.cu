@@ -410,6 +410,27 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   };
   auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
   fetch_recs(0);
+  // dq of earlier rounds for this thread's tokens of a tile, fetched while the previous
+  // tile's last scatter runs (global loads in flight slow the math's table reads)
+  constexpr int kPasses = kTile / (4 * tcb::kMathWarps);
+  static_assert(kPasses * 4 * tcb::kMathWarps == kTile, "token passes");
+  float4 prev[kPasses][2];
+  auto fetch_prev = [&](int tile_idx) {
+    const int nn0 = t_beg + tile_idx * kTile;
+    const int nnt = min(kTile, t_end - nn0);
+#pragma unroll
+    for (int it = 0; it < kPasses; ++it) {
+      const int t = 4 * (tid >> 5) + it * 4 * tcb::kMathWarps + ((tid & 31) >> 3);
+      prev[it][0] = prev[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!first && t < nnt) {
+        const float4* acc =
+            reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + nn0 + t) * g.D + 8 * (tid & 7));
+        prev[it][0] = acc[0];
+        prev[it][1] = acc[1];
+      }
+    }
+  };
+  fetch_prev(0);
   uint2 old_ix = make_uint2(0u, 0u);  // thread t's token row of P in the previous tile
   bool old_live = false;
 
@@ -456,27 +477,13 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       issue_scatter(a_g, tcb::COL_DV, tile == 0);
       mma_commit(bar_mma);
     }
-    if (tile + 1 < ntiles) fetch_recs(tile + 1);
 
     // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp, 2 passes ----
     const uint32_t a_q = s_base + tcb::OFF_Q + (tile & 1) * 16384;
     const uint8_t* sq = sm + tcb::OFF_Q + (tile & 1) * 16384;
     const uint8_t* sgo = sm + tcb::OFF_G;
     const int grp = lane >> 3, c8 = lane & 7;
-    constexpr int kPasses = kTile / (4 * tcb::kMathWarps);
-    static_assert(kPasses * 4 * tcb::kMathWarps == kTile, "token passes");
     const bool math_warp = warp < tcb::kMathWarps;
-    float4 prev[kPasses][2];  // dq of earlier rounds, fetched before the math
-#pragma unroll
-    for (int it = 0; it < kPasses; ++it) {
-      const int t = 4 * warp + it * 4 * tcb::kMathWarps + grp;
-      prev[it][0] = prev[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (math_warp && !first && t < nt) {
-        const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n0 + t) * g.D + 8 * c8);
-        prev[it][0] = acc[0];
-        prev[it][1] = acc[1];
-      }
-    }
     bool p_free = false;  // has this thread seen the first scatter complete?
 #pragma unroll
     for (int it = 0; it < kPasses; ++it) {
@@ -565,6 +572,12 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       }
     }
     if (!p_free) wait_mma();  // warps without tokens in this tile, and the issuer
+
+    // the next tile's records and earlier-round dq, in flight during the last scatter
+    if (tile + 1 < ntiles) {
+      fetch_recs(tile + 1);
+      fetch_prev(tile + 1);
+    }
 
     // ---- remaining scatter phases: fp16 dK; bf16 dV_lo, dK_hi, dK_lo ----
     bool stop = false;
