@@ -68,6 +68,59 @@ __device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// acc += sum over i = 0..7 of a_i * b_i for two runs of eight 16-bit values (one uint4
+// each), in order; each product is exact and added with one rounding (fp32 fma on the
+// 16-bit operands: the same result as converting both to fp32 first, in fewer instructions).
+#define MURM_DOT8(TY)                                                                                    \
+  asm("{\n .reg .b16 a0, a1, b0, b1;\n"                                                                \
+      " mov.b32 {a0, a1}, %1;\n mov.b32 {b0, b1}, %5;\n fma.rn.f32." TY " %0, a0, b0, %0;\n"          \
+      " fma.rn.f32." TY " %0, a1, b1, %0;\n"                                                            \
+      " mov.b32 {a0, a1}, %2;\n mov.b32 {b0, b1}, %6;\n fma.rn.f32." TY " %0, a0, b0, %0;\n"          \
+      " fma.rn.f32." TY " %0, a1, b1, %0;\n"                                                            \
+      " mov.b32 {a0, a1}, %3;\n mov.b32 {b0, b1}, %7;\n fma.rn.f32." TY " %0, a0, b0, %0;\n"          \
+      " fma.rn.f32." TY " %0, a1, b1, %0;\n"                                                            \
+      " mov.b32 {a0, a1}, %4;\n mov.b32 {b0, b1}, %8;\n fma.rn.f32." TY " %0, a0, b0, %0;\n"          \
+      " fma.rn.f32." TY " %0, a1, b1, %0;\n}"                                                           \
+      : "+f"(acc)                                                                                        \
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w))
+template <typename T>
+__device__ __forceinline__ float dot8(const uint4& a, const uint4& b, float acc);
+template <>
+__device__ __forceinline__ float dot8<__half>(const uint4& a, const uint4& b, float acc) {
+  MURM_DOT8("f16");
+  return acc;
+}
+template <>
+__device__ __forceinline__ float dot8<__nv_bfloat16>(const uint4& a, const uint4& b, float acc) {
+  MURM_DOT8("bf16");
+  return acc;
+}
+#undef MURM_DOT8
+
+// acc[i] += x * row_i over eight 16-bit values. fp16: x is rounded to fp16 and each
+// product taken by an fp32 fma on the 16-bit operands (the precision the fp16 scatter
+// MMAs use for the same weights); bf16: the row is converted and x kept in fp32.
+template <typename T>
+__device__ __forceinline__ void axpy8(float x, const uint4& row, float (&acc)[8]);
+template <>
+__device__ __forceinline__ void axpy8<__half>(float x, const uint4& row, float (&acc)[8]) {
+  const uint16_t xh = __half_as_ushort(__float2half_rn(x));
+  asm("{\n .reg .b16 r0, r1;\n"
+      " mov.b32 {r0, r1}, %9;\n fma.rn.f32.f16 %0, %8, r0, %0;\n fma.rn.f32.f16 %1, %8, r1, %1;\n"
+      " mov.b32 {r0, r1}, %10;\n fma.rn.f32.f16 %2, %8, r0, %2;\n fma.rn.f32.f16 %3, %8, r1, %3;\n"
+      " mov.b32 {r0, r1}, %11;\n fma.rn.f32.f16 %4, %8, r0, %4;\n fma.rn.f32.f16 %5, %8, r1, %5;\n"
+      " mov.b32 {r0, r1}, %12;\n fma.rn.f32.f16 %6, %8, r0, %6;\n fma.rn.f32.f16 %7, %8, r1, %7;\n}"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+        "+f"(acc[7])
+      : "h"(xh), "r"(row.x), "r"(row.y), "r"(row.z), "r"(row.w));
+}
+template <>
+__device__ __forceinline__ void axpy8<__nv_bfloat16>(float x, const uint4& row, float (&acc)[8]) {
+  const __nv_bfloat16* t = reinterpret_cast<const __nv_bfloat16*>(&row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = fmaf(x, __bfloat162float(t[i]), acc[i]);
+}
+
 template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
@@ -501,27 +554,18 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
       // swizzled 128-byte rows of the TMA tiles: 16-byte chunk c8 of row t
       const uint32_t rq = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
-      float qv[8], gv[8];
-      tcb::load8<T>(sq + rq, qv);
-      tcb::load8<T>(sgo + rq, gv);
+      const uint4 qv = *reinterpret_cast<const uint4*>(sq + rq);
+      const uint4 gv = *reinterpret_cast<const uint4*>(sgo + rq);
       float dq[8] = {prev[it][0].x, prev[it][0].y, prev[it][0].z, prev[it][0].w,
                      prev[it][1].x, prev[it][1].y, prev[it][1].z, prev[it][1].w};
       float part[8];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        float vv[8];
-        tcb::load8<T>(tV + ix[j] * 128 + 16 * c8, vv);
-        float a = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) a = fmaf(gv[i], vv[i], a);
+        float a = tcb::dot8<T>(gv, *reinterpret_cast<const uint4*>(tV + ix[j] * 128 + 16 * c8), 0.f);
         if (has_slot_grad) {  // dS[i_j] enters both dw_j and dq
-          float ds[8];
-          tcb::load8<T>(tS + ix[j] * 128 + 16 * c8, ds);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            a = fmaf(qv[i], ds[i], a);
-            dq[i] = fmaf(w[j], ds[i], dq[i]);
-          }
+          const uint4 ds = *reinterpret_cast<const uint4*>(tS + ix[j] * 128 + 16 * c8);
+          a = tcb::dot8<T>(qv, ds, a);
+          tcb::axpy8<T>(w[j], ds, dq);
         }
         part[j] = a;
       }
@@ -538,10 +582,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         c[j] = g.scale * (w[j] * (dw[j] - s));
-        float kv[8];
-        tcb::load8<T>(tK + ix[j] * 128 + 16 * c8, kv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dq[i] = fmaf(c[j], kv[i], dq[i]);
+        tcb::axpy8<T>(c[j], *reinterpret_cast<const uint4*>(tK + ix[j] * 128 + 16 * c8), dq);
       }
       if (live) {
         if (r == 0) {
