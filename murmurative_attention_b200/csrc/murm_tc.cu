@@ -788,14 +788,18 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           nwgt[j] = sc * g.scale;
           mx = fmaxf(mx, nwgt[j]);
         }
+        // softmax with the hardware exponential and one reciprocal: the weights enter P as
+        // 16-bit terms and the update sums, where a relative error of ~1e-6 is far below
+        // the rounding of those terms and the parity tolerance
         float sum = 0.f;
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
-          nwgt[j] = expf(nwgt[j] - mx);
+          nwgt[j] = __expf(nwgt[j] - mx);
           sum += nwgt[j];
         }
+        const float inv = __frcp_rn(sum);
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) nwgt[j] = nwgt[j] / sum;
+        for (int j = 0; j < kTopK; ++j) nwgt[j] *= inv;
       } else {
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
