@@ -457,6 +457,58 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+LAYER = dict(B=2, N=8192, dim=1024, heads=16, slots=256, R=3)
+
+
+def run_layer(args):
+    """the MurmurativeAttention layer training step, bf16, data
+    parallel: every rank trains on its own 2 sequences of 8192 tokens (16 sequences at 8
+    GPUs) and the parameter gradients are averaged over NCCL while the backward runs.
+    One step = forward, mean-square loss, backward, gradient average, SGD update."""
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from murmurative_attention_b200 import MurmurativeAttention
+    from murmurative_attention_b200.training import GradientAverager, dp_train_step
+
+    L = LAYER
+    torch.manual_seed(0)  # the same initial parameters on every rank
+    layer = MurmurativeAttention(L["dim"], L["heads"], L["slots"], rounds=L["R"]).to(dev, torch.bfloat16)
+    with torch.no_grad():
+        layer.q_proj.weight.normal_(0.0, L["dim"] ** -0.5)
+        layer.o_proj.weight.normal_(0.0, L["dim"] ** -0.5)
+        layer.slot_embeddings.normal_(0.0, 1.0)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x = torch.randn(L["B"], L["N"], L["dim"], device=dev, dtype=torch.bfloat16, generator=g)
+    opt = torch.optim.SGD(layer.parameters(), lr=1e-3)
+    avg = GradientAverager(layer.parameters())
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        dp_train_step(layer, x, opt, avg)
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(lambda: dp_train_step(layer, x, opt, avg), args.steps, flush)
+    barrier(world)
+    total_ms = max_over_ranks(sum(times), world)
+    tokens = world * L["B"] * L["N"] * args.steps
+    ms = total_ms / args.steps
+    if rank == 0:
+        line = {"metric": "MurmurativeAttention layer training step tokens/s (BASELINE configs[3])",
+                "value": round(tokens / (total_ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "layer: dim 1024, heads 16 (d=64), M=256, R=3, k=7, x~N(0,1) [2 per rank,8192,1024], "
+                                       "q_proj/o_proj ~N(0,1/1024), slot_embeddings ~N(0,1); SGD",
+                           "batch_per_rank": L["B"], "global_batch": world * L["B"], "seq_len": L["N"],
+                           "parallelism": f"dp{world}",
+                           "l2": "flushed by a 256 MiB write before every timed step"}}
+        print(json.dumps(line), flush=True)
+    avg.remove()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,10 +518,17 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", choices=("northstar", "layer"), default="northstar",
+                    help="layer: BASELINE configs[3], the data-parallel layer training step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "layer":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the layer workload has no reference arm here"}))
+            return
+        run_layer(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

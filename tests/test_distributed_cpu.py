@@ -67,3 +67,58 @@ def test_gloo_two_ranks_shard_and_allreduce():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert dict(results) == {0: True, 1: True}
+
+
+class _Toy(torch.nn.Module):
+    """Two bias-free Linear layers and a free parameter, like the layer's projections and
+    slot embeddings."""
+
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(1)
+        self.a = torch.nn.Linear(6, 5, bias=False)
+        self.b = torch.nn.Linear(5, 4, bias=False)
+        self.emb = torch.nn.Parameter(torch.randn(4))
+
+    def forward(self, x):
+        return self.b(torch.tanh(self.a(x))) + self.emb
+
+
+def _train_worker(rank, world, port, results):
+    """Two ranks take one data-parallel step on their own batches; the parameters must
+    match one step on the union of the batches (equal batch sizes: the mean of the ranks'
+    gradients is the gradient of the global mean loss)."""
+    from murmurative_attention_b200.training import GradientAverager, dp_train_step
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(7)
+        xs = [torch.randn(3, 6, generator=g) for _ in range(world)]
+        model = _Toy()
+        opt = torch.optim.SGD(model.parameters(), lr=0.1)
+        avg = GradientAverager(model.parameters())
+        dp_train_step(model, xs[rank], opt, avg)
+        avg.remove()
+        ref = _Toy()
+        ref_opt = torch.optim.SGD(ref.parameters(), lr=0.1)
+        ref(torch.cat(xs)).square().mean().backward()
+        ref_opt.step()
+        results[rank] = all(torch.allclose(p, q, atol=1e-6) for p, q in zip(model.parameters(), ref.parameters()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_dp_train_step_matches_single_process():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_train_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert dict(results) == {0: True, 1: True}
