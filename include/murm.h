@@ -143,6 +143,126 @@ MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* st
 #define MURM_NOSCRATCH_BYTES (64u << 20)
 MURM_API murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Per-phase operations: the reference's op surface one round at a time
+ * (torch-ext/torch_binding.cpp:6-33 slot_select_attend, slot_update,
+ * slot_diffusion and their _backward ops; src/murmurative/ops.py:219-327),
+ * general CUDA-core kernels with everything the fused call leaves out: a
+ * selection mask, a position bias, effective (dynamic) M, separate token keys
+ * and values, any head_dim that is a multiple of 8 up to 128, and M up to
+ * 1024 (M x head_dim x 4 bytes at most 200 KiB). Slot sums are deterministic
+ * (slot-major, token order). Conventions as above; grads are written in the
+ * tensors' dtype, weights fp32, indices int64 [B,H,N,7] contiguous.
+ * ------------------------------------------------------------------------ */
+typedef struct murm_phase_shape {
+  int32_t batch, heads, tokens, slots, head_dim;
+  int32_t dtype; /* murm_dtype of every non-index, non-weight tensor */
+} murm_phase_shape;
+
+/* Replaces slot_select_attend (torch_binding.cpp:8, cuda_ops.h:6-19;
+ * semantics reference.py:6-68): scores q.k (+ position_bias) with masked,
+ * causal (slot m > token n) and tail (m >= effective_m) slots at -inf, top-7
+ * (ties to the lowest slot), softmax of scale * q.k over the 7 picks (the mask
+ * and bias do not enter the attend, reference.py:61-63), weighted sum of their
+ * values. With `indices_in` set the selection is skipped and those indices are
+ * attended (slot_attend, reference.py:42-68; out-of-range values clamped). */
+typedef struct murm_select_attend_args {
+  murm_phase_shape shape;
+  int32_t causal;
+  int32_t effective_m;         /* <= 0 or >= M: every slot */
+  double scale;                /* <= 0: 1/sqrt(head_dim) */
+  const void* q; int64_t q_stride[3];
+  const void* slot_keys; int64_t sk_stride[3];
+  const void* slot_values; int64_t sv_stride[3];
+  const uint8_t* mask; int64_t mask_stride[4];     /* optional; 0 = masked; element strides b,h,n,m (0 broadcasts) */
+  const void* position_bias; int64_t bias_stride[4]; /* optional, dtype of q */
+  const int64_t* indices_in;   /* optional [B,H,N,7]: attend only */
+  void* out; int64_t out_stride[3];
+  int64_t* indices;            /* [B,H,N,7]; may equal indices_in */
+  float* weights;              /* [B,H,N,7] */
+} murm_select_attend_args;
+MURM_API murm_status murm_select_attend_fwd(const murm_select_attend_args* args, void* stream);
+
+/* Replaces slot_select_attend_backward (torch_binding.cpp:9): gradients of q,
+ * slot_keys and slot_values from grad_out and (optional) grad_weights. The
+ * slot gradients are per batch element ([B,H,M,d]) even when the forward
+ * broadcast the slots. */
+typedef struct murm_select_attend_bwd_args {
+  murm_phase_shape shape;
+  double scale;
+  const void* q; int64_t q_stride[3];
+  const void* slot_keys; int64_t sk_stride[3];
+  const void* slot_values; int64_t sv_stride[3];
+  const int64_t* indices; const float* weights;    /* the forward's outputs */
+  const void* grad_out; int64_t go_stride[3];
+  const float* grad_weights;                        /* optional [B,H,N,7] */
+  void* grad_q; int64_t gq_stride[3];
+  void* grad_slot_keys; int64_t gsk_stride[3];
+  void* grad_slot_values; int64_t gsv_stride[3];
+  void* workspace; size_t workspace_bytes;         /* murm_phase_sizes */
+} murm_select_attend_bwd_args;
+MURM_API murm_status murm_select_attend_bwd(const murm_select_attend_bwd_args* args, void* stream);
+
+/* Replaces slot_update (torch_binding.cpp:15-18; reference.py:71-115): per
+ * slot, the weight-summed token keys/values of the (token, pick) pairs that
+ * chose it, divided by (weight sum + 1e-8); slots with a positive weight sum
+ * take alpha * old + (1 - alpha) * mean, the others keep their value. `saved`
+ * keeps the means and weight sums for the backward. */
+typedef struct murm_slot_update_args {
+  murm_phase_shape shape;
+  double alpha;
+  const void* token_keys; int64_t tk_stride[3];
+  const void* token_values; int64_t tv_stride[3];
+  const void* slot_keys; int64_t sk_stride[3];
+  const void* slot_values; int64_t sv_stride[3];
+  const int64_t* indices; const float* weights;
+  void* new_slot_keys; int64_t nsk_stride[3];
+  void* new_slot_values; int64_t nsv_stride[3];
+  void* saved; size_t saved_bytes;                 /* murm_phase_sizes */
+  void* workspace; size_t workspace_bytes;
+} murm_slot_update_args;
+MURM_API murm_status murm_slot_update_fwd(const murm_slot_update_args* args, void* stream);
+
+/* Replaces slot_update_backward (torch_binding.cpp:19-21). */
+typedef struct murm_slot_update_bwd_args {
+  murm_phase_shape shape;
+  double alpha;
+  const void* token_keys; int64_t tk_stride[3];
+  const void* token_values; int64_t tv_stride[3];
+  const int64_t* indices; const float* weights;
+  const void* saved; size_t saved_bytes;           /* the forward's */
+  const void* grad_new_keys; int64_t gnk_stride[3];
+  const void* grad_new_values; int64_t gnv_stride[3];
+  void* grad_token_keys; int64_t gtk_stride[3];
+  void* grad_token_values; int64_t gtv_stride[3];
+  void* grad_slot_keys; int64_t gsk_stride[3];
+  void* grad_slot_values; int64_t gsv_stride[3];
+  float* grad_weights;                              /* [B,H,N,7] */
+  void* workspace; size_t workspace_bytes;
+} murm_slot_update_bwd_args;
+MURM_API murm_status murm_slot_update_bwd(const murm_slot_update_bwd_args* args, void* stream);
+
+/* Replaces slot_diffusion and its backward (torch_binding.cpp:22-27;
+ * reference.py:118-135): out[m] = x[m] + gamma (x[m-1] + x[m+1] - 2 x[m]) on
+ * the interior slots, boundaries unchanged; the backward applies the
+ * transposed stencil to the output gradients. Keys and values alike; `tokens`
+ * of the shape is ignored. */
+typedef struct murm_slot_diffusion_args {
+  murm_phase_shape shape;
+  double gamma;
+  const void* in_keys; int64_t ik_stride[3];
+  const void* in_values; int64_t iv_stride[3];
+  void* out_keys; int64_t ok_stride[3];
+  void* out_values; int64_t ov_stride[3];
+} murm_slot_diffusion_args;
+MURM_API murm_status murm_slot_diffusion_fwd(const murm_slot_diffusion_args* args, void* stream);
+MURM_API murm_status murm_slot_diffusion_bwd(const murm_slot_diffusion_args* args, void* stream);
+
+/* Byte sizes of slot_update's saved block and of the workspace every
+ * per-phase call above takes (one size fits all of them). */
+MURM_API murm_status murm_phase_sizes(const murm_phase_shape* shape, size_t* update_saved_bytes,
+                                      size_t* workspace_bytes);
+
 /* Launch accounting and per-kernel timing (host-side instrumentation; no
  * effect on results). murm_kernel_launches() counts every kernel this library
  * has launched in the process. Between murm_profile_begin() and

@@ -63,6 +63,88 @@ class BwdArgs(ctypes.Structure):
     ]
 
 
+Strides4 = ctypes.c_int64 * 4
+
+
+class PhaseShape(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("slots", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+class SelectAttendArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape), ("causal", ctypes.c_int32), ("effective_m", ctypes.c_int32),
+        ("scale", ctypes.c_double),
+        ("q", ctypes.c_void_p), ("q_stride", Strides),
+        ("slot_keys", ctypes.c_void_p), ("sk_stride", Strides),
+        ("slot_values", ctypes.c_void_p), ("sv_stride", Strides),
+        ("mask", ctypes.c_void_p), ("mask_stride", Strides4),
+        ("position_bias", ctypes.c_void_p), ("bias_stride", Strides4),
+        ("indices_in", ctypes.c_void_p),
+        ("out", ctypes.c_void_p), ("out_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+    ]
+
+
+class SelectAttendBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape), ("scale", ctypes.c_double),
+        ("q", ctypes.c_void_p), ("q_stride", Strides),
+        ("slot_keys", ctypes.c_void_p), ("sk_stride", Strides),
+        ("slot_values", ctypes.c_void_p), ("sv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+        ("grad_out", ctypes.c_void_p), ("go_stride", Strides),
+        ("grad_weights", ctypes.c_void_p),
+        ("grad_q", ctypes.c_void_p), ("gq_stride", Strides),
+        ("grad_slot_keys", ctypes.c_void_p), ("gsk_stride", Strides),
+        ("grad_slot_values", ctypes.c_void_p), ("gsv_stride", Strides),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class SlotUpdateArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape), ("alpha", ctypes.c_double),
+        ("token_keys", ctypes.c_void_p), ("tk_stride", Strides),
+        ("token_values", ctypes.c_void_p), ("tv_stride", Strides),
+        ("slot_keys", ctypes.c_void_p), ("sk_stride", Strides),
+        ("slot_values", ctypes.c_void_p), ("sv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+        ("new_slot_keys", ctypes.c_void_p), ("nsk_stride", Strides),
+        ("new_slot_values", ctypes.c_void_p), ("nsv_stride", Strides),
+        ("saved", ctypes.c_void_p), ("saved_bytes", ctypes.c_size_t),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class SlotUpdateBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape), ("alpha", ctypes.c_double),
+        ("token_keys", ctypes.c_void_p), ("tk_stride", Strides),
+        ("token_values", ctypes.c_void_p), ("tv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+        ("saved", ctypes.c_void_p), ("saved_bytes", ctypes.c_size_t),
+        ("grad_new_keys", ctypes.c_void_p), ("gnk_stride", Strides),
+        ("grad_new_values", ctypes.c_void_p), ("gnv_stride", Strides),
+        ("grad_token_keys", ctypes.c_void_p), ("gtk_stride", Strides),
+        ("grad_token_values", ctypes.c_void_p), ("gtv_stride", Strides),
+        ("grad_slot_keys", ctypes.c_void_p), ("gsk_stride", Strides),
+        ("grad_slot_values", ctypes.c_void_p), ("gsv_stride", Strides),
+        ("grad_weights", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class SlotDiffusionArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape), ("gamma", ctypes.c_double),
+        ("in_keys", ctypes.c_void_p), ("ik_stride", Strides),
+        ("in_values", ctypes.c_void_p), ("iv_stride", Strides),
+        ("out_keys", ctypes.c_void_p), ("ok_stride", Strides),
+        ("out_values", ctypes.c_void_p), ("ov_stride", Strides),
+    ]
+
+
 # Every symbol include/murm.h declares; tests check the library exports them all.
 EXPORTS = (
     "murm_slot_murmurate_sizes",
@@ -76,6 +158,13 @@ EXPORTS = (
     "murm_kernel_launches",
     "murm_profile_begin",
     "murm_profile_end",
+    "murm_phase_sizes",
+    "murm_select_attend_fwd",
+    "murm_select_attend_bwd",
+    "murm_slot_update_fwd",
+    "murm_slot_update_bwd",
+    "murm_slot_diffusion_fwd",
+    "murm_slot_diffusion_bwd",
 )
 
 STATUS_NAMES = {
@@ -122,6 +211,16 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_profile_begin.restype = ctypes.c_int
         lib.murm_profile_end.argtypes = [ctypes.POINTER(KernelTime), ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
         lib.murm_profile_end.restype = ctypes.c_int
+        lib.murm_phase_sizes.argtypes = [ctypes.POINTER(PhaseShape), ctypes.POINTER(ctypes.c_size_t),
+                                         ctypes.POINTER(ctypes.c_size_t)]
+        lib.murm_phase_sizes.restype = ctypes.c_int
+        for name, st in (("murm_select_attend_fwd", SelectAttendArgs), ("murm_select_attend_bwd", SelectAttendBwdArgs),
+                         ("murm_slot_update_fwd", SlotUpdateArgs), ("murm_slot_update_bwd", SlotUpdateBwdArgs),
+                         ("murm_slot_diffusion_fwd", SlotDiffusionArgs),
+                         ("murm_slot_diffusion_bwd", SlotDiffusionArgs)):
+            fn = getattr(lib, name)
+            fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
+            fn.restype = ctypes.c_int
         if lib.murm_abi_version() != 1:
             raise RuntimeError("murmurative_attention_b200: libmurm_b200.so ABI version mismatch; rebuild it")
         _lib = lib

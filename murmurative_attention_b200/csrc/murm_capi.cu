@@ -31,6 +31,16 @@ murm_status fail(murm_status s, const char* fmt, ...) {
   return s;
 }
 
+}  // namespace
+
+// The per-phase entry points (murm_ops.cu) report through the same message.
+murm_status report_error(murm_status s, const char* msg) {
+  g_last_error = msg;
+  return s;
+}
+
+namespace {
+
 constexpr int kSmCount = 148;  // B200; fixes the chunking so sizes() is device-independent
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }

@@ -36,6 +36,9 @@ struct BwdPtrs {
   void* gsv; Strides3 gsvs;
 };
 
+// Sets the calling thread's murm_last_error_message() (murm_capi.cu).
+murm_status report_error(murm_status s, const char* msg);
+
 // Launch accounting (murm_profile.cu). Every launch goes through MURM_LAUNCH.
 void launch_begin(const char* name, cudaStream_t st);
 void launch_end(cudaStream_t st);

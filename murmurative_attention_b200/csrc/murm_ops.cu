@@ -1,0 +1,806 @@
+// murm_ops.cu — per-phase operations of the reference's op surface (include/murm.h,
+// "Per-phase operations"): select+attend with mask / position bias / effective M,
+// slot update with separate token keys and values, slot diffusion, each with its
+// backward. General CUDA-core kernels (any head_dim that is a multiple of 8 up to
+// 128, M up to 1024); the fused round loop (murm_tc.cu, murm_simt.cu) remains the
+// fast path for the north-star operation.
+//
+// Semantics: reference.py:6-39 (select), 42-68 (attend), 71-115 (update),
+// 118-135 (diffusion). Slot sums are deterministic: the (token, pick) pairs are
+// sorted by slot with a stable counting sort (k_csr), then each slot sums its pairs
+// in token order; no floating-point atomics.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+
+#include "murm_kernels.cuh"
+
+namespace murm {
+namespace ph {
+
+constexpr int kMaxD = 128;
+constexpr int kMaxM = 1024;
+constexpr size_t kMaxStage = 200 * 1024;   // transposed fp32 key table per block
+constexpr int kTokPerWarp = 8;             // select+attend: tokens per warp
+constexpr int kWarps = 8;
+
+struct Dims {
+  int B, H, N, M, D;
+};
+
+__device__ __forceinline__ int clampi(int64_t v, int M) { return (int)(v < 0 ? 0 : (v >= M ? M - 1 : v)); }
+
+// 64-bit rank: larger = earlier in (score desc, slot asc); 0 = empty.
+__device__ __forceinline__ uint64_t rank64(uint32_t key, int slot) {
+  return ((uint64_t)key << 32) | (uint32_t)~slot;
+}
+__device__ __forceinline__ uint64_t mx64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+__device__ __forceinline__ uint64_t mn64(uint64_t a, uint64_t b) { return a > b ? b : a; }
+
+// Insert into a 7-entry list kept in rank order; offers must come in ascending slot
+// order (then equal keys never displace an earlier slot).
+__device__ __forceinline__ void offer7(uint32_t (&k)[kTopK], int (&s)[kTopK], uint32_t xk, int xs) {
+  bool gt[kTopK];
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) gt[j] = xk > k[j];
+#pragma unroll
+  for (int j = kTopK - 1; j >= 1; --j) {
+    k[j] = gt[j - 1] ? k[j - 1] : (gt[j] ? xk : k[j]);
+    s[j] = gt[j - 1] ? s[j - 1] : (gt[j] ? xs : s[j]);
+  }
+  k[0] = gt[0] ? xk : k[0];
+  s[0] = gt[0] ? xs : s[0];
+}
+
+// The warp's best 7 of all lanes' lists: butterfly of bitonic merges of 64-bit ranks.
+__device__ __forceinline__ void warp_top7(uint32_t (&k)[kTopK], int (&s)[kTopK]) {
+  uint64_t a[8];
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) a[j] = rank64(k[j], s[j]);
+  a[7] = 0;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    uint64_t b[8], c[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) b[j] = __shfl_xor_sync(0xffffffffu, a[j], o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = mx64(a[i], b[7 - i]);
+#pragma unroll
+    for (int st = 4; st >= 1; st >>= 1)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if ((i & st) == 0) {
+          const uint64_t x = c[i], y = c[i + st];
+          c[i] = mx64(x, y);
+          c[i + st] = mn64(x, y);
+        }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = c[j];
+    a[7] = 0;
+  }
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) {
+    k[j] = (uint32_t)(a[j] >> 32);
+    s[j] = (int)~(uint32_t)a[j];
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <typename T>
+__device__ __forceinline__ float ld(const void* base, int64_t i) {
+  return Elem<T>::load(static_cast<const T*>(base) + i);
+}
+template <typename T>
+__device__ __forceinline__ void st(void* base, int64_t i, float v) {
+  Elem<T>::store(static_cast<T*>(base) + i, v);
+}
+__device__ __forceinline__ int64_t off3(const int64_t* s, int b, int h, int r) {
+  return (int64_t)b * s[0] + (int64_t)h * s[1] + (int64_t)r * s[2];
+}
+__device__ __forceinline__ int64_t off4(const int64_t* s, int b, int h, int n, int m) {
+  return (int64_t)b * s[0] + (int64_t)h * s[1] + (int64_t)n * s[2] + (int64_t)m * s[3];
+}
+
+// ---------------------------------------------------------------------------
+// select + attend, forward. grid (ceil(N / 64), B*H), 8 warps, a warp per token.
+// Shared memory: the (b,h) key table transposed to [d][Mp] fp32 (lanes read
+// consecutive slots), and each warp's q row.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args a, int Mp) {
+  extern __shared__ float sh[];
+  const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
+  float* Kt = sh;                       // [D][Mp]
+  float* qs = sh + (size_t)D * Mp;      // [kWarps][D]
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < M * D; e += blockDim.x) {
+    const int m = e / D, d = e - m * D;
+    Kt[(size_t)d * Mp + m] = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+  }
+  __syncthreads();
+  const int em = (a.effective_m > 0 && a.effective_m < M) ? a.effective_m : M;
+  const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
+  float* q = qs + warp * D;
+  for (int tt = 0; tt < kTokPerWarp; ++tt) {
+    const int n = (blockIdx.x * kWarps + warp) * kTokPerWarp + tt;
+    if (n >= N) break;
+    for (int d = lane; d < D; d += 32) q[d] = ld<T>(a.q, off3(a.q_stride, b, h, n) + d);
+    __syncwarp();
+    const int64_t rec = ((int64_t)bh * N + n) * kTopK;
+    int pick[kTopK];
+    if (a.indices_in) {
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) pick[j] = clampi(a.indices_in[rec + j], M);
+    } else {
+      uint32_t tk[kTopK];
+      int ts[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
+      for (int m = lane; m < M; m += 32) {
+        float s = 0.f;
+        for (int d = 0; d < D; ++d) s = fmaf(q[d], Kt[(size_t)d * Mp + m], s);
+        if (a.position_bias) s += ld<T>(a.position_bias, off4(a.bias_stride, b, h, n, m));     // reference.py:21-22
+        bool masked = m >= em || (a.causal && m > n);                                            // :27-36
+        if (a.mask) masked = masked || a.mask[off4(a.mask_stride, b, h, n, m)] == 0;               // :24-25
+        offer7(tk, ts, rank_key(masked ? -INFINITY : s), m);
+      }
+      warp_top7(tk, ts);
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) pick[j] = ts[j];
+    }
+    // attend over the picks with the plain scaled scores (reference.py:58-66)
+    float sc[kTopK], mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      float p = 0.f;
+      for (int d = lane; d < D; d += 32) p = fmaf(q[d], Kt[(size_t)d * Mp + pick[j]], p);
+      sc[j] = warp_sum(p) * scale;
+      mx = fmaxf(mx, sc[j]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      sc[j] = expf(sc[j] - mx);
+      sum += sc[j];
+    }
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) sc[j] = sc[j] / sum;
+    for (int d = lane; d < D; d += 32) {
+      float o = 0.f;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) o = fmaf(sc[j], ld<T>(a.slot_values, off3(a.sv_stride, b, h, pick[j]) + d), o);
+      st<T>(a.out, off3(a.out_stride, b, h, n) + d, o);
+    }
+    if (lane < kTopK) {
+      int pj = pick[0];
+      float wj = sc[0];
+#pragma unroll
+      for (int j = 1; j < kTopK; ++j)
+        if (lane == j) { pj = pick[j]; wj = sc[j]; }
+      a.indices[rec + lane] = pj;
+      a.weights[rec + lane] = wj;
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Stable counting sort of the (token, pick) pairs of every (b,h) by slot:
+// offsets [BH][M+1], entries [BH][N*7] = token*8 + pick, ordered by slot, then
+// token, then pick. grid BH, 256 threads. A tile of `tile` tokens marks its pairs
+// in a per-slot bitmap; a pair's position is the slot's running count plus the
+// number of earlier pairs of the tile in that slot.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_csr(const int64_t* idx, int N, int M, int tile, int words, int* offsets,
+                                             int* entries) {
+  extern __shared__ uint32_t smu[];
+  int* run = reinterpret_cast<int*>(smu);       // [M]
+  uint32_t* bm = smu + M;                       // [M][words]
+  const int bh = blockIdx.x, tid = threadIdx.x;
+  const int64_t* ix = idx + (int64_t)bh * N * kTopK;
+  for (int m = tid; m < M; m += blockDim.x) run[m] = 0;
+  for (int e = tid; e < M * words; e += blockDim.x) bm[e] = 0u;
+  __syncthreads();
+  for (int e = tid; e < N * kTopK; e += blockDim.x) atomicAdd(&run[clampi(ix[e], M)], 1);
+  __syncthreads();
+  int* off = offsets + (int64_t)bh * (M + 1);
+  if (tid == 0) {
+    int acc = 0;
+    for (int m = 0; m < M; ++m) {
+      const int c = run[m];
+      off[m] = acc;
+      run[m] = acc;
+      acc += c;
+    }
+    off[M] = acc;
+  }
+  __syncthreads();
+  int* ent = entries + (int64_t)bh * N * kTopK;
+  for (int base = 0; base < N; base += tile) {
+    const int t = base + tid;
+    const bool live = tid < tile && t < N;
+    int mm[kTopK];
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        mm[j] = clampi(ix[(int64_t)t * kTopK + j], M);
+        const int p = tid * kTopK + j;
+        atomicOr(&bm[mm[j] * words + (p >> 5)], 1u << (p & 31));
+      }
+    }
+    __syncthreads();
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        const int p = tid * kTopK + j, w = p >> 5;
+        const uint32_t* row = bm + mm[j] * words;
+        int before = __popc(row[w] & ((1u << (p & 31)) - 1u)), after = __popc(row[w] >> (p & 31)) - 1;
+        for (int x = 0; x < w; ++x) before += __popc(row[x]);
+        for (int x = w + 1; x < words; ++x) after += __popc(row[x]);
+        ent[run[mm[j]] + before] = t * 8 + j;
+        mm[j] = (after == 0) ? ~(before + 1) : mm[j];  // the slot's last pair of the tile advances it
+      }
+    }
+    __syncthreads();
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        const int p = tid * kTopK + j;
+        const int m = clampi(ix[(int64_t)t * kTopK + j], M);
+        if (mm[j] < 0) run[m] += ~mm[j];
+        bm[m * words + (p >> 5)] = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// select + attend, backward, token side: a warp per token.
+//   dw_j = g . V[i_j] (+ grad_weights), da_j = w_j (dw_j - sum_k w_k dw_k),
+//   dq = scale sum_j da_j K[i_j]; coef[t][j] = scale da_j for the slot side.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args a, float* coef) {
+  const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  if (n >= N) return;
+  const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
+  const int64_t rec = ((int64_t)bh * N + n) * kTopK;
+  int pick[kTopK];
+  float w[kTopK], dw[kTopK];
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) {
+    pick[j] = clampi(a.indices[rec + j], M);
+    w[j] = a.weights[rec + j];
+  }
+  float g[kMaxD / 32];
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    g[u] = d < D ? ld<T>(a.grad_out, off3(a.go_stride, b, h, n) + d) : 0.f;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) {
+    float p = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxD / 32; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) p = fmaf(g[u], ld<T>(a.slot_values, off3(a.sv_stride, b, h, pick[j]) + d), p);
+    }
+    dw[j] = warp_sum(p) + (a.grad_weights ? a.grad_weights[rec + j] : 0.f);
+    s = fmaf(w[j], dw[j], s);
+  }
+  float c[kTopK];
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) c[j] = scale * (w[j] * (dw[j] - s));
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      float dq = 0.f;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) dq = fmaf(c[j], ld<T>(a.slot_keys, off3(a.sk_stride, b, h, pick[j]) + d), dq);
+      st<T>(a.grad_q, off3(a.gq_stride, b, h, n) + d, dq);
+    }
+  }
+  if (lane < kTopK) {
+    float cj = c[0];
+#pragma unroll
+    for (int j = 1; j < kTopK; ++j)
+      if (lane == j) cj = c[j];
+    coef[((int64_t)bh * N + n) * 8 + lane] = cj;
+  }
+}
+
+// slot side: a warp per (b,h, slot), its pairs in token order:
+//   dK[m] = sum coef * q[t],  dV[m] = sum w * g[t]
+template <typename T>
+__global__ void __launch_bounds__(256) k_sa_bwd_slot(murm_select_attend_bwd_args a, const float* coef,
+                                                     const int* offsets, const int* entries) {
+  const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp;
+  if (m >= M) return;
+  const int* off = offsets + (int64_t)bh * (M + 1);
+  const int* ent = entries + (int64_t)bh * N * kTopK;
+  float dk[kMaxD / 32], dv[kMaxD / 32];
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) dk[u] = dv[u] = 0.f;
+  for (int e = off[m]; e < off[m + 1]; ++e) {
+    const int t = ent[e] >> 3, j = ent[e] & 7;
+    const float cf = coef[((int64_t)bh * N + t) * 8 + j];
+    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
+#pragma unroll
+    for (int u = 0; u < kMaxD / 32; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        dk[u] = fmaf(cf, ld<T>(a.q, off3(a.q_stride, b, h, t) + d), dk[u]);
+        dv[u] = fmaf(wt, ld<T>(a.grad_out, off3(a.go_stride, b, h, t) + d), dv[u]);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      st<T>(a.grad_slot_keys, off3(a.gsk_stride, b, h, m) + d, dk[u]);
+      st<T>(a.grad_slot_values, off3(a.gsv_stride, b, h, m) + d, dv[u]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// slot update, forward: a warp per (b,h, slot). saved = U_k, U_v [BH][M][D] and
+// W [BH][M] (fp32).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const int* offsets, const int* entries,
+                                                 float* Uk, float* Uv, float* Wsum) {
+  const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp;
+  if (m >= M) return;
+  const int* off = offsets + (int64_t)bh * (M + 1);
+  const int* ent = entries + (int64_t)bh * N * kTopK;
+  float sk[kMaxD / 32], sv[kMaxD / 32];
+  float W = 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
+  for (int e = off[m]; e < off[m + 1]; ++e) {
+    const int t = ent[e] >> 3, j = ent[e] & 7;
+    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
+    W += wt;
+#pragma unroll
+    for (int u = 0; u < kMaxD / 32; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        sk[u] = fmaf(wt, ld<T>(a.token_keys, off3(a.tk_stride, b, h, t) + d), sk[u]);
+        sv[u] = fmaf(wt, ld<T>(a.token_values, off3(a.tv_stride, b, h, t) + d), sv[u]);
+      }
+    }
+  }
+  const bool valid = W > 0.f;                       // reference.py:105
+  const float den = __fadd_rn(W, kEmaEps);          // :106-107
+  const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
+  const size_t so = ((size_t)bh * M + m) * D;
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      const float uk = __fdiv_rn(sk[u], den), uv = __fdiv_rn(sv[u], den);
+      Uk[so + d] = uk;
+      Uv[so + d] = uv;
+      const float ok = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+      const float ov = ld<T>(a.slot_values, off3(a.sv_stride, b, h, m) + d);
+      // :112-113 alpha * old + (1 - alpha) * update where valid
+      st<T>(a.new_slot_keys, off3(a.nsk_stride, b, h, m) + d,
+            valid ? __fadd_rn(__fmul_rn(al, ok), __fmul_rn(om, uk)) : ok);
+      st<T>(a.new_slot_values, off3(a.nsv_stride, b, h, m) + d,
+            valid ? __fadd_rn(__fmul_rn(al, ov), __fmul_rn(om, uv)) : ov);
+    }
+  }
+  if (lane == 0) Wsum[(size_t)bh * M + m] = W;
+}
+
+// slot update, backward, slot side: grad of the old slots and the adjoints of the
+// sums: dks = (1-a) g_k / (W + eps), dW = -(dks . U_k + dvs . U_v), where W > 0.
+template <typename T>
+__global__ void __launch_bounds__(256) k_upd_bwd_slot(murm_slot_update_bwd_args a, const float* Uk, const float* Uv,
+                                                      const float* Wsum, float* dks, float* dvs, float* dW) {
+  const int D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp;
+  if (m >= M) return;
+  const float W = Wsum[(size_t)bh * M + m];
+  const bool valid = W > 0.f;
+  const float den = __fadd_rn(W, kEmaEps);
+  const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
+  const size_t so = ((size_t)bh * M + m) * D;
+  float dot = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float gk = ld<T>(a.grad_new_keys, off3(a.gnk_stride, b, h, m) + d);
+    const float gv = ld<T>(a.grad_new_values, off3(a.gnv_stride, b, h, m) + d);
+    st<T>(a.grad_slot_keys, off3(a.gsk_stride, b, h, m) + d, valid ? al * gk : gk);
+    st<T>(a.grad_slot_values, off3(a.gsv_stride, b, h, m) + d, valid ? al * gv : gv);
+    const float k2 = valid ? om * gk / den : 0.f, v2 = valid ? om * gv / den : 0.f;
+    dks[so + d] = k2;
+    dvs[so + d] = v2;
+    dot = fmaf(k2, Uk[so + d], fmaf(v2, Uv[so + d], dot));
+  }
+  dot = warp_sum(dot);
+  if (lane == 0) dW[(size_t)bh * M + m] = -dot;
+}
+
+// slot update, backward, token side: a warp per token.
+template <typename T>
+__global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a, const float* dks, const float* dvs,
+                                                     const float* dW) {
+  const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  if (n >= N) return;
+  const int64_t rec = ((int64_t)bh * N + n) * kTopK;
+  float tk[kMaxD / 32], tv[kMaxD / 32], gk[kMaxD / 32], gv[kMaxD / 32];
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    tk[u] = d < D ? ld<T>(a.token_keys, off3(a.tk_stride, b, h, n) + d) : 0.f;
+    tv[u] = d < D ? ld<T>(a.token_values, off3(a.tv_stride, b, h, n) + d) : 0.f;
+    gk[u] = gv[u] = 0.f;
+  }
+  float gw[kTopK];
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) {
+    const int m = clampi(a.indices[rec + j], M);
+    const float wt = a.weights[rec + j];
+    const size_t so = ((size_t)bh * M + m) * D;
+    float p = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxD / 32; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        const float k2 = dks[so + d], v2 = dvs[so + d];
+        gk[u] = fmaf(wt, k2, gk[u]);
+        gv[u] = fmaf(wt, v2, gv[u]);
+        p = fmaf(tk[u], k2, fmaf(tv[u], v2, p));
+      }
+    }
+    gw[j] = warp_sum(p) + dW[(size_t)bh * M + m];
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      st<T>(a.grad_token_keys, off3(a.gtk_stride, b, h, n) + d, gk[u]);
+      st<T>(a.grad_token_values, off3(a.gtv_stride, b, h, n) + d, gv[u]);
+    }
+  }
+  if (lane < kTopK) {
+    float x = gw[0];
+#pragma unroll
+    for (int j = 1; j < kTopK; ++j)
+      if (lane == j) x = gw[j];
+    a.grad_weights[rec + lane] = x;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// slot diffusion: grid (M, BH), a thread per head dim. Forward in the reference's
+// operation order (reference.py:128-133) with explicit roundings; backward is the
+// transposed stencil.
+// ---------------------------------------------------------------------------
+template <typename T, bool kBackward>
+__global__ void k_diffusion(murm_slot_diffusion_args a) {
+  const int M = a.shape.slots, D = a.shape.head_dim;
+  const int m = blockIdx.x, bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const float gm = (float)a.gamma;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const void* in = kv ? a.in_values : a.in_keys;
+      const int64_t* is = kv ? a.iv_stride : a.ik_stride;
+      void* out = kv ? a.out_values : a.out_keys;
+      const int64_t* os = kv ? a.ov_stride : a.ok_stride;
+      const float x = ld<T>(in, off3(is, b, h, m) + d);
+      float y;
+      if (!kBackward) {
+        y = x;
+        if (m > 0 && m < M - 1) {
+          const float l = ld<T>(in, off3(is, b, h, m - 1) + d), r = ld<T>(in, off3(is, b, h, m + 1) + d);
+          y = __fadd_rn(x, __fmul_rn(gm, __fsub_rn(__fadd_rn(l, r), __fmul_rn(2.f, x))));
+        }
+      } else {
+        const bool in_m = m > 0 && m < M - 1, in_l = m - 1 > 0, in_r = m + 1 < M - 1;
+        y = in_m ? __fadd_rn(x, __fmul_rn(-2.f * gm, x)) : x;
+        if (in_l) y = __fadd_rn(y, __fmul_rn(gm, ld<T>(in, off3(is, b, h, m - 1) + d)));
+        if (in_r) y = __fadd_rn(y, __fmul_rn(gm, ld<T>(in, off3(is, b, h, m + 1) + d)));
+      }
+      st<T>(out, off3(os, b, h, m) + d, y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct Sizes {
+  size_t saved, ws, off_csr_entries, off_coef, off_dks, off_dvs, off_dw;
+};
+inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Sizes sizes(const murm_phase_shape& s) {
+  const size_t BH = (size_t)s.batch * s.heads, N = s.tokens, M = s.slots, D = s.head_dim;
+  Sizes z;
+  z.saved = a256(BH * M * D * 4) * 2 + a256(BH * M * 4);
+  size_t o = a256(BH * (M + 1) * 4);  // offsets
+  z.off_csr_entries = o;
+  o += a256(BH * N * kTopK * 4);
+  z.off_coef = o;
+  o += a256(BH * N * 8 * 4);
+  z.off_dks = o;
+  o += a256(BH * M * D * 4);
+  z.off_dvs = o;
+  o += a256(BH * M * D * 4);
+  z.off_dw = o;
+  o += a256(BH * M * 4);
+  z.ws = o;
+  return z;
+}
+
+murm_status bad(murm_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+murm_status bad(murm_status s, const char* fmt, ...) {
+  char msg[256];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, sizeof(msg), fmt, ap);
+  va_end(ap);
+  return report_error(s, msg);
+}
+
+murm_status check(const murm_phase_shape& s) {
+  if (s.batch < 1 || s.heads < 1 || s.tokens < 1)
+    return bad(MURM_ERR_INVALID_ARGUMENT, "batch, heads and tokens must be >= 1");
+  if (s.slots < kTopK) return bad(MURM_ERR_INVALID_ARGUMENT, "slots=%d < top_k=%d", s.slots, kTopK);
+  if (s.slots > kMaxM) return bad(MURM_ERR_UNSUPPORTED, "slots=%d > %d not supported", s.slots, kMaxM);
+  if (s.head_dim < 8 || s.head_dim > kMaxD || s.head_dim % 8)
+    return bad(MURM_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 in [8, %d], got %d", kMaxD, s.head_dim);
+  if ((size_t)s.head_dim * (s.slots + 1) * 4 > kMaxStage)
+    return bad(MURM_ERR_UNSUPPORTED, "slots x head_dim too large (%d x %d)", s.slots, s.head_dim);
+  if (s.dtype < MURM_F32 || s.dtype > MURM_BF16) return bad(MURM_ERR_DTYPE, "unsupported dtype code %d", s.dtype);
+  if ((double)s.batch * s.heads * s.tokens * kTopK * 8 > 2147483647.0)
+    return bad(MURM_ERR_UNSUPPORTED, "batch*heads*tokens too large");
+  return MURM_OK;
+}
+
+murm_status launched(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return bad(MURM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return MURM_OK;
+}
+
+murm_status ws_ok(const murm_phase_shape& s, const void* ws, size_t bytes) {
+  if (!ws || bytes < sizes(s).ws || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return bad(MURM_ERR_WORKSPACE, "workspace NULL, unaligned or smaller than %zu bytes", sizes(s).ws);
+  return MURM_OK;
+}
+
+void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cudaStream_t st) {
+  const int M = s.slots;
+  const int tile = M <= 256 ? 256 : (M <= 512 ? 128 : 64);
+  const int words = (tile * kTopK + 31) / 32;
+  const size_t smem = (size_t)M * 4 + (size_t)M * words * 4;
+  cudaFuncSetAttribute(k_csr, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const Sizes z = sizes(s);
+  MURM_LAUNCH("phase_csr", k_csr, dim3(s.batch * s.heads), 256, smem, st, idx, s.tokens, M, tile, words,
+              reinterpret_cast<int*>(ws), reinterpret_cast<int*>(ws + z.off_csr_entries));
+}
+
+template <typename T>
+murm_status sa_fwd(const murm_select_attend_args& a, cudaStream_t st) {
+  const int Mp = ((a.shape.slots + 31) / 32) * 32 + 1;
+  const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
+  cudaFuncSetAttribute(k_sa_fwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const dim3 grid((a.shape.tokens + kWarps * kTokPerWarp - 1) / (kWarps * kTokPerWarp), a.shape.batch * a.shape.heads);
+  MURM_LAUNCH("phase_select_attend", k_sa_fwd<T>, grid, 32 * kWarps, smem, st, a, Mp);
+  return launched("select_attend forward");
+}
+
+template <typename T>
+murm_status sa_bwd(const murm_select_attend_bwd_args& a, cudaStream_t st) {
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  const Sizes z = sizes(a.shape);
+  const int BH = a.shape.batch * a.shape.heads;
+  launch_csr(a.shape, a.indices, ws, st);
+  float* coef = reinterpret_cast<float*>(ws + z.off_coef);
+  MURM_LAUNCH("phase_select_attend_bwd_tokens", k_sa_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a,
+              coef);
+  MURM_LAUNCH("phase_select_attend_bwd_slots", k_sa_bwd_slot<T>, dim3((a.shape.slots + 7) / 8, BH), 256, 0, st, a,
+              coef, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
+  return launched("select_attend backward");
+}
+
+template <typename T>
+murm_status upd_fwd(const murm_slot_update_args& a, cudaStream_t st) {
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  uint8_t* sv = static_cast<uint8_t*>(a.saved);
+  const Sizes z = sizes(a.shape);
+  const size_t BH = (size_t)a.shape.batch * a.shape.heads, MD = (size_t)a.shape.slots * a.shape.head_dim;
+  launch_csr(a.shape, a.indices, ws, st);
+  float* Uk = reinterpret_cast<float*>(sv);
+  float* Uv = reinterpret_cast<float*>(sv + a256(BH * MD * 4));
+  float* W = reinterpret_cast<float*>(sv + 2 * a256(BH * MD * 4));
+  MURM_LAUNCH("phase_update", k_upd_fwd<T>, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st, a,
+              reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries), Uk, Uv, W);
+  return launched("slot_update forward");
+}
+
+template <typename T>
+murm_status upd_bwd(const murm_slot_update_bwd_args& a, cudaStream_t st) {
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  const uint8_t* sv = static_cast<const uint8_t*>(a.saved);
+  const Sizes z = sizes(a.shape);
+  const size_t BH = (size_t)a.shape.batch * a.shape.heads, MD = (size_t)a.shape.slots * a.shape.head_dim;
+  const float* Uk = reinterpret_cast<const float*>(sv);
+  const float* Uv = reinterpret_cast<const float*>(sv + a256(BH * MD * 4));
+  const float* W = reinterpret_cast<const float*>(sv + 2 * a256(BH * MD * 4));
+  float* dks = reinterpret_cast<float*>(ws + z.off_dks);
+  float* dvs = reinterpret_cast<float*>(ws + z.off_dvs);
+  float* dW = reinterpret_cast<float*>(ws + z.off_dw);
+  MURM_LAUNCH("phase_update_bwd_slots", k_upd_bwd_slot<T>, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st,
+              a, Uk, Uv, W, dks, dvs, dW);
+  MURM_LAUNCH("phase_update_bwd_tokens", k_upd_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, (unsigned)BH), 256, 0, st,
+              a, dks, dvs, dW);
+  return launched("slot_update backward");
+}
+
+template <typename T>
+murm_status diff(const murm_slot_diffusion_args& a, bool backward, cudaStream_t st) {
+  const dim3 grid(a.shape.slots, a.shape.batch * a.shape.heads);
+  const int threads = a.shape.head_dim < 32 ? 32 : (a.shape.head_dim > 128 ? 128 : a.shape.head_dim);
+  auto kern = backward ? k_diffusion<T, true> : k_diffusion<T, false>;
+  MURM_LAUNCH(backward ? "phase_diffusion_bwd" : "phase_diffusion", kern, grid, threads, 0, st, a);
+  return launched("slot_diffusion");
+}
+
+template <template <typename> class F, typename A>
+murm_status dispatch(int dtype, const A& a, cudaStream_t st) {
+  switch (dtype) {
+    case MURM_F32: return F<float>::run(a, st);
+    case MURM_F16: return F<__half>::run(a, st);
+    case MURM_BF16: return F<__nv_bfloat16>::run(a, st);
+  }
+  return bad(MURM_ERR_DTYPE, "unsupported dtype code %d", dtype);
+}
+template <typename T> struct SaFwd { static murm_status run(const murm_select_attend_args& a, cudaStream_t s) { return sa_fwd<T>(a, s); } };
+template <typename T> struct SaBwd { static murm_status run(const murm_select_attend_bwd_args& a, cudaStream_t s) { return sa_bwd<T>(a, s); } };
+template <typename T> struct UpFwd { static murm_status run(const murm_slot_update_args& a, cudaStream_t s) { return upd_fwd<T>(a, s); } };
+template <typename T> struct UpBwd { static murm_status run(const murm_slot_update_bwd_args& a, cudaStream_t s) { return upd_bwd<T>(a, s); } };
+
+#define PH_REQUIRE(ptr, name) \
+  if (!(ptr)) return ::murm::ph::bad(MURM_ERR_INVALID_ARGUMENT, "%s is NULL", name)
+
+}  // namespace ph
+}  // namespace murm
+
+using namespace murm;
+
+extern "C" {
+
+MURM_API murm_status murm_phase_sizes(const murm_phase_shape* shape, size_t* update_saved_bytes,
+                                      size_t* workspace_bytes) {
+  if (!shape) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "shape is NULL");
+  if (murm_status s = ph::check(*shape)) return s;
+  const ph::Sizes z = ph::sizes(*shape);
+  if (update_saved_bytes) *update_saved_bytes = z.saved;
+  if (workspace_bytes) *workspace_bytes = z.ws;
+  return MURM_OK;
+}
+
+MURM_API murm_status murm_select_attend_fwd(const murm_select_attend_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->q, "q");
+  PH_REQUIRE(a->slot_keys, "slot_keys");
+  PH_REQUIRE(a->slot_values, "slot_values");
+  PH_REQUIRE(a->out, "out");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  if (!std::isfinite(a->scale)) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "scale must be finite");
+  return ph::dispatch<ph::SaFwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+MURM_API murm_status murm_select_attend_bwd(const murm_select_attend_bwd_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->q, "q");
+  PH_REQUIRE(a->slot_keys, "slot_keys");
+  PH_REQUIRE(a->slot_values, "slot_values");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  PH_REQUIRE(a->grad_out, "grad_out");
+  PH_REQUIRE(a->grad_q, "grad_q");
+  PH_REQUIRE(a->grad_slot_keys, "grad_slot_keys");
+  PH_REQUIRE(a->grad_slot_values, "grad_slot_values");
+  if (murm_status s = ph::ws_ok(a->shape, a->workspace, a->workspace_bytes)) return s;
+  return ph::dispatch<ph::SaBwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+MURM_API murm_status murm_slot_update_fwd(const murm_slot_update_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->token_keys, "token_keys");
+  PH_REQUIRE(a->token_values, "token_values");
+  PH_REQUIRE(a->slot_keys, "slot_keys");
+  PH_REQUIRE(a->slot_values, "slot_values");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  PH_REQUIRE(a->new_slot_keys, "new_slot_keys");
+  PH_REQUIRE(a->new_slot_values, "new_slot_values");
+  if (!a->saved || a->saved_bytes < ph::sizes(a->shape).saved || (reinterpret_cast<uintptr_t>(a->saved) & 255))
+    return ph::bad(MURM_ERR_WORKSPACE, "saved NULL, unaligned or smaller than %zu bytes", ph::sizes(a->shape).saved);
+  if (murm_status s = ph::ws_ok(a->shape, a->workspace, a->workspace_bytes)) return s;
+  if (!std::isfinite(a->alpha)) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "alpha must be finite");
+  return ph::dispatch<ph::UpFwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+MURM_API murm_status murm_slot_update_bwd(const murm_slot_update_bwd_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->token_keys, "token_keys");
+  PH_REQUIRE(a->token_values, "token_values");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  PH_REQUIRE(a->grad_new_keys, "grad_new_keys");
+  PH_REQUIRE(a->grad_new_values, "grad_new_values");
+  PH_REQUIRE(a->grad_token_keys, "grad_token_keys");
+  PH_REQUIRE(a->grad_token_values, "grad_token_values");
+  PH_REQUIRE(a->grad_slot_keys, "grad_slot_keys");
+  PH_REQUIRE(a->grad_slot_values, "grad_slot_values");
+  PH_REQUIRE(a->grad_weights, "grad_weights");
+  if (!a->saved || a->saved_bytes < ph::sizes(a->shape).saved)
+    return ph::bad(MURM_ERR_WORKSPACE, "saved NULL or smaller than %zu bytes", ph::sizes(a->shape).saved);
+  if (murm_status s = ph::ws_ok(a->shape, a->workspace, a->workspace_bytes)) return s;
+  return ph::dispatch<ph::UpBwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+static murm_status diffusion(const murm_slot_diffusion_args* a, bool backward, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  murm_phase_shape s = a->shape;
+  s.tokens = 1;
+  if (murm_status e = ph::check(s)) return e;
+  PH_REQUIRE(a->in_keys, "in_keys");
+  PH_REQUIRE(a->in_values, "in_values");
+  PH_REQUIRE(a->out_keys, "out_keys");
+  PH_REQUIRE(a->out_values, "out_values");
+  if (!std::isfinite(a->gamma)) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "gamma must be finite");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (a->shape.dtype) {
+    case MURM_F32: return ph::diff<float>(*a, backward, st);
+    case MURM_F16: return ph::diff<__half>(*a, backward, st);
+    case MURM_BF16: return ph::diff<__nv_bfloat16>(*a, backward, st);
+  }
+  return ph::bad(MURM_ERR_DTYPE, "unsupported dtype code %d", a->shape.dtype);
+}
+
+MURM_API murm_status murm_slot_diffusion_fwd(const murm_slot_diffusion_args* a, void* stream) {
+  return diffusion(a, false, stream);
+}
+MURM_API murm_status murm_slot_diffusion_bwd(const murm_slot_diffusion_args* a, void* stream) {
+  return diffusion(a, true, stream);
+}
+
+}  // extern "C"

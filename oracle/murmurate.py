@@ -180,6 +180,40 @@ def slot_murmurate(q, slots_k, slots_v, rounds: int = 3, top_k: int = 7, causal:
     return out, idx, w
 
 
+def slot_murmurate_full(x, q_proj, k_proj, v_proj, slot_k_emb, slot_v_emb, num_heads: int = 8,
+                        rounds: int = 3, alpha: float = 0.9, gamma: float = 0.15, causal: bool = False,
+                        mask=None, position_bias_fn=None, use_dynamic_m: bool = False,
+                        slot_ratio: int = 8, tie_rule: str = "lowest_index"):
+    """reference.py:138-191 (``slot_murmurate_reference``), the full op: separate token
+    keys and values, the residual stream x, an optional selection mask and position
+    bias (recomputed from the current x every round), and dynamic M. Inputs are used in
+    their own dtype, as the reference does; differentiable through autograd."""
+    B, N, D = x.shape
+    H = num_heads
+    if D % H != 0:                                                        # :157-160
+        raise ValueError(f"Embedding dimension D ({D}) must be divisible by num_heads ({H})")
+    Dh = D // H
+    x_h = x.view(B, N, H, Dh).permute(0, 2, 1, 3)                          # :163-166
+    q_h = q_proj.view(B, N, H, Dh).permute(0, 2, 1, 3)
+    k_h = k_proj.view(B, N, H, Dh).permute(0, 2, 1, 3)
+    v_h = v_proj.view(B, N, H, Dh).permute(0, 2, 1, 3)
+    M = slot_k_emb.shape[1]
+    slot_k = slot_k_emb.unsqueeze(0).expand(B, -1, -1, -1).contiguous()     # :169-170
+    slot_v = slot_v_emb.unsqueeze(0).expand(B, -1, -1, -1).contiguous()
+    effective_M = None
+    if use_dynamic_m:                                                      # :173-175
+        effective_M = min(M, max(32, (N + slot_ratio - 1) // slot_ratio))
+    for _ in range(rounds):                                                # :177-189
+        pos_bias = position_bias_fn(x_h) if position_bias_fn is not None else None
+        indices = slot_select(q_h, slot_k, mask=mask, causal=causal, position_bias=pos_bias,
+                              effective_M=effective_M, tie_rule=tie_rule)
+        attn_out, attn_w = slot_attend(q_h, slot_k, slot_v, indices)
+        x_h = x_h + attn_out
+        slot_k, slot_v = slot_update(k_h, v_h, slot_k, slot_v, indices, attn_w, alpha)
+        slot_k, slot_v = slot_diffusion(slot_k, slot_v, gamma)
+    return x_h.permute(0, 2, 1, 3).contiguous().view(B, N, D)              # :191
+
+
 @torch.no_grad()
 def slot_murmurate_trace(q, slots_k, slots_v, rounds: int = 3, causal: bool = False,
                          alpha: float = 0.9, gamma: float = 0.15,

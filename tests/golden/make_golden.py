@@ -185,6 +185,40 @@ def main(src):
     _save("phases", dict(tk=tk, tv=tv, slots_k=sk, slots_v=sv, idx=idx, w=w),
           dict(upd_k=nk, upd_v=nv, diff_k=dk, diff_v=dv), dict(alpha=0.9, gamma=0.1))
 
+    make_surface(ref)
+
+
+def surface_bias_fn(M: int):
+    """The position-bias function of the ``surface`` fixture (also used by the tests):
+    depends on the current residual stream, so it changes every round."""
+    ramp = torch.linspace(-1.0, 1.0, M)
+    return lambda xh: 0.1 * torch.tanh(xh[..., :1]) * ramp.to(xh.device, xh.dtype)
+
+
+def make_surface(ref):
+    """8. The full op surface (reference.py:138-191): residual x, separate q/k/v
+    projections, a selection mask, a position bias from x, dynamic M (N=64 -> 32 of
+    the 48 slots active), with gradients of every input. Every row keeps at least 8
+    selectable slots, so torch.topk has no ties to order."""
+    g = torch.Generator().manual_seed(8)
+    B, N, H, Dh, M = 2, 64, 2, 16, 48
+    x = _randn(g, B, N, H * Dh)
+    qp, kp, vp = (_randn(g, B, N, H * Dh) for _ in range(3))
+    ske = _randn(g, H, M, Dh)
+    sve = _randn(g, H, M, Dh, std=0.5)
+    mask = (torch.rand(N, M, generator=g) > 0.15).to(torch.uint8)
+    assert int(mask[:, :32].sum(-1).min()) >= 8
+    go = _randn(g, B, N, H * Dh)
+    leaves = [t.clone().requires_grad_(True) for t in (x, qp, kp, vp, ske, sve)]
+    out = ref.slot_murmurate_reference(*leaves, num_heads=H, rounds=3, mask=mask,
+                                       position_bias_fn=surface_bias_fn(M), use_dynamic_m=True)
+    (out * go).sum().backward()
+    names = ("x", "q_proj", "k_proj", "v_proj", "slot_k_emb", "slot_v_emb")
+    res = dict(out=out.detach(), **{"grad_" + n: t.grad for n, t in zip(names, leaves)})
+    _save("surface", dict(x=x, q_proj=qp, k_proj=kp, v_proj=vp, slot_k_emb=ske, slot_v_emb=sve,
+                          mask=mask.to(torch.int64), grad_out=go), res,
+          dict(rounds=3, heads=H, use_dynamic_m=1))
+
 
 if __name__ == "__main__":
     main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")

@@ -93,3 +93,52 @@ def test_status_strings():
     lib = _lib.load_library()
     for code in range(7):
         assert lib.murm_status_string(code)
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_phase_struct_layout_matches_header(tmp_path):
+    structs = [("murm_phase_shape", _lib.PhaseShape), ("murm_select_attend_args", _lib.SelectAttendArgs),
+               ("murm_select_attend_bwd_args", _lib.SelectAttendBwdArgs),
+               ("murm_slot_update_args", _lib.SlotUpdateArgs), ("murm_slot_update_bwd_args", _lib.SlotUpdateBwdArgs),
+               ("murm_slot_diffusion_args", _lib.SlotDiffusionArgs)]
+    fields = [("murm_select_attend_args", "indices_in", _lib.SelectAttendArgs),
+              ("murm_select_attend_args", "weights", _lib.SelectAttendArgs),
+              ("murm_select_attend_bwd_args", "workspace_bytes", _lib.SelectAttendBwdArgs),
+              ("murm_slot_update_args", "saved", _lib.SlotUpdateArgs),
+              ("murm_slot_update_bwd_args", "grad_weights", _lib.SlotUpdateBwdArgs),
+              ("murm_slot_diffusion_args", "out_values", _lib.SlotDiffusionArgs)]
+    body = "".join(f'printf("%zu ", sizeof({c}));' for c, _ in structs)
+    body += "".join(f'printf("%zu ", offsetof({c}, {f}));' for c, f, _ in fields)
+    src = tmp_path / "phase.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "murm.h"\nint main(void){' + body + "return 0;}\n")
+    exe = tmp_path / "phase"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    want = [ctypes.sizeof(s) for _, s in structs] + [getattr(s, f).offset for _, f, s in fields]
+    assert got == want
+
+
+def _phase_sizes(**kw):
+    base = dict(batch=2, heads=4, tokens=128, slots=256, head_dim=64, dtype=_lib.MURM_F16)
+    base.update(kw)
+    s = _lib.PhaseShape(**base)
+    a, b = ctypes.c_size_t(), ctypes.c_size_t()
+    st = _lib.load_library().murm_phase_sizes(ctypes.byref(s), ctypes.byref(a), ctypes.byref(b))
+    return st, a.value, b.value
+
+
+def test_phase_sizes_and_validation():
+    st, saved, ws = _phase_sizes()
+    assert st == 0 and saved > 0 and ws > 0
+    assert _phase_sizes(tokens=256)[2] > ws
+    assert _phase_sizes(head_dim=128, slots=384)[0] == 0      # general path: d up to 128, M beyond 256
+    for kw, status in [(dict(slots=6), 1), (dict(slots=2048), 2), (dict(head_dim=12), 2),
+                       (dict(head_dim=256), 2), (dict(dtype=9), 3), (dict(batch=0), 1)]:
+        assert _phase_sizes(**kw)[0] == status, kw
+
+
+def test_phase_null_args_rejected_without_gpu():
+    lib = _lib.load_library()
+    for name in ("murm_select_attend_fwd", "murm_select_attend_bwd", "murm_slot_update_fwd", "murm_slot_update_bwd",
+                 "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd"):
+        assert getattr(lib, name)(None, None) == 1, name

@@ -107,3 +107,27 @@ def test_row_gap_flags_near_ties():
     t = torch.tensor([[5.0, 4.0, 3.0, 2.0, 1.0, 0.5, 0.25, 0.1],
                       [5.0, 4.0, 3.0, 2.0, 1.0, 0.5, 0.25, 0.25 - 1e-7]])
     assert om.row_gap_ok(t).tolist() == [True, False]
+
+
+def surface_inputs():
+    """The ``surface`` fixture's inputs and its position-bias function."""
+    import sys
+    sys.path.insert(0, GOLDEN)
+    from make_golden import surface_bias_fn
+    f = load("surface")
+    names = ("x", "q_proj", "k_proj", "v_proj", "slot_k_emb", "slot_v_emb")
+    return f, names, surface_bias_fn(f["slot_k_emb"].shape[1])
+
+
+def test_oracle_full_surface_matches_reference():
+    """The full op (reference.py:138-191): residual x, separate token keys and values, a
+    mask, a position bias from x, dynamic M — output and every input gradient."""
+    f, names, bias_fn = surface_inputs()
+    leaves = [f[n].clone().requires_grad_(True) for n in names]
+    out = om.slot_murmurate_full(*leaves, num_heads=int(f["meta_heads"]), rounds=int(f["meta_rounds"]),
+                                 mask=f["mask"].to(torch.uint8), position_bias_fn=bias_fn,
+                                 use_dynamic_m=bool(int(f["meta_use_dynamic_m"])))
+    torch.testing.assert_close(out, f["out"], atol=1e-5, rtol=1e-5)
+    (out * f["grad_out"]).sum().backward()
+    for n, t in zip(names, leaves):
+        torch.testing.assert_close(t.grad, f["grad_" + n], atol=1e-5, rtol=1e-4, msg=n)
