@@ -509,6 +509,42 @@ def run_layer(args):
         dist.destroy_process_group()
 
 
+def run_surface(args):
+    """The reference's full op (ops.slot_murmurate, 6 arguments) on the north-star sizes:
+    B=1, N=8192, 16 heads of d=64 (D=1024), M=256, R=3, fp16, separate q/k/v projections,
+    residual x, a selection mask and a position bias; forward + backward through the
+    per-phase CUDA-core kernels (murm_ops.cu). One rank."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from murmurative_attention_b200 import functional as F
+    B, N, H, Dh, M = 1, 8192, 16, 64, 256
+    g = torch.Generator(device=dev).manual_seed(3000)
+    mk = lambda *s, std=1.0: (torch.randn(*s, device=dev, generator=g) * std).half().requires_grad_(True)
+    x, qp, kp, vp = (mk(B, N, H * Dh) for _ in range(4))
+    ske, sve = mk(H, M, Dh), mk(H, M, Dh, std=0.5)
+    mask = (torch.rand(N, M, device=dev, generator=g) > 0.1).to(torch.uint8)
+    ramp = torch.linspace(-1.0, 1.0, M, device=dev, dtype=torch.float16)
+    bias_fn = lambda xh: 0.1 * torch.tanh(xh[..., :1]) * ramp
+    go = torch.randn(B, N, H * Dh, device=dev, generator=g).half()
+
+    def step():
+        out = F.slot_murmurate(x, qp, kp, vp, ske, sve, num_heads=H, rounds=3, mask=mask, position_bias_fn=bias_fn)
+        out.backward(go)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    times = time_steps(step, args.steps, flush)
+    ms = sum(times) / args.steps
+    line = {"metric": "ops.slot_murmurate (6-argument op surface) fwd+bwd tokens/s", "value": round(B * N / (ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "op surface: x, q/k/v projections [1,8192,1024], slot embeddings [16,256,64], "
+                                   "mask [8192,256] (90% kept), position bias from x, dynamic M, R=3",
+                       "path": "per-phase CUDA-core kernels (murm_ops.cu)"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,16 +554,17 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=("northstar", "layer"), default="northstar",
-                    help="layer: BASELINE configs[3], the data-parallel layer training step")
+    ap.add_argument("--workload", choices=("northstar", "layer", "surface"), default="northstar",
+                    help="layer: BASELINE configs[3], the data-parallel layer training step; "
+                         "surface: the reference's 6-argument op through the per-phase kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "layer":
+    if args.workload in ("layer", "surface"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the layer workload has no reference arm here"}))
+            print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference arm here"}))
             return
-        run_layer(args)
+        (run_layer if args.workload == "layer" else run_surface)(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
