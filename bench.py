@@ -545,6 +545,40 @@ def run_surface(args):
     print(json.dumps(line), flush=True)
 
 
+def run_decode(args):
+    """Streaming decode (the reference's decode plan): 16 sequences x 16 heads of d=64,
+    M=256 resident slots, fp16, one token per sequence per step through murm_decode_step,
+    the step replayed from a CUDA graph. tokens/s = sequences / step time."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from murmurative_attention_b200.decode import SlotPool
+    B, H, M, D = 16, 16, 256, 64
+    g = torch.Generator(device=dev).manual_seed(4000)
+    ske = torch.randn(H, M, D, device=dev, generator=g).half()
+    sve = (torch.randn(H, M, D, device=dev, generator=g) * 0.5).half()
+    pool = SlotPool.from_embeddings(ske, sve, B)
+    pool.positions.fill_(4096)
+    q, k, v, x = (torch.randn(B, H * D, device=dev, generator=g).half() for _ in range(4))
+    for _ in range(args.warmup):
+        pool.step(q, k, v, x, causal=True)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        pool.step(q, k, v, x, causal=True)
+    graph.replay()
+    torch.cuda.synchronize()
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    times = time_steps(graph.replay, args.steps, flush)
+    ms = sum(times) / args.steps
+    line = {"metric": "streaming decode tokens/s (one token per sequence per step)", "value": round(B / (ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "decode: 16 sequences x 16 heads, d=64, M=256 resident slots, causal, one launch per step",
+                       "pool_bytes_per_step": 2 * 2 * B * H * M * D * 2,
+                       "l2": "flushed by a 256 MiB write before every timed step"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -554,17 +588,18 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=("northstar", "layer", "surface"), default="northstar",
+    ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode"), default="northstar",
                     help="layer: BASELINE configs[3], the data-parallel layer training step; "
-                         "surface: the reference's 6-argument op through the per-phase kernels")
+                         "surface: the reference's 6-argument op through the per-phase kernels; "
+                         "decode: the streaming decode step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in ("layer", "surface"):
+    if args.workload != "northstar":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference arm here"}))
             return
-        (run_layer if args.workload == "layer" else run_surface)(args)
+        {"layer": run_layer, "surface": run_surface, "decode": run_decode}[args.workload](args)
     elif args.impl == "reference":
         run_reference(args)
     else:

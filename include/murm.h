@@ -258,6 +258,32 @@ typedef struct murm_slot_diffusion_args {
 MURM_API murm_status murm_slot_diffusion_fwd(const murm_slot_diffusion_args* args, void* stream);
 MURM_API murm_status murm_slot_diffusion_bwd(const murm_slot_diffusion_args* args, void* stream);
 
+/* Streaming decode step (the reference's decode plan,
+ * docs/murmurative-attention-kernel-plan.md:154-173; no counterpart in its code):
+ * one new token per (batch, head) against a resident slot pool that is updated
+ * in place. Select (top-7 of q . slot_keys, slots above the token's absolute
+ * position masked when causal), attend (softmax of scale * q.k over the picks),
+ * out = x + attend, then update the picked slots with the token's key/value
+ * (reference.py:71-115 with one token) and diffuse the whole pool
+ * (reference.py:118-135). O(M * head_dim) per token and head; one launch.
+ * Slots live in the pool's dtype between steps (as type_as does in the
+ * reference). M * (head_dim + 1) * 8 bytes must fit in 200 KiB. */
+typedef struct murm_decode_args {
+  int32_t batch, heads, slots, head_dim, dtype;
+  int32_t causal;
+  const int64_t* positions;                  /* [batch] absolute positions; required when causal */
+  double alpha, gamma, scale;                /* scale <= 0: 1/sqrt(head_dim) */
+  const void* q; int64_t q_stride[2];        /* [B, H, d], strides {batch, head} */
+  const void* k; int64_t k_stride[2];
+  const void* v; int64_t v_stride[2];
+  const void* x; int64_t x_stride[2];        /* optional residual; NULL = 0 */
+  void* out; int64_t out_stride[2];
+  void* slot_keys; int64_t sk_stride[3];     /* pool [B, H, M, d], read and written */
+  void* slot_values; int64_t sv_stride[3];
+  int64_t* indices; float* weights;          /* [B, H, 7], optional */
+} murm_decode_args;
+MURM_API murm_status murm_decode_step(const murm_decode_args* args, void* stream);
+
 /* Byte sizes of slot_update's saved block and of the workspace every
  * per-phase call above takes (one size fits all of them). */
 MURM_API murm_status murm_phase_sizes(const murm_phase_shape* shape, size_t* update_saved_bytes,

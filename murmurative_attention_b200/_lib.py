@@ -145,6 +145,26 @@ class SlotDiffusionArgs(ctypes.Structure):
     ]
 
 
+Strides2 = ctypes.c_int64 * 2
+
+
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("slots", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32),
+        ("positions", ctypes.c_void_p),
+        ("alpha", ctypes.c_double), ("gamma", ctypes.c_double), ("scale", ctypes.c_double),
+        ("q", ctypes.c_void_p), ("q_stride", Strides2),
+        ("k", ctypes.c_void_p), ("k_stride", Strides2),
+        ("v", ctypes.c_void_p), ("v_stride", Strides2),
+        ("x", ctypes.c_void_p), ("x_stride", Strides2),
+        ("out", ctypes.c_void_p), ("out_stride", Strides2),
+        ("slot_keys", ctypes.c_void_p), ("sk_stride", Strides),
+        ("slot_values", ctypes.c_void_p), ("sv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+    ]
+
+
 # Every symbol include/murm.h declares; tests check the library exports them all.
 EXPORTS = (
     "murm_slot_murmurate_sizes",
@@ -165,6 +185,7 @@ EXPORTS = (
     "murm_slot_update_bwd",
     "murm_slot_diffusion_fwd",
     "murm_slot_diffusion_bwd",
+    "murm_decode_step",
 )
 
 STATUS_NAMES = {
@@ -217,7 +238,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         for name, st in (("murm_select_attend_fwd", SelectAttendArgs), ("murm_select_attend_bwd", SelectAttendBwdArgs),
                          ("murm_slot_update_fwd", SlotUpdateArgs), ("murm_slot_update_bwd", SlotUpdateBwdArgs),
                          ("murm_slot_diffusion_fwd", SlotDiffusionArgs),
-                         ("murm_slot_diffusion_bwd", SlotDiffusionArgs)):
+                         ("murm_slot_diffusion_bwd", SlotDiffusionArgs), ("murm_decode_step", DecodeArgs)):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
             fn.restype = ctypes.c_int

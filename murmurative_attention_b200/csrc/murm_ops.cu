@@ -535,6 +535,125 @@ __global__ void k_diffusion(murm_slot_diffusion_args a) {
 }
 
 // ---------------------------------------------------------------------------
+// Streaming decode: one CTA per (b,h), 256 threads. The pool is staged in shared
+// memory as fp32 rows of d+1 words (odd stride: a thread per slot row reads
+// without bank conflicts); the 7 picked rows are updated there, rounded to the
+// pool's dtype (the reference's type_as), and the diffused pool is written back.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_decode(murm_decode_args a) {
+  extern __shared__ float sm[];
+  const int M = a.slots, D = a.head_dim, Dp = D + 1;
+  float* sK = sm;                          // [M][Dp]
+  float* sV = sK + (size_t)M * Dp;         // [M][Dp]
+  float* qv = sV + (size_t)M * Dp;         // [D]
+  float* kv = qv + D;                      // [D] token key
+  float* vv = kv + D;                      // [D] token value
+  uint32_t* keys = reinterpret_cast<uint32_t*>(vv + D);  // [M]
+  int* pick_s = reinterpret_cast<int*>(keys + M);        // [8]
+  float* w_s = reinterpret_cast<float*>(pick_s + 8);     // [8]
+  const int bh = blockIdx.x, b = bh / a.heads, h = bh - b * a.heads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < M * D; e += blockDim.x) {
+    const int m = e / D, d = e - m * D;
+    sK[m * Dp + d] = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+    sV[m * Dp + d] = ld<T>(a.slot_values, off3(a.sv_stride, b, h, m) + d);
+  }
+  const int64_t qo = (int64_t)b * a.q_stride[0] + (int64_t)h * a.q_stride[1];
+  const int64_t ko = (int64_t)b * a.k_stride[0] + (int64_t)h * a.k_stride[1];
+  const int64_t vo = (int64_t)b * a.v_stride[0] + (int64_t)h * a.v_stride[1];
+  for (int d = tid; d < D; d += blockDim.x) {
+    qv[d] = ld<T>(a.q, qo + d);
+    kv[d] = ld<T>(a.k, ko + d);
+    vv[d] = ld<T>(a.v, vo + d);
+  }
+  __syncthreads();
+  const int64_t pos = a.causal ? a.positions[b] : 0;
+  for (int m = tid; m < M; m += blockDim.x) {  // selection scores (reference.py:19, 27-31)
+    float s = 0.f;
+    for (int d = 0; d < D; ++d) s = fmaf(qv[d], sK[m * Dp + d], s);
+    keys[m] = rank_key((a.causal && m > pos) ? -INFINITY : s);
+  }
+  __syncthreads();
+  const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
+  if (warp == 0) {
+    uint32_t tk[kTopK];
+    int ts[kTopK];
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
+    for (int m = lane; m < M; m += 32) offer7(tk, ts, keys[m], m);
+    warp_top7(tk, ts);
+    float sc[kTopK], mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {  // attend scores without the mask (reference.py:61)
+      float p = 0.f;
+      for (int d = lane; d < D; d += 32) p = fmaf(qv[d], sK[ts[j] * Dp + d], p);
+      sc[j] = warp_sum(p) * scale;
+      mx = fmaxf(mx, sc[j]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      sc[j] = expf(sc[j] - mx);
+      sum += sc[j];
+    }
+    if (lane < kTopK) {
+      int pj = ts[0];
+      float wj = sc[0];
+#pragma unroll
+      for (int j = 1; j < kTopK; ++j)
+        if (lane == j) { pj = ts[j]; wj = sc[j]; }
+      wj = wj / sum;
+      pick_s[lane] = pj;
+      w_s[lane] = wj;
+      if (a.indices) a.indices[(int64_t)bh * kTopK + lane] = pj;
+      if (a.weights) a.weights[(int64_t)bh * kTopK + lane] = wj;
+    }
+  }
+  __syncthreads();
+  // out = x + sum_j w_j V[i_j] (with the values before this token's update)
+  const int64_t oo = (int64_t)b * a.out_stride[0] + (int64_t)h * a.out_stride[1];
+  const int64_t xo = a.x ? (int64_t)b * a.x_stride[0] + (int64_t)h * a.x_stride[1] : 0;
+  for (int d = tid; d < D; d += blockDim.x) {
+    float o = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) o = fmaf(w_s[j], sV[pick_s[j] * Dp + d], o);
+    st<T>(a.out, oo + d, (a.x ? ld<T>(a.x, xo + d) : 0.f) + o);
+  }
+  __syncthreads();
+  // update of the picked (distinct) slots with this one token (reference.py:93-115)
+  const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
+  for (int e = tid; e < kTopK * D; e += blockDim.x) {
+    const int j = e / D, d = e - j * D, m = pick_s[j];
+    const float wj = w_s[j];
+    if (wj > 0.f) {
+      const float den = __fadd_rn(wj, kEmaEps);
+      const float uk = __fdiv_rn(__fmul_rn(kv[d], wj), den), uv = __fdiv_rn(__fmul_rn(vv[d], wj), den);
+      T rk, rv;
+      Elem<T>::store(&rk, __fadd_rn(__fmul_rn(al, sK[m * Dp + d]), __fmul_rn(om, uk)));
+      Elem<T>::store(&rv, __fadd_rn(__fmul_rn(al, sV[m * Dp + d]), __fmul_rn(om, uv)));
+      sK[m * Dp + d] = Elem<T>::load(&rk);
+      sV[m * Dp + d] = Elem<T>::load(&rv);
+    }
+  }
+  __syncthreads();
+  // diffusion of the whole pool, written back (reference.py:128-133)
+  const float gm = (float)a.gamma;
+  for (int e = tid; e < M * D; e += blockDim.x) {
+    const int m = e / D, d = e - m * D;
+    float k = sK[m * Dp + d], v = sV[m * Dp + d];
+    if (m > 0 && m < M - 1) {
+      k = __fadd_rn(k, __fmul_rn(gm, __fsub_rn(__fadd_rn(sK[(m - 1) * Dp + d], sK[(m + 1) * Dp + d]),
+                                                __fmul_rn(2.f, k))));
+      v = __fadd_rn(v, __fmul_rn(gm, __fsub_rn(__fadd_rn(sV[(m - 1) * Dp + d], sV[(m + 1) * Dp + d]),
+                                                __fmul_rn(2.f, v))));
+    }
+    st<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d, k);
+    st<T>(a.slot_values, off3(a.sv_stride, b, h, m) + d, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct Sizes {
@@ -801,6 +920,37 @@ MURM_API murm_status murm_slot_diffusion_fwd(const murm_slot_diffusion_args* a, 
 }
 MURM_API murm_status murm_slot_diffusion_bwd(const murm_slot_diffusion_args* a, void* stream) {
   return diffusion(a, true, stream);
+}
+
+MURM_API murm_status murm_decode_step(const murm_decode_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  murm_phase_shape s{a->batch, a->heads, 1, a->slots, a->head_dim, a->dtype};
+  if (murm_status e = ph::check(s)) return e;
+  const size_t smem = (size_t)a->slots * (a->head_dim + 1) * 8 + (size_t)a->head_dim * 12 + (size_t)a->slots * 4 + 64;
+  if (smem > ph::kMaxStage)
+    return ph::bad(MURM_ERR_UNSUPPORTED, "decode pool too large for shared memory (%d slots x %d)", a->slots,
+                   a->head_dim);
+  PH_REQUIRE(a->q, "q");
+  PH_REQUIRE(a->k, "k");
+  PH_REQUIRE(a->v, "v");
+  PH_REQUIRE(a->out, "out");
+  PH_REQUIRE(a->slot_keys, "slot_keys");
+  PH_REQUIRE(a->slot_values, "slot_values");
+  if (a->causal) PH_REQUIRE(a->positions, "positions");
+  if (!std::isfinite(a->alpha) || !std::isfinite(a->gamma) || !std::isfinite(a->scale))
+    return ph::bad(MURM_ERR_INVALID_ARGUMENT, "alpha, gamma and scale must be finite");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    MURM_LAUNCH("decode_step", kern, dim3(a->batch * a->heads), 256, smem, st, *a);
+    return ph::launched("decode step");
+  };
+  switch (a->dtype) {
+    case MURM_F32: return go(ph::k_decode<float>);
+    case MURM_F16: return go(ph::k_decode<__half>);
+    case MURM_BF16: return go(ph::k_decode<__nv_bfloat16>);
+  }
+  return ph::bad(MURM_ERR_DTYPE, "unsupported dtype code %d", a->dtype);
 }
 
 }  // extern "C"

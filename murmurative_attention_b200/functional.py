@@ -294,11 +294,13 @@ def slot_murmurate(x: torch.Tensor, q_proj: torch.Tensor, k_proj: torch.Tensor, 
                    mask: Optional[torch.Tensor] = None,
                    position_bias_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
                    use_dynamic_m: bool = True, slot_ratio: int = 8,
-                   use_fused_update_diffuse: bool = True) -> torch.Tensor:
+                   use_fused_update_diffuse: bool = True, return_slots: bool = False):
     """The reference's full round loop (ops.py:330-422): x, q/k/v projections [B, N, D],
     per-head slot embeddings [H, M, D/H] -> x + the rounds' attend outputs, [B, N, D].
     ``use_fused_update_diffuse`` is accepted for signature compatibility (update and
-    diffusion are separate kernels here with identical results)."""
+    diffusion are separate kernels here with identical results). With ``return_slots``
+    the final slot tables [B, H, M, D/H] are returned too, ``(out, slot_k, slot_v)``: the
+    prefill of a streaming decode (murmurative_attention_b200.decode)."""
     B, N, D = x.shape
     H = num_heads
     if D % H != 0:
@@ -321,4 +323,5 @@ def slot_murmurate(x: torch.Tensor, q_proj: torch.Tensor, k_proj: torch.Tensor, 
         x_h = x_h + attn_out
         slot_k, slot_v = _SlotUpdate.apply(k_h, v_h, slot_k, slot_v, indices, attn_w, alpha)
         slot_k, slot_v = _SlotDiffusion.apply(slot_k, slot_v, gamma)
-    return x_h.permute(0, 2, 1, 3).contiguous().view(B, N, D)
+    out = x_h.permute(0, 2, 1, 3).contiguous().view(B, N, D)
+    return (out, slot_k, slot_v) if return_slots else out

@@ -100,13 +100,14 @@ def test_phase_struct_layout_matches_header(tmp_path):
     structs = [("murm_phase_shape", _lib.PhaseShape), ("murm_select_attend_args", _lib.SelectAttendArgs),
                ("murm_select_attend_bwd_args", _lib.SelectAttendBwdArgs),
                ("murm_slot_update_args", _lib.SlotUpdateArgs), ("murm_slot_update_bwd_args", _lib.SlotUpdateBwdArgs),
-               ("murm_slot_diffusion_args", _lib.SlotDiffusionArgs)]
+               ("murm_slot_diffusion_args", _lib.SlotDiffusionArgs), ("murm_decode_args", _lib.DecodeArgs)]
     fields = [("murm_select_attend_args", "indices_in", _lib.SelectAttendArgs),
               ("murm_select_attend_args", "weights", _lib.SelectAttendArgs),
               ("murm_select_attend_bwd_args", "workspace_bytes", _lib.SelectAttendBwdArgs),
               ("murm_slot_update_args", "saved", _lib.SlotUpdateArgs),
               ("murm_slot_update_bwd_args", "grad_weights", _lib.SlotUpdateBwdArgs),
-              ("murm_slot_diffusion_args", "out_values", _lib.SlotDiffusionArgs)]
+              ("murm_slot_diffusion_args", "out_values", _lib.SlotDiffusionArgs),
+              ("murm_decode_args", "positions", _lib.DecodeArgs), ("murm_decode_args", "weights", _lib.DecodeArgs)]
     body = "".join(f'printf("%zu ", sizeof({c}));' for c, _ in structs)
     body += "".join(f'printf("%zu ", offsetof({c}, {f}));' for c, f, _ in fields)
     src = tmp_path / "phase.c"
@@ -140,5 +141,5 @@ def test_phase_sizes_and_validation():
 def test_phase_null_args_rejected_without_gpu():
     lib = _lib.load_library()
     for name in ("murm_select_attend_fwd", "murm_select_attend_bwd", "murm_slot_update_fwd", "murm_slot_update_bwd",
-                 "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd"):
+                 "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd", "murm_decode_step"):
         assert getattr(lib, name)(None, None) == 1, name
