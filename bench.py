@@ -579,6 +579,56 @@ def run_decode(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sp(args):
+    """Sequence parallelism (sequence_parallel.slot_murmurate_sp) for a long context with
+    few (batch, head) pairs: B=1, H=2, N=65536, d=64, M=256, R=3, fp16, causal; the
+    tokens are split over the ranks (strong scaling), one NCCL all-reduce of the slot sums
+    per round. Forward + backward (+ the slot-gradient all-reduce)."""
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from murmurative_attention_b200.sequence_parallel import slot_murmurate_sp
+    import torch.distributed as dist
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    B, H, N, D, M = 1, 2, 65536, 64, 256
+    n = N // world
+    g = torch.Generator(device=dev).manual_seed(5000)
+    q = torch.randn(B, H, N, D, device=dev, generator=g).half()[:, :, rank * n:(rank + 1) * n].contiguous()
+    sk = torch.randn(B, H, M, D, device=dev, generator=g).half()
+    sv = torch.zeros(B, H, M, D, device=dev, dtype=torch.float16)
+    go = torch.randn(B, H, n, D, device=dev, generator=g).half()
+    qd, skd, svd = (t.clone().requires_grad_(True) for t in (q, sk, sv))
+
+    def step():
+        out, _, _ = slot_murmurate_sp(qd, skd, svd, rounds=3, causal=True)
+        out.backward(go)
+        if world > 1:
+            dist.all_reduce(skd.grad)
+            dist.all_reduce(svd.grad)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(step, args.steps, flush)
+    barrier(world)
+    total_ms = max_over_ranks(sum(times), world)
+    ms = total_ms / args.steps
+    if rank == 0:
+        line = {"metric": "sequence-parallel slot_murmurate fwd+bwd tokens/s (long context, few (b,h))",
+                "value": round(B * H * N / (ms / 1e3), 1), "unit": "(b,h)-tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": "sp: B=1, H=2, N=65536 split over the ranks, d=64, M=256, R=3, causal",
+                           "path": "per-phase kernels + one NCCL all-reduce of the slot sums per round",
+                           "parallelism": f"sp{world}"}}
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -588,10 +638,10 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode"), default="northstar",
+    ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode", "sp"), default="northstar",
                     help="layer: BASELINE configs[3], the data-parallel layer training step; "
                          "surface: the reference's 6-argument op through the per-phase kernels; "
-                         "decode: the streaming decode step")
+                         "decode: the streaming decode step; sp: sequence parallelism over the tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -599,7 +649,7 @@ def main():
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference arm here"}))
             return
-        {"layer": run_layer, "surface": run_surface, "decode": run_decode}[args.workload](args)
+        {"layer": run_layer, "surface": run_surface, "decode": run_decode, "sp": run_sp}[args.workload](args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -242,6 +242,35 @@ typedef struct murm_slot_update_bwd_args {
 } murm_slot_update_bwd_args;
 MURM_API murm_status murm_slot_update_bwd(const murm_slot_update_bwd_args* args, void* stream);
 
+/* The first half of slot_update alone: per slot, the weight-summed token keys
+ * and values and the weight sum of the (token, pick) pairs that chose it
+ * (reference.py:87-103), fp32, contiguous [B,H,M,d] / [B,H,M,d] / [B,H,M]. Sums
+ * over token shards add up, so sequence-parallel callers all-reduce these and
+ * finish the EMA on the totals. No counterpart in the reference's op schemas. */
+typedef struct murm_slot_sums_args {
+  murm_phase_shape shape;
+  const void* token_keys; int64_t tk_stride[3];
+  const void* token_values; int64_t tv_stride[3];
+  const int64_t* indices; const float* weights;
+  float* key_sums; float* value_sums; float* weight_sums;
+  void* workspace; size_t workspace_bytes;
+} murm_slot_sums_args;
+MURM_API murm_status murm_slot_sums_fwd(const murm_slot_sums_args* args, void* stream);
+
+/* Backward of murm_slot_sums_fwd: token-key/value and weight gradients from the
+ * sums' gradients (fp32 contiguous, like the forward's outputs). */
+typedef struct murm_slot_sums_bwd_args {
+  murm_phase_shape shape;
+  const void* token_keys; int64_t tk_stride[3];
+  const void* token_values; int64_t tv_stride[3];
+  const int64_t* indices; const float* weights;
+  const float* grad_key_sums; const float* grad_value_sums; const float* grad_weight_sums;
+  void* grad_token_keys; int64_t gtk_stride[3];
+  void* grad_token_values; int64_t gtv_stride[3];
+  float* grad_weights;
+} murm_slot_sums_bwd_args;
+MURM_API murm_status murm_slot_sums_bwd(const murm_slot_sums_bwd_args* args, void* stream);
+
 /* Replaces slot_diffusion and its backward (torch_binding.cpp:22-27;
  * reference.py:118-135): out[m] = x[m] + gamma (x[m-1] + x[m+1] - 2 x[m]) on
  * the interior slots, boundaries unchanged; the backward applies the

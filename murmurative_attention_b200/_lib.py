@@ -145,6 +145,31 @@ class SlotDiffusionArgs(ctypes.Structure):
     ]
 
 
+class SlotSumsArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape),
+        ("token_keys", ctypes.c_void_p), ("tk_stride", Strides),
+        ("token_values", ctypes.c_void_p), ("tv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+        ("key_sums", ctypes.c_void_p), ("value_sums", ctypes.c_void_p), ("weight_sums", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class SlotSumsBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", PhaseShape),
+        ("token_keys", ctypes.c_void_p), ("tk_stride", Strides),
+        ("token_values", ctypes.c_void_p), ("tv_stride", Strides),
+        ("indices", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+        ("grad_key_sums", ctypes.c_void_p), ("grad_value_sums", ctypes.c_void_p),
+        ("grad_weight_sums", ctypes.c_void_p),
+        ("grad_token_keys", ctypes.c_void_p), ("gtk_stride", Strides),
+        ("grad_token_values", ctypes.c_void_p), ("gtv_stride", Strides),
+        ("grad_weights", ctypes.c_void_p),
+    ]
+
+
 Strides2 = ctypes.c_int64 * 2
 
 
@@ -186,6 +211,8 @@ EXPORTS = (
     "murm_slot_diffusion_fwd",
     "murm_slot_diffusion_bwd",
     "murm_decode_step",
+    "murm_slot_sums_fwd",
+    "murm_slot_sums_bwd",
 )
 
 STATUS_NAMES = {
@@ -238,7 +265,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         for name, st in (("murm_select_attend_fwd", SelectAttendArgs), ("murm_select_attend_bwd", SelectAttendBwdArgs),
                          ("murm_slot_update_fwd", SlotUpdateArgs), ("murm_slot_update_bwd", SlotUpdateBwdArgs),
                          ("murm_slot_diffusion_fwd", SlotDiffusionArgs),
-                         ("murm_slot_diffusion_bwd", SlotDiffusionArgs), ("murm_decode_step", DecodeArgs)):
+                         ("murm_slot_diffusion_bwd", SlotDiffusionArgs), ("murm_decode_step", DecodeArgs),
+                         ("murm_slot_sums_fwd", SlotSumsArgs), ("murm_slot_sums_bwd", SlotSumsBwdArgs)):
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
             fn.restype = ctypes.c_int

@@ -414,6 +414,45 @@ __global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const 
   if (lane == 0) Wsum[(size_t)bh * M + m] = W;
 }
 
+// slot sums alone (a warp per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
+template <typename T>
+__global__ void __launch_bounds__(256) k_sums_fwd(murm_slot_sums_args a, const int* offsets, const int* entries) {
+  const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp;
+  if (m >= M) return;
+  const int* off = offsets + (int64_t)bh * (M + 1);
+  const int* ent = entries + (int64_t)bh * N * kTopK;
+  float sk[kMaxD / 32], sv[kMaxD / 32];
+  float W = 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
+  for (int e = off[m]; e < off[m + 1]; ++e) {
+    const int t = ent[e] >> 3, j = ent[e] & 7;
+    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
+    W += wt;
+#pragma unroll
+    for (int u = 0; u < kMaxD / 32; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        sk[u] = fmaf(wt, ld<T>(a.token_keys, off3(a.tk_stride, b, h, t) + d), sk[u]);
+        sv[u] = fmaf(wt, ld<T>(a.token_values, off3(a.tv_stride, b, h, t) + d), sv[u]);
+      }
+    }
+  }
+  const size_t so = ((size_t)bh * M + m) * D;
+#pragma unroll
+  for (int u = 0; u < kMaxD / 32; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      a.key_sums[so + d] = sk[u];
+      a.value_sums[so + d] = sv[u];
+    }
+  }
+  if (lane == 0) a.weight_sums[(size_t)bh * M + m] = W;
+}
+
 // slot update, backward, slot side: grad of the old slots and the adjoints of the
 // sums: dks = (1-a) g_k / (W + eps), dW = -(dks . U_k + dvs . U_v), where W > 0.
 template <typename T>
@@ -787,6 +826,41 @@ murm_status upd_bwd(const murm_slot_update_bwd_args& a, cudaStream_t st) {
 }
 
 template <typename T>
+murm_status sums_fwd(const murm_slot_sums_args& a, cudaStream_t st) {
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  const Sizes z = sizes(a.shape);
+  launch_csr(a.shape, a.indices, ws, st);
+  MURM_LAUNCH("phase_sums", k_sums_fwd<T>, dim3((a.shape.slots + 7) / 8, a.shape.batch * a.shape.heads), 256, 0, st,
+              a, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
+  return launched("slot sums forward");
+}
+
+template <typename T>
+murm_status sums_bwd(const murm_slot_sums_bwd_args& a, cudaStream_t st) {
+  // the token side of the update's backward, with the sums' gradients as its slot adjoints
+  murm_slot_update_bwd_args u{};
+  u.shape = a.shape;
+  u.token_keys = a.token_keys;
+  u.token_values = a.token_values;
+  for (int i = 0; i < 3; ++i) {
+    u.tk_stride[i] = a.tk_stride[i];
+    u.tv_stride[i] = a.tv_stride[i];
+    u.gtk_stride[i] = a.gtk_stride[i];
+    u.gtv_stride[i] = a.gtv_stride[i];
+  }
+  u.indices = a.indices;
+  u.weights = a.weights;
+  u.grad_token_keys = a.grad_token_keys;
+  u.grad_token_values = a.grad_token_values;
+  u.grad_weights = a.grad_weights;
+  MURM_LAUNCH("phase_sums_bwd", k_upd_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, a.shape.batch * a.shape.heads), 256,
+              0, st, u, a.grad_key_sums, a.grad_value_sums, a.grad_weight_sums);
+  return launched("slot sums backward");
+}
+template <typename T> struct SumFwd { static murm_status run(const murm_slot_sums_args& a, cudaStream_t s) { return sums_fwd<T>(a, s); } };
+template <typename T> struct SumBwd { static murm_status run(const murm_slot_sums_bwd_args& a, cudaStream_t s) { return sums_bwd<T>(a, s); } };
+
+template <typename T>
 murm_status diff(const murm_slot_diffusion_args& a, bool backward, cudaStream_t st) {
   const dim3 grid(a.shape.slots, a.shape.batch * a.shape.heads);
   const int threads = a.shape.head_dim < 32 ? 32 : (a.shape.head_dim > 128 ? 128 : a.shape.head_dim);
@@ -894,6 +968,36 @@ MURM_API murm_status murm_slot_update_bwd(const murm_slot_update_bwd_args* a, vo
     return ph::bad(MURM_ERR_WORKSPACE, "saved NULL or smaller than %zu bytes", ph::sizes(a->shape).saved);
   if (murm_status s = ph::ws_ok(a->shape, a->workspace, a->workspace_bytes)) return s;
   return ph::dispatch<ph::UpBwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+MURM_API murm_status murm_slot_sums_fwd(const murm_slot_sums_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->token_keys, "token_keys");
+  PH_REQUIRE(a->token_values, "token_values");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  PH_REQUIRE(a->key_sums, "key_sums");
+  PH_REQUIRE(a->value_sums, "value_sums");
+  PH_REQUIRE(a->weight_sums, "weight_sums");
+  if (murm_status s = ph::ws_ok(a->shape, a->workspace, a->workspace_bytes)) return s;
+  return ph::dispatch<ph::SumFwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
+}
+
+MURM_API murm_status murm_slot_sums_bwd(const murm_slot_sums_bwd_args* a, void* stream) {
+  if (!a) return ph::bad(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (murm_status s = ph::check(a->shape)) return s;
+  PH_REQUIRE(a->token_keys, "token_keys");
+  PH_REQUIRE(a->token_values, "token_values");
+  PH_REQUIRE(a->indices, "indices");
+  PH_REQUIRE(a->weights, "weights");
+  PH_REQUIRE(a->grad_key_sums, "grad_key_sums");
+  PH_REQUIRE(a->grad_value_sums, "grad_value_sums");
+  PH_REQUIRE(a->grad_weight_sums, "grad_weight_sums");
+  PH_REQUIRE(a->grad_token_keys, "grad_token_keys");
+  PH_REQUIRE(a->grad_token_values, "grad_token_values");
+  PH_REQUIRE(a->grad_weights, "grad_weights");
+  return ph::dispatch<ph::SumBwd>(a->shape.dtype, *a, static_cast<cudaStream_t>(stream));
 }
 
 static murm_status diffusion(const murm_slot_diffusion_args* a, bool backward, void* stream) {

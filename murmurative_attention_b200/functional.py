@@ -213,6 +213,59 @@ class _SlotUpdate(torch.autograd.Function):
 
 
 
+class _SlotSums(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, token_keys, token_values, indices, weights, slots):
+        ctx.M = int(slots)
+        lib = _lib.load_library()
+        code = _dtype_code(token_keys, "token_keys")
+        dt = token_keys.dtype
+        tk = _rows(token_keys, dt)
+        tv = _rows(token_values, dt)
+        B, H, N, D = tk.shape
+        M = ctx.M
+        shape = _shape(B, H, N, M, D, code)
+        _, ws_bytes = _sizes(shape)
+        dev = tk.device
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+        idx = indices.to(device=dev, dtype=torch.int64).contiguous()
+        w = weights.to(device=dev, dtype=torch.float32).contiguous()
+        ks = torch.empty(B, H, M, D, device=dev, dtype=torch.float32)
+        vs = torch.empty(B, H, M, D, device=dev, dtype=torch.float32)
+        ws_ = torch.empty(B, H, M, device=dev, dtype=torch.float32)
+        a = _lib.SlotSumsArgs(shape=shape, token_keys=_ptr(tk), tk_stride=_s3(tk), token_values=_ptr(tv),
+                              tv_stride=_s3(tv), indices=_ptr(idx), weights=_ptr(w), key_sums=_ptr(ks),
+                              value_sums=_ptr(vs), weight_sums=_ptr(ws_), workspace=_ptr(ws),
+                              workspace_bytes=ws_bytes)
+        _lib.check(lib.murm_slot_sums_fwd(ctypes.byref(a), _stream()))
+        ctx.save_for_backward(tk, tv, idx, w)
+        ctx.in_dtypes = (token_keys.dtype, token_values.dtype)
+        return ks, vs, ws_
+
+    @staticmethod
+    def backward(ctx, gks, gvs, gw_):
+        lib = _lib.load_library()
+        tk, tv, idx, w = ctx.saved_tensors
+        B, H, N, D = tk.shape
+        M = ctx.M
+        dev = tk.device
+        z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
+        gks = gks.float().contiguous() if gks is not None else z(B, H, M, D)
+        gvs = gvs.float().contiguous() if gvs is not None else z(B, H, M, D)
+        gw_ = gw_.float().contiguous() if gw_ is not None else z(B, H, M)
+        gtk = torch.empty(B, H, N, D, device=dev, dtype=tk.dtype)
+        gtv = torch.empty(B, H, N, D, device=dev, dtype=tk.dtype)
+        gw = torch.empty(B, H, N, 7, device=dev, dtype=torch.float32)
+        a = _lib.SlotSumsBwdArgs(shape=_shape(B, H, N, M, D, _DT[tk.dtype]), token_keys=_ptr(tk), tk_stride=_s3(tk),
+                                 token_values=_ptr(tv), tv_stride=_s3(tv), indices=_ptr(idx), weights=_ptr(w),
+                                 grad_key_sums=_ptr(gks), grad_value_sums=_ptr(gvs), grad_weight_sums=_ptr(gw_),
+                                 grad_token_keys=_ptr(gtk), gtk_stride=_s3(gtk), grad_token_values=_ptr(gtv),
+                                 gtv_stride=_s3(gtv), grad_weights=_ptr(gw))
+        _lib.check(lib.murm_slot_sums_bwd(ctypes.byref(a), _stream()))
+        a_t, b_t = ctx.in_dtypes
+        return gtk.to(a_t), gtv.to(b_t), None, gw, None
+
+
 class _SlotDiffusion(torch.autograd.Function):
     @staticmethod
     def _run(fn, sk, sv, gamma):
@@ -280,6 +333,14 @@ def slot_update(token_keys: torch.Tensor, token_values: torch.Tensor, slot_keys:
     """EMA of every slot towards the weighted mean of the tokens that chose it (ops.py:282-308).
     Returns new tensors (the reference mutates clones of its inputs)."""
     return _SlotUpdate.apply(token_keys, token_values, slot_keys, slot_values, indices, weights, alpha)
+
+
+def slot_sums(token_keys: torch.Tensor, token_values: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor,
+              slots: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The first half of slot_update (reference.py:87-103): fp32 per-slot sums of the
+    weighted token keys, token values and weights, ([B,H,M,d], [B,H,M,d], [B,H,M]).
+    Differentiable. Sums over token shards add up (sequence parallelism)."""
+    return _SlotSums.apply(token_keys, token_values, indices, weights, slots)
 
 
 def slot_diffusion(slot_keys: torch.Tensor, slot_values: torch.Tensor,

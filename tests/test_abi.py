@@ -100,7 +100,8 @@ def test_phase_struct_layout_matches_header(tmp_path):
     structs = [("murm_phase_shape", _lib.PhaseShape), ("murm_select_attend_args", _lib.SelectAttendArgs),
                ("murm_select_attend_bwd_args", _lib.SelectAttendBwdArgs),
                ("murm_slot_update_args", _lib.SlotUpdateArgs), ("murm_slot_update_bwd_args", _lib.SlotUpdateBwdArgs),
-               ("murm_slot_diffusion_args", _lib.SlotDiffusionArgs), ("murm_decode_args", _lib.DecodeArgs)]
+               ("murm_slot_diffusion_args", _lib.SlotDiffusionArgs), ("murm_decode_args", _lib.DecodeArgs),
+               ("murm_slot_sums_args", _lib.SlotSumsArgs), ("murm_slot_sums_bwd_args", _lib.SlotSumsBwdArgs)]
     fields = [("murm_select_attend_args", "indices_in", _lib.SelectAttendArgs),
               ("murm_select_attend_args", "weights", _lib.SelectAttendArgs),
               ("murm_select_attend_bwd_args", "workspace_bytes", _lib.SelectAttendBwdArgs),
@@ -141,5 +142,6 @@ def test_phase_sizes_and_validation():
 def test_phase_null_args_rejected_without_gpu():
     lib = _lib.load_library()
     for name in ("murm_select_attend_fwd", "murm_select_attend_bwd", "murm_slot_update_fwd", "murm_slot_update_bwd",
-                 "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd", "murm_decode_step"):
+                 "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd", "murm_decode_step",
+                 "murm_slot_sums_fwd", "murm_slot_sums_bwd"):
         assert getattr(lib, name)(None, None) == 1, name
