@@ -193,71 +193,91 @@ __global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args 
 // ---------------------------------------------------------------------------
 // Stable counting sort of the (token, pick) pairs of every (b,h) by slot:
 // offsets [BH][M+1], entries [BH][N*7] = token*8 + pick, ordered by slot, then
-// token, then pick. grid BH, 256 threads. A tile of `tile` tokens marks its pairs
-// in a per-slot bitmap; a pair's position is the slot's running count plus the
-// number of earlier pairs of the tile in that slot.
+// token, then pick. Parallel over token tiles: (1) each tile marks its pairs in a
+// per-slot bitmap and counts them per slot, (2) per slot, an exclusive scan over
+// the tiles gives each tile's base (and the slot offsets), (3) each tile places its
+// pairs at offset + base + the number of earlier pairs of the tile in that slot.
+// Integer work only: the order, and so every sum taken over it, is deterministic.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_csr(const int64_t* idx, int N, int M, int tile, int words, int* offsets,
-                                             int* entries) {
-  extern __shared__ uint32_t smu[];
-  int* run = reinterpret_cast<int*>(smu);       // [M]
-  uint32_t* bm = smu + M;                       // [M][words]
-  const int bh = blockIdx.x, tid = threadIdx.x;
-  const int64_t* ix = idx + (int64_t)bh * N * kTopK;
-  for (int m = tid; m < M; m += blockDim.x) run[m] = 0;
+__device__ __forceinline__ void tile_bitmap(const int64_t* ix, int N, int M, int tile, int words, int base,
+                                            uint32_t* bm, int (&mm)[kTopK], bool& live) {
+  const int tid = threadIdx.x;
   for (int e = tid; e < M * words; e += blockDim.x) bm[e] = 0u;
   __syncthreads();
-  for (int e = tid; e < N * kTopK; e += blockDim.x) atomicAdd(&run[clampi(ix[e], M)], 1);
+  const int t = base + tid;
+  live = tid < tile && t < N;
+  if (live) {
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      mm[j] = clampi(ix[(int64_t)t * kTopK + j], M);
+      const int p = tid * kTopK + j;
+      atomicOr(&bm[mm[j] * words + (p >> 5)], 1u << (p & 31));
+    }
+  }
   __syncthreads();
-  int* off = offsets + (int64_t)bh * (M + 1);
-  if (tid == 0) {
+}
+
+// (1) grid (ntiles, BH): per-tile, per-slot pair counts -> cnt [BH][ntiles][M]
+__global__ void __launch_bounds__(256) k_csr_count(const int64_t* idx, int N, int M, int tile, int words, int* cnt) {
+  extern __shared__ uint32_t smu[];
+  const int bh = blockIdx.y, ti = blockIdx.x;
+  int mm[kTopK];
+  bool live;
+  tile_bitmap(idx + (int64_t)bh * N * kTopK, N, M, tile, words, ti * tile, smu, mm, live);
+  int* c = cnt + ((int64_t)bh * gridDim.x + ti) * M;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    int x = 0;
+    for (int w = 0; w < words; ++w) x += __popc(smu[m * words + w]);
+    c[m] = x;
+  }
+}
+
+// (2) grid BH: per slot, tile bases (in place) and the slot offsets
+__global__ void __launch_bounds__(256) k_csr_scan(int ntiles, int M, int* cnt, int* offsets) {
+  __shared__ int tot[1024];
+  const int bh = blockIdx.x;
+  int* c = cnt + (int64_t)bh * ntiles * M;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    int run = 0;
+    for (int t = 0; t < ntiles; ++t) {
+      const int x = c[(int64_t)t * M + m];
+      c[(int64_t)t * M + m] = run;
+      run += x;
+    }
+    tot[m] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* off = offsets + (int64_t)bh * (M + 1);
     int acc = 0;
     for (int m = 0; m < M; ++m) {
-      const int c = run[m];
       off[m] = acc;
-      run[m] = acc;
-      acc += c;
+      acc += tot[m];
     }
     off[M] = acc;
   }
-  __syncthreads();
+}
+
+// (3) grid (ntiles, BH): place the tile's pairs
+__global__ void __launch_bounds__(256) k_csr_fill(const int64_t* idx, int N, int M, int tile, int words,
+                                                  const int* cnt, const int* offsets, int* entries) {
+  extern __shared__ uint32_t smu[];
+  const int bh = blockIdx.y, ti = blockIdx.x;
+  int mm[kTopK];
+  bool live;
+  tile_bitmap(idx + (int64_t)bh * N * kTopK, N, M, tile, words, ti * tile, smu, mm, live);
+  if (!live) return;
+  const int* c = cnt + ((int64_t)bh * gridDim.x + ti) * M;
+  const int* off = offsets + (int64_t)bh * (M + 1);
   int* ent = entries + (int64_t)bh * N * kTopK;
-  for (int base = 0; base < N; base += tile) {
-    const int t = base + tid;
-    const bool live = tid < tile && t < N;
-    int mm[kTopK];
-    if (live) {
+  const int t = ti * tile + threadIdx.x;
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        mm[j] = clampi(ix[(int64_t)t * kTopK + j], M);
-        const int p = tid * kTopK + j;
-        atomicOr(&bm[mm[j] * words + (p >> 5)], 1u << (p & 31));
-      }
-    }
-    __syncthreads();
-    if (live) {
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        const int p = tid * kTopK + j, w = p >> 5;
-        const uint32_t* row = bm + mm[j] * words;
-        int before = __popc(row[w] & ((1u << (p & 31)) - 1u)), after = __popc(row[w] >> (p & 31)) - 1;
-        for (int x = 0; x < w; ++x) before += __popc(row[x]);
-        for (int x = w + 1; x < words; ++x) after += __popc(row[x]);
-        ent[run[mm[j]] + before] = t * 8 + j;
-        mm[j] = (after == 0) ? ~(before + 1) : mm[j];  // the slot's last pair of the tile advances it
-      }
-    }
-    __syncthreads();
-    if (live) {
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        const int p = tid * kTopK + j;
-        const int m = clampi(ix[(int64_t)t * kTopK + j], M);
-        if (mm[j] < 0) run[m] += ~mm[j];
-        bm[m * words + (p >> 5)] = 0u;
-      }
-    }
-    __syncthreads();
+  for (int j = 0; j < kTopK; ++j) {
+    const int p = threadIdx.x * kTopK + j, w = p >> 5;
+    const uint32_t* row = smu + mm[j] * words;
+    int before = __popc(row[w] & ((1u << (p & 31)) - 1u));
+    for (int x = 0; x < w; ++x) before += __popc(row[x]);
+    ent[off[mm[j]] + c[mm[j]] + before] = t * 8 + j;
   }
 }
 
@@ -696,7 +716,7 @@ __global__ void __launch_bounds__(256) k_decode(murm_decode_args a) {
 // host side
 // ---------------------------------------------------------------------------
 struct Sizes {
-  size_t saved, ws, off_csr_entries, off_coef, off_dks, off_dvs, off_dw;
+  size_t saved, ws, off_csr_entries, off_coef, off_dks, off_dvs, off_dw, off_cnt;
 };
 inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -715,6 +735,8 @@ Sizes sizes(const murm_phase_shape& s) {
   o += a256(BH * M * D * 4);
   z.off_dw = o;
   o += a256(BH * M * 4);
+  z.off_cnt = o;
+  o += a256(BH * (size_t)((N + 63) / 64) * M * 4);  // per-tile slot counts (tiles of >= 64 tokens)
   z.ws = o;
   return z;
 }
@@ -757,14 +779,21 @@ murm_status ws_ok(const murm_phase_shape& s, const void* ws, size_t bytes) {
 }
 
 void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cudaStream_t st) {
-  const int M = s.slots;
+  const int M = s.slots, N = s.tokens, BH = s.batch * s.heads;
   const int tile = M <= 256 ? 256 : (M <= 512 ? 128 : 64);
   const int words = (tile * kTopK + 31) / 32;
-  const size_t smem = (size_t)M * 4 + (size_t)M * words * 4;
-  cudaFuncSetAttribute(k_csr, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int ntiles = (N + tile - 1) / tile;
+  const size_t smem = (size_t)M * words * 4;
   const Sizes z = sizes(s);
-  MURM_LAUNCH("phase_csr", k_csr, dim3(s.batch * s.heads), 256, smem, st, idx, s.tokens, M, tile, words,
-              reinterpret_cast<int*>(ws), reinterpret_cast<int*>(ws + z.off_csr_entries));
+  int* offsets = reinterpret_cast<int*>(ws);
+  int* entries = reinterpret_cast<int*>(ws + z.off_csr_entries);
+  int* cnt = reinterpret_cast<int*>(ws + z.off_cnt);
+  cudaFuncSetAttribute(k_csr_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(k_csr_fill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt);
+  MURM_LAUNCH("phase_csr_scan", k_csr_scan, dim3(BH), 256, 0, st, ntiles, M, cnt, offsets);
+  MURM_LAUNCH("phase_csr_fill", k_csr_fill, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt, offsets,
+              entries);
 }
 
 template <typename T>
