@@ -216,77 +216,98 @@ __device__ __forceinline__ float pick32(const float* x, int b) {
 }  // namespace tc
 
 // ---------------------------------------------------------------------------
-// Slot-side kernels of the tensor-core path: warp per slot row (2 dims per
-// lane, coalesced), and they also write the next round's operand images.
+// Slot-side kernels of the tensor-core path: 16 threads per slot row (4 dims
+// each, 16-byte coalesced accesses, two rows per warp), and they also write the
+// next round's operand images.
 // ---------------------------------------------------------------------------
 namespace tc {
-// Write this lane's two columns of slot row m into the operand images.
+constexpr int kRowLanes = 16;  // threads per slot row
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 x) { *reinterpret_cast<float4*>(p) = x; }
+
+// Write columns 4*l .. 4*l+3 of slot row m into the operand images (row m at
+// m*128 bytes, 16-byte chunks XOR-swizzled by m & 7).
 template <typename T>
-__device__ __forceinline__ void put_images(uint8_t* base, int m, int lane, float2 k, float2 v) {
-  const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)lane >> 2) ^ (m & 7)) << 4) + (lane & 3) * 4;
+__device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k, float4 v) {
+  const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)l >> 1) ^ (m & 7)) << 4) + (l & 1) * 8;
+  float kk[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
   for (int s = 0; s < Cfg<T>::kSplits; ++s) {
-    const uint16_t a = to_bits<T>(k.x), b = to_bits<T>(k.y);
-    *reinterpret_cast<uint32_t*>(base + s * kImg + off) = a | ((uint32_t)b << 16);
-    k.x -= from_bits<T>(a);  // exact in fp32: the next term carries the residual
-    k.y -= from_bits<T>(b);
+    uint32_t a[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = to_bits<T>(kk[i]);
+      kk[i] -= from_bits<T>((uint16_t)a[i]);  // exact in fp32: the next term carries the residual
+    }
+    *reinterpret_cast<uint2*>(base + s * kImg + off) = make_uint2(a[0] | (a[1] << 16), a[2] | (a[3] << 16));
   }
-  *reinterpret_cast<uint32_t*>(base + Layout<T>::OFF_V + off) = to_bits<T>(v.x) | ((uint32_t)to_bits<T>(v.y) << 16);
+  const uint32_t v0 = to_bits<T>(v.x), v1 = to_bits<T>(v.y), v2 = to_bits<T>(v.z), v3 = to_bits<T>(v.w);
+  *reinterpret_cast<uint2*>(base + Layout<T>::OFF_V + off) = make_uint2(v0 | (v1 << 16), v2 | (v3 << 16));
 }
 }  // namespace tc
 
 // Round-0 state: slot tables (dtype, strided; batch stride 0 broadcasts) -> fp32 state + images.
-// grid (BH, 256/16): block y covers 16 slot rows, a warp each (rows >= M write zero images).
+// grid (BH, 256/16): block y covers 16 slot rows, 16 threads each (rows >= M write zero images).
 template <typename T>
-__global__ void __launch_bounds__(32 * kSlotRows) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv,
-                                                            Strides3 svs, Saved sv, uint8_t* images) {
-  const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv,
+                                                                        Strides3 svs, Saved sv, uint8_t* images) {
+  const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, l = threadIdx.x & 15;
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
-  {
-    const int m = blockIdx.y * kSlotRows + warp;
-    float2 k = make_float2(0.f, 0.f), v = k;
-    if (m < g.M) {
-      const T* pk = row_ptr(sk, sks, b, h, m) + 2 * lane;
-      const T* pv = row_ptr(svv, svs, b, h, m) + 2 * lane;
-      k = make_float2(Elem<T>::load(pk), Elem<T>::load(pk + 1));
-      v = make_float2(Elem<T>::load(pv), Elem<T>::load(pv + 1));
-      const size_t e = (size_t)bh * g.M * tc::kD + (size_t)m * tc::kD + 2 * lane;
-      *reinterpret_cast<float2*>(sv.K + e) = k;
-      *reinterpret_cast<float2*>(sv.V + e) = v;
-    }
-    tc::put_images<T>(base, m, lane, k, v);
+  const int m = blockIdx.y * kSlotRows + (threadIdx.x >> 4);
+  float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+  if (m < g.M) {
+    const T* pk = row_ptr(sk, sks, b, h, m) + 4 * l;
+    const T* pv = row_ptr(svv, svs, b, h, m) + 4 * l;
+    k = make_float4(Elem<T>::load(pk), Elem<T>::load(pk + 1), Elem<T>::load(pk + 2), Elem<T>::load(pk + 3));
+    v = make_float4(Elem<T>::load(pv), Elem<T>::load(pv + 1), Elem<T>::load(pv + 2), Elem<T>::load(pv + 3));
+    const size_t e = (size_t)bh * g.M * tc::kD + (size_t)m * tc::kD + 4 * l;
+    tc::st4(sv.K + e, k);
+    tc::st4(sv.V + e, v);
   }
+  tc::put_images<T>(base, m, l, k, v);
+}
+
+__device__ __forceinline__ float4 ema4(float a, float b, float4 x, float4 u) {
+  return make_float4(__fadd_rn(__fmul_rn(a, x.x), __fmul_rn(b, u.x)), __fadd_rn(__fmul_rn(a, x.y), __fmul_rn(b, u.y)),
+                     __fadd_rn(__fmul_rn(a, x.z), __fmul_rn(b, u.z)), __fadd_rn(__fmul_rn(a, x.w), __fmul_rn(b, u.w)));
+}
+// x + gamma * ((l + r) - 2 x), each operation rounded as the reference's fp32 tensor ops.
+__device__ __forceinline__ float diffuse1(float x, float l, float r, float gamma) {
+  return __fadd_rn(x, __fmul_rn(gamma, __fsub_rn(__fadd_rn(l, r), __fmul_rn(2.f, x))));
+}
+__device__ __forceinline__ float4 diffuse4(float4 x, float4 l, float4 r, float gamma) {
+  return make_float4(diffuse1(x.x, l.x, r.x, gamma), diffuse1(x.y, l.y, r.y, gamma), diffuse1(x.z, l.z, r.z, gamma),
+                     diffuse1(x.w, l.w, r.w, gamma));
 }
 
 // Finalize round r: combine the chunk partials in chunk order, EMA (reference.py:105-113)
 // and diffusion (reference.py:128-133) -> state entering round r+1, U_r, W_r and
-// the images of round r+1. grid (BH, M/16): a block owns 16 slot rows and recomputes
-// one halo row on each side; one warp per row, every chunk load of a row in flight at once.
+// the images of round r+1. grid (BH, 256/16): a block owns 16 slot rows and recomputes
+// one halo row on each side; 16 threads per row, every chunk load of a row in flight at once.
 template <typename T>
-__global__ void __launch_bounds__(32 * kSlotHalo) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
-  __shared__ float2 kn[kSlotHalo][32];
-  __shared__ float2 vn[kSlotHalo][32];
-  const int bh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
+  __shared__ float4 kn[kSlotHalo][tc::kRowLanes];
+  __shared__ float4 vn[kSlotHalo][tc::kRowLanes];
+  const int bh = blockIdx.x, rr = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int m0 = blockIdx.y * kSlotRows;
+  const int m = m0 - 1 + rr;  // rows m0-1 .. m0+16
   const size_t MD = (size_t)g.M * tc::kD;
   const size_t cur = ((size_t)r * g.BH + bh) * MD;
   {
-    const int rr = warp;  // one row per warp: rows m0-1 .. m0+16
-    const int m = m0 - 1 + rr;
-    float2 k = make_float2(0.f, 0.f), v = k;
+    float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
     if (m >= 0 && m < g.M) {
-      const size_t e = cur + (size_t)m * tc::kD + 2 * lane;
-      k = *reinterpret_cast<const float2*>(sv.K + e);
-      v = *reinterpret_cast<const float2*>(sv.V + e);
-      float2 S = make_float2(0.f, 0.f);
+      const size_t e = cur + (size_t)m * tc::kD + 4 * l;
+      k = tc::ld4(sv.K + e);
+      v = tc::ld4(sv.V + e);
+      float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
       float W = 0.f;
       for (int ch = 0; ch < g.red_chunks; ch += 8) {  // eight loads in flight, added in chunk order
-        float2 a[8];
+        float4 a[8];
         float wv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const size_t po = (size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1);
-          a[u] = *reinterpret_cast<const float2*>(fs.Spart + (po * g.M + m) * tc::kD + 2 * lane);
+          a[u] = tc::ld4(fs.Spart + (po * g.M + m) * tc::kD + 4 * l);
           wv[u] = fs.Wpart[po * g.M + m];
         }
 #pragma unroll
@@ -294,50 +315,44 @@ __global__ void __launch_bounds__(32 * kSlotHalo) k_tc_finalize(Geom g, int r, S
           if (ch + u < g.red_chunks) {
             S.x = __fadd_rn(S.x, a[u].x);
             S.y = __fadd_rn(S.y, a[u].y);
+            S.z = __fadd_rn(S.z, a[u].z);
+            S.w = __fadd_rn(S.w, a[u].w);
             W = __fadd_rn(W, wv[u]);
           }
         }
       }
       const bool hit = W > 0.f;
       const float den = __fadd_rn(W, kEmaEps);
-      const float2 U = make_float2(__fdiv_rn(S.x, den), __fdiv_rn(S.y, den));
+      const float4 U = make_float4(__fdiv_rn(S.x, den), __fdiv_rn(S.y, den), __fdiv_rn(S.z, den), __fdiv_rn(S.w, den));
       if (rr >= 1 && rr <= kSlotRows) {  // this block's rows record U and W
-        *reinterpret_cast<float2*>(sv.U + e) = U;
-        if (lane == 0) sv.W[((size_t)r * g.BH + bh) * g.M + m] = W;
+        tc::st4(sv.U + e, U);
+        if (l == 0) sv.W[((size_t)r * g.BH + bh) * g.M + m] = W;
       }
       if (hit) {
-        const float dx = __fmul_rn(g.one_minus_alpha, U.x), dy = __fmul_rn(g.one_minus_alpha, U.y);
-        k = make_float2(__fadd_rn(__fmul_rn(g.alpha, k.x), dx), __fadd_rn(__fmul_rn(g.alpha, k.y), dy));
-        v = make_float2(__fadd_rn(__fmul_rn(g.alpha, v.x), dx), __fadd_rn(__fmul_rn(g.alpha, v.y), dy));
+        k = ema4(g.alpha, g.one_minus_alpha, k, U);
+        v = ema4(g.alpha, g.one_minus_alpha, v, U);
       }
     }
-    kn[rr][lane] = k;
-    vn[rr][lane] = v;
+    kn[rr][l] = k;
+    vn[rr][l] = v;
   }
   __syncthreads();
-  if (warp < 1 || warp > kSlotRows) return;
+  if (rr < 1 || rr > kSlotRows) return;
   uint8_t* base = fs.images + (size_t)bh * tc::Layout<T>::kImages;
   const size_t nxt = ((size_t)(r + 1) * g.BH + bh) * MD;
-  const int rr = warp;
-  const int m = m0 - 1 + rr;
-  float2 k = make_float2(0.f, 0.f), v = k;
+  float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
   if (m < g.M) {
-    k = kn[rr][lane];
-    v = vn[rr][lane];
+    k = kn[rr][l];
+    v = vn[rr][l];
     if (m > 0 && m < g.M - 1) {
-      const float2 kl = kn[rr - 1][lane], kr = kn[rr + 1][lane], vl = vn[rr - 1][lane], vr = vn[rr + 1][lane];
-      const float2 tk = make_float2(__fsub_rn(__fadd_rn(kl.x, kr.x), __fmul_rn(2.f, k.x)),
-                                    __fsub_rn(__fadd_rn(kl.y, kr.y), __fmul_rn(2.f, k.y)));
-      const float2 tv = make_float2(__fsub_rn(__fadd_rn(vl.x, vr.x), __fmul_rn(2.f, v.x)),
-                                    __fsub_rn(__fadd_rn(vl.y, vr.y), __fmul_rn(2.f, v.y)));
-      k = make_float2(__fadd_rn(k.x, __fmul_rn(g.gamma, tk.x)), __fadd_rn(k.y, __fmul_rn(g.gamma, tk.y)));
-      v = make_float2(__fadd_rn(v.x, __fmul_rn(g.gamma, tv.x)), __fadd_rn(v.y, __fmul_rn(g.gamma, tv.y)));
+      k = diffuse4(k, kn[rr - 1][l], kn[rr + 1][l], g.gamma);
+      v = diffuse4(v, vn[rr - 1][l], vn[rr + 1][l], g.gamma);
     }
-    const size_t e = nxt + (size_t)m * tc::kD + 2 * lane;
-    *reinterpret_cast<float2*>(sv.K + e) = k;
-    *reinterpret_cast<float2*>(sv.V + e) = v;
+    const size_t e = nxt + (size_t)m * tc::kD + 4 * l;
+    tc::st4(sv.K + e, k);
+    tc::st4(sv.V + e, v);
   }
-  tc::put_images<T>(base, m, lane, k, v);  // rows >= M: zero
+  tc::put_images<T>(base, m, l, k, v);  // rows >= M: zero
 }
 
 // ---------------------------------------------------------------------------
@@ -968,13 +983,13 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
     cudaFuncSetAttribute(k_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Layout<T>::kSmem);
     attr = true;
   }
-  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), 32 * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
+  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
               static_cast<const T*>(p.sv), p.svs, sv, images);
   for (int r = 0; r < g.R; ++r) {
     MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
     if (r + 1 < g.R)
-      MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), 32 * kSlotHalo, 0, st, g, r, sv, fs);
+      MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs);
   }
   return cudaGetLastError();
 }

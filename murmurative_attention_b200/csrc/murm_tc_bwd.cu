@@ -20,7 +20,7 @@
 // every token: dV += P^T . G with P = w, then dK += P^T . Q with P = scale da,
 // accumulated in TMEM over the chunk — deterministic, no atomics.
 // k_bwd_slots: finalize of round r (direct part + chunk partials, in chunk
-// order) fused with the per-slot adjoints of round r-1, warp per slot row.
+// order) fused with the per-slot adjoints of round r-1, 16 threads per slot row.
 #include <cudaTypedefs.h>
 
 #include "murm_kernels.cuh"
@@ -197,117 +197,135 @@ __device__ __forceinline__ void warp_sum8(float (&v)[8]) {
 // ---------------------------------------------------------------------------
 // Slot side: finalize round r (dK_r, dV_r) and, for r > 0, the adjoints of
 // round r-1 (dS, dW, direct parts) plus its 16-bit tables for the token kernel.
-// grid (BH, ceil(M/32)), 256 threads; warp per slot row, 2 dims per lane.
+// grid (BH, ceil(M/16)), 288 threads: 16 threads per slot row (4 dims each,
+// 16-byte accesses), rows m0-1 .. m0+16 (one diffusion halo row on each side).
 // ---------------------------------------------------------------------------
 // Direct parts live in bs.dK[r & 1] / bs.dV[r & 1] (round parity): a block reads
 // its neighbours' rows of round r while they write round r-1.
+namespace tcb {
+constexpr int kRowLanes = 16;
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 x) { *reinterpret_cast<float4*>(p) = x; }
+__device__ __forceinline__ void add4(float4& a, float4 b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
+// a + c * b, each product and sum rounded (reference.py:128-133 transposed)
+__device__ __forceinline__ float4 axpy4(float4 a, float c, float4 b) {
+  return make_float4(__fadd_rn(a.x, __fmul_rn(c, b.x)), __fadd_rn(a.y, __fmul_rn(c, b.y)),
+                     __fadd_rn(a.z, __fmul_rn(c, b.z)), __fadd_rn(a.w, __fmul_rn(c, b.w)));
+}
+__device__ __forceinline__ float4 scale4(float c, float4 b) {
+  return make_float4(__fmul_rn(c, b.x), __fmul_rn(c, b.y), __fmul_rn(c, b.z), __fmul_rn(c, b.w));
+}
 template <typename T>
-__global__ void __launch_bounds__(32 * kSlotHalo) k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv,
-                                                             BwdScratch bs, uint8_t* tables, float* dWpad, T* gsk,
-                                                             Strides3 gsks, T* gsv, Strides3 gsvs) {
+__device__ __forceinline__ uint2 pack4(float4 x) {
+  return make_uint2(bits<T>(x.x) | ((uint32_t)bits<T>(x.y) << 16), bits<T>(x.z) | ((uint32_t)bits<T>(x.w) << 16));
+}
+}  // namespace tcb
+
+template <typename T>
+__global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
+    k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv, BwdScratch bs, uint8_t* tables, float* dWpad,
+                T* gsk, Strides3 gsks, T* gsv, Strides3 gsvs) {
   const float* dir_k = bs.dK[r & 1];
   const float* dir_v = bs.dV[r & 1];
   float* nxt_k = bs.dK[(r + 1) & 1];  // direct parts of round r-1
   float* nxt_v = bs.dV[(r + 1) & 1];
-  __shared__ float2 skk[kSlotHalo][32];  // dK_r rows m0-1 .. m0+16, as float2 per lane
-  __shared__ float2 svv[kSlotHalo][32];
+  __shared__ float4 skk[kSlotHalo][tcb::kRowLanes];  // dK_r rows m0-1 .. m0+16
+  __shared__ float4 svv[kSlotHalo][tcb::kRowLanes];
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H;
-  const int m0 = blockIdx.y * kSlotRows, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rr = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int m = blockIdx.y * kSlotRows - 1 + rr;
   const size_t MD = (size_t)g.M * g.D;
-  // 1. dK_r, dV_r for the block and its halo: one row per warp, every chunk load in flight at once
+  // 1. dK_r, dV_r for the block and its halo, every chunk load of a row in flight at once
   {
-    const int rr = warp;
-    const int m = m0 - 1 + rr;
-    float2 k = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+    float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
     if (m >= 0 && m < g.M) {
-      const size_t e = bh * MD + (size_t)m * g.D + 2 * lane;
+      const size_t e = bh * MD + (size_t)m * g.D + 4 * l;
       if (has_dir) {
-        k = *reinterpret_cast<const float2*>(dir_k + e);
-        v = *reinterpret_cast<const float2*>(dir_v + e);
+        k = tcb::ld4(dir_k + e);
+        v = tcb::ld4(dir_v + e);
       }
       if (has_part) {
         for (int ch = 0; ch < g.red_chunks; ch += 8) {  // added in chunk order
-          float2 a[8], c[8];
+          float4 a[8], c[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const size_t po = ((size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1)) * MD + (size_t)m * g.D + 2 * lane;
-            a[u] = *reinterpret_cast<const float2*>(bs.dKpart + po);
-            c[u] = *reinterpret_cast<const float2*>(bs.dVpart + po);
+            const size_t po = ((size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1)) * MD + (size_t)m * g.D + 4 * l;
+            a[u] = tcb::ld4(bs.dKpart + po);
+            c[u] = tcb::ld4(bs.dVpart + po);
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            if (ch + u < g.red_chunks) { k.x += a[u].x; k.y += a[u].y; v.x += c[u].x; v.y += c[u].y; }
+            if (ch + u < g.red_chunks) {
+              tcb::add4(k, a[u]);
+              tcb::add4(v, c[u]);
+            }
           }
         }
       }
     }
-    skk[rr][lane] = k;
-    svv[rr][lane] = v;
+    skk[rr][l] = k;
+    svv[rr][l] = v;
   }
   __syncthreads();
-  if (warp < 1 || warp > kSlotRows) return;
-  const int rr = warp;
-  const int m = m0 - 1 + rr;
-  if (m >= g.M) return;
+  if (rr < 1 || rr > kSlotRows || m >= g.M) return;  // uniform per half warp
   if (r == 0) {  // the slot gradients
-    T* pk = row_ptr(gsk, gsks, b, h, m) + 2 * lane;
-    T* pv = row_ptr(gsv, gsvs, b, h, m) + 2 * lane;
-    Elem<T>::store(pk, skk[rr][lane].x);
-    Elem<T>::store(pk + 1, skk[rr][lane].y);
-    Elem<T>::store(pv, svv[rr][lane].x);
-    Elem<T>::store(pv + 1, svv[rr][lane].y);
+    T* pk = row_ptr(gsk, gsks, b, h, m) + 4 * l;
+    T* pv = row_ptr(gsv, gsvs, b, h, m) + 4 * l;
+    const float4 k = skk[rr][l], v = svv[rr][l];
+    Elem<T>::store(pk, k.x);
+    Elem<T>::store(pk + 1, k.y);
+    Elem<T>::store(pk + 2, k.z);
+    Elem<T>::store(pk + 3, k.w);
+    Elem<T>::store(pv, v.x);
+    Elem<T>::store(pv + 1, v.y);
+    Elem<T>::store(pv + 2, v.z);
+    Elem<T>::store(pv + 3, v.w);
     return;
   }
   // 2. adjoints of round r-1 for slots of this block
   const int rp = r - 1;
-  const float gm2 = -2.f * g.gamma;
-  uint8_t* tab = tables + (size_t)bh * tcb::kTables;
-  {
-    const bool in_m = m > 0 && m < g.M - 1, in_l = m - 1 > 0, in_r = m + 1 < g.M - 1;
-    float2 ak = skk[rr][lane], av = svv[rr][lane];
-    if (in_m) {
-      ak.x = __fadd_rn(ak.x, __fmul_rn(gm2, ak.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(gm2, ak.y));
-      av.x = __fadd_rn(av.x, __fmul_rn(gm2, av.x)); av.y = __fadd_rn(av.y, __fmul_rn(gm2, av.y));
-    }
-    if (in_l) {
-      const float2 lk = skk[rr - 1][lane], lv = svv[rr - 1][lane];
-      ak.x = __fadd_rn(ak.x, __fmul_rn(g.gamma, lk.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(g.gamma, lk.y));
-      av.x = __fadd_rn(av.x, __fmul_rn(g.gamma, lv.x)); av.y = __fadd_rn(av.y, __fmul_rn(g.gamma, lv.y));
-    }
-    if (in_r) {
-      const float2 rk = skk[rr + 1][lane], rv = svv[rr + 1][lane];
-      ak.x = __fadd_rn(ak.x, __fmul_rn(g.gamma, rk.x)); ak.y = __fadd_rn(ak.y, __fmul_rn(g.gamma, rk.y));
-      av.x = __fadd_rn(av.x, __fmul_rn(g.gamma, rv.x)); av.y = __fadd_rn(av.y, __fmul_rn(g.gamma, rv.y));
-    }
-    const float W = sv.W[((size_t)rp * g.BH + bh) * g.M + m];
-    const bool hit = W > 0.f;
-    const float den = __fadd_rn(W, kEmaEps);
-    float2 dU = make_float2(0.f, 0.f);
-    if (hit) {
-      dU.x = __fmul_rn(g.one_minus_alpha, __fadd_rn(ak.x, av.x));
-      dU.y = __fmul_rn(g.one_minus_alpha, __fadd_rn(ak.y, av.y));
-    }
-    const size_t st = ((size_t)rp * g.BH + bh) * MD + (size_t)m * g.D + 2 * lane;
-    const float2 U = *reinterpret_cast<const float2*>(sv.U + st);
-    float dot = fmaf(dU.x, U.x, dU.y * U.y);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const float2 dS = make_float2(__fdiv_rn(dU.x, den), __fdiv_rn(dU.y, den));
-    const size_t e = bh * MD + (size_t)m * g.D + 2 * lane;
-    *reinterpret_cast<float2*>(nxt_k + e) =
-        hit ? make_float2(__fmul_rn(g.alpha, ak.x), __fmul_rn(g.alpha, ak.y)) : ak;
-    *reinterpret_cast<float2*>(nxt_v + e) =
-        hit ? make_float2(__fmul_rn(g.alpha, av.x), __fmul_rn(g.alpha, av.y)) : av;
-    if (lane == 0) dWpad[(size_t)bh * tcb::kSlotsPad + m] = -__fdiv_rn(dot, den);
-    // 16-bit tables of round r-1 (row-major [256][64])
-    const float2 K = *reinterpret_cast<const float2*>(sv.K + st);
-    const float2 V = *reinterpret_cast<const float2*>(sv.V + st);
-    const uint32_t off = (uint32_t)m * 128 + 4 * lane;
-    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_K + off) = tcb::bits<T>(K.x) | ((uint32_t)tcb::bits<T>(K.y) << 16);
-    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_V + off) = tcb::bits<T>(V.x) | ((uint32_t)tcb::bits<T>(V.y) << 16);
-    *reinterpret_cast<uint32_t*>(tab + tcb::OFF_DS + off) =
-        tcb::bits<T>(dS.x) | ((uint32_t)tcb::bits<T>(dS.y) << 16);
+  const size_t st = ((size_t)rp * g.BH + bh) * MD + (size_t)m * g.D + 4 * l;
+  const float W = sv.W[((size_t)rp * g.BH + bh) * g.M + m];
+  const float4 U = tcb::ld4(sv.U + st);
+  const float4 K = tcb::ld4(sv.K + st);
+  const float4 V = tcb::ld4(sv.V + st);
+  const bool in_m = m > 0 && m < g.M - 1, in_l = m - 1 > 0, in_r = m + 1 < g.M - 1;
+  float4 ak = skk[rr][l], av = svv[rr][l];
+  if (in_m) {
+    const float gm2 = -2.f * g.gamma;
+    ak = tcb::axpy4(ak, gm2, ak);
+    av = tcb::axpy4(av, gm2, av);
   }
+  if (in_l) {
+    ak = tcb::axpy4(ak, g.gamma, skk[rr - 1][l]);
+    av = tcb::axpy4(av, g.gamma, svv[rr - 1][l]);
+  }
+  if (in_r) {
+    ak = tcb::axpy4(ak, g.gamma, skk[rr + 1][l]);
+    av = tcb::axpy4(av, g.gamma, svv[rr + 1][l]);
+  }
+  const bool hit = W > 0.f;
+  const float den = __fadd_rn(W, kEmaEps);
+  float4 dU = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (hit) {
+    dU = make_float4(__fadd_rn(ak.x, av.x), __fadd_rn(ak.y, av.y), __fadd_rn(ak.z, av.z), __fadd_rn(ak.w, av.w));
+    dU = tcb::scale4(g.one_minus_alpha, dU);
+  }
+  float dot = fmaf(dU.x, U.x, fmaf(dU.y, U.y, fmaf(dU.z, U.z, dU.w * U.w)));
+  const unsigned half = 0xffffu << (threadIdx.x & 16);
+#pragma unroll
+  for (int o = 8; o; o >>= 1) dot += __shfl_xor_sync(half, dot, o);
+  const float4 dS = make_float4(__fdiv_rn(dU.x, den), __fdiv_rn(dU.y, den), __fdiv_rn(dU.z, den), __fdiv_rn(dU.w, den));
+  const size_t e = bh * MD + (size_t)m * g.D + 4 * l;
+  tcb::st4(nxt_k + e, hit ? tcb::scale4(g.alpha, ak) : ak);
+  tcb::st4(nxt_v + e, hit ? tcb::scale4(g.alpha, av) : av);
+  if (l == 0) dWpad[(size_t)bh * tcb::kSlotsPad + m] = -__fdiv_rn(dot, den);
+  // 16-bit tables of round r-1 (row-major [256][64])
+  uint8_t* tab = tables + (size_t)bh * tcb::kTables;
+  const uint32_t off = (uint32_t)m * 128 + 8 * l;
+  *reinterpret_cast<uint2*>(tab + tcb::OFF_K + off) = tcb::pack4<T>(K);
+  *reinterpret_cast<uint2*>(tab + tcb::OFF_V + off) = tcb::pack4<T>(V);
+  *reinterpret_cast<uint2*>(tab + tcb::OFF_DS + off) = tcb::pack4<T>(dS);
 }
 
 // Tables of the last round (no slot gradient flows into it): K, V; dS = 0, dW = 0.
@@ -748,7 +766,7 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
     MURM_LAUNCH("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
                 qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,
                 static_cast<T*>(p.gq), p.gqs, sv, bs, tables, dWpad);
-    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), 32 * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
+    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), tcb::kRowLanes * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
                 sv, bs, tables, dWpad, static_cast<T*>(p.gsk), p.gsks, static_cast<T*>(p.gsv), p.gsvs);
   }
   return cudaGetLastError();
