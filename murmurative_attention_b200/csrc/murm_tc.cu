@@ -199,6 +199,24 @@ __device__ __forceinline__ void merge8_rank(const uint64_t (&A)[8], const uint64
         c[i + s] = min64(x, y);
       }
 }
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Bit i set where x[i] >= t (t finite, x[i] finite or -inf). x - t is >= 0 exactly when
+// x >= t (a difference of distinct floats never rounds to +0), so the complement of its
+// sign bit is the comparison: one subtraction on the FMA pipe and one funnel shift per
+// column, four independent chains of 8.
+__device__ __forceinline__ uint32_t ge_mask32(const float (&x)[32], float t) {
+  uint32_t c[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 7; i >= 0; --i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) c[q] = __funnelshift_l(__float_as_uint(x[8 * q + i] - t), c[q], 1);
+  return ~(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24));
+}
 // x[b] for a run-time b in [0, 32) over 32 values held in registers (select tree).
 __device__ __forceinline__ float pick32(const float* x, int b) {
   float t[16];
@@ -661,8 +679,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           load2(c, x0, x1);
 #pragma unroll
           for (int gq = 0; gq < 16; ++gq) {
-            const float y = fmaxf(fmaxf(x0[gq], x0[gq + 16]), fmaxf(x1[gq], x1[gq + 16]));
-            gm[gq] = c ? fmaxf(gm[gq], y) : y;
+            const float y = tc::max3(x0[gq], x0[gq + 16], x1[gq]);
+            gm[gq] = c ? tc::max3(y, x1[gq + 16], gm[gq]) : fmaxf(y, x1[gq + 16]);
           }
         }
         float ga[8], gb[8], top8[8];
@@ -710,13 +728,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         load2(c, x[0], x[1]);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-          uint32_t a = 0, b2 = 0;  // two independent chains
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            a |= (x[k][i] >= thr) ? (1u << i) : 0u;
-            b2 |= (x[k][16 + i] >= thr) ? (1u << (16 + i)) : 0u;
-          }
-          uint32_t msk = scan ? (a | b2) : 0u;
+          uint32_t msk = scan ? tc::ge_mask32(x[k], thr) : 0u;
           while (__any_sync(0xffffffffu, msk != 0)) {
             // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
             const int bit = __ffs(msk) - 1;
