@@ -508,6 +508,23 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   for (int tile = 0; tile < ntiles; ++tile) {
     const int n0 = t_beg + tile * kTile;
     const int nt = min(kTile, t_end - n0);
+    if (tid == tcb::kIssuer && tile + 1 < ntiles) {
+      // the next tile's inputs into L2 a tile ahead: its grad_out tile is loaded (and its
+      // records and earlier-round dq read) only once this tile's consumers are done
+      const int nn0 = n0 + kTile;
+      const int nnt = min(kTile, t_end - nn0);
+      const size_t trow = ((size_t)r * g.BH + bh) * g.N + nn0;
+      tma_prefetch_4d(&gmap, 0, nn0, h, b);
+      if (nnt >= 2) bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(sv.idx) + trow * 8, (uint32_t)(nnt * 8) & ~15u);
+      bulk_prefetch_l2(sv.w + trow * 8, (uint32_t)nnt * 32);
+      if (!first) bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(nnt * g.D * 4));
+      if (gw && first) {  // 28 bytes per token: the 16-byte aligned run inside
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(gw + ((size_t)bh * g.N + nn0) * kTopK);
+        const uintptr_t hi = lo + (uintptr_t)nnt * kTopK * 4;
+        const uintptr_t a0 = (lo + 15) & ~(uintptr_t)15, a1 = hi & ~(uintptr_t)15;
+        if (a1 > a0) bulk_prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
+      }
+    }
     // ---- records into shared memory; P rows: clear the previous tile's entries, then w ----
     if (tid < kTile) {
       if (old_live) {
