@@ -108,6 +108,7 @@ template <typename T> struct Layout {
 };
 
 __device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
   // About one second of polling, measured on the global timer.
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));

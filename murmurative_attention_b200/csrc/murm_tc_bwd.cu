@@ -13,12 +13,14 @@
 // on slots that received picks, dK' = D^T dK_{r+1} (diffusion adjoint), and
 // dKdir = alpha dK' (or dK' on slots without picks).
 //
-// k_bwd_tokens_tc: one CTA per (batch, head) and token chunk, 8 warps. A warp
-// handles one token at a time with 2 head dims per lane; the slot tables K_r,
-// V_r, dS_r (16-bit) and dW_r sit in shared memory. The slot scatters are
-// dense tensor-core products over a 128 x 256 tile P that holds the 7 picks of
-// every token: dV += P^T . G with P = w, then dK += P^T . Q with P = scale da,
-// accumulated in TMEM over the chunk — deterministic, no atomics.
+// k_bwd_tokens_tc: one CTA per (batch, head) and token chunk, 16 warps. Eight
+// lanes share a token (8 head dims each), a warp takes 4 tokens of a 64-token
+// tile; the slot tables K_r, V_r, dS_r (16-bit) and dW_r sit in shared memory.
+// The slot scatters are dense tensor-core products over a 64 x 256 tile P that
+// holds the 7 picks of every token: dV += P^T . G with P = w, then
+// dK += P^T . Q with P = scale da, accumulated in TMEM over the chunk —
+// deterministic, no atomics. P is double-buffered, so a tile's dK scatter runs
+// under the next tile's token math.
 // k_bwd_slots: finalize of round r (direct part + chunk partials, in chunk
 // order) fused with the per-slot adjoints of round r-1, 16 threads per slot row.
 #include <cudaTypedefs.h>
@@ -40,15 +42,19 @@ constexpr int kIssuer = 0;                  // the thread that issues the MMAs a
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
+constexpr int kBTile = 64;                           // tokens per tile of the token kernel
+constexpr uint32_t kTileBytes = kBTile * 128;        // one [64][64] 16-bit swizzled TMA tile
+constexpr uint32_t kPBlock = kBTile * 128;           // P block: [64 tokens][64 slots], swizzled
+constexpr uint32_t kPBuf = 4 * kPBlock;              // P of one tile: 256 slots
 constexpr uint32_t OFF_DW = kTables;                 // fp32 [256]
-constexpr uint32_t OFF_P = OFF_DW + 1024;            // 4 slot blocks x 16 KB (1024-aligned)
-constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;        // 2 q tiles (tile parity), swizzled (MMA operand)
-constexpr uint32_t OFF_G = OFF_Q + 2 * 16384;        // grad_out tile, swizzled
-constexpr uint32_t OFF_COEF = OFF_G + 16384;         // fp32 [128][8] scale*da per pick
-constexpr uint32_t OFF_TW = OFF_COEF + kTile * 8 * 4;  // fp32 [128][8] weights of the tile's tokens
-constexpr uint32_t OFF_TGW = OFF_TW + kTile * 8 * 4;   // fp32 [128][8] dL/d weights (last round)
-constexpr uint32_t OFF_TIX = OFF_TGW + kTile * 8 * 4;  // u8 [128][8] picks
-constexpr uint32_t OFF_MISC = OFF_TIX + kTile * 8;
+constexpr uint32_t OFF_P = OFF_DW + 1024;            // P[2] by tile parity (1024-aligned)
+constexpr uint32_t OFF_Q = OFF_P + 2 * kPBuf;        // q tiles [3] by tile mod 3 (MMA operand)
+constexpr uint32_t OFF_G = OFF_Q + 3 * kTileBytes;   // grad_out tiles [2] by tile parity
+constexpr uint32_t OFF_TW = OFF_G + 2 * kTileBytes;  // fp32 [2][64][8] weights of the tiles' tokens
+constexpr uint32_t OFF_COEF = OFF_TW + 2 * kBTile * 32;  // fp32 [64][8] scale*da per pick
+constexpr uint32_t OFF_TGW = OFF_COEF + kBTile * 32;     // fp32 [64][8] dL/d weights (last round)
+constexpr uint32_t OFF_TIX = OFF_TGW + kBTile * 32;      // u8 [2][64][8] picks
+constexpr uint32_t OFF_MISC = OFF_TIX + 2 * kBTile * 8;
 constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 256;
@@ -56,6 +62,8 @@ constexpr uint32_t COL_DV = 0, COL_DK = 128;
 enum : int { kErrWait = 8 };
 
 __device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
+  // About one second of polling, measured on the global timer.
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   for (;;) {
@@ -352,6 +360,10 @@ __global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8
 // ---------------------------------------------------------------------------
 // Token side of round r
 // ---------------------------------------------------------------------------
+// Tiles of 64 tokens, software-pipelined: P, the grad_out tiles and the weight
+// records are double-buffered by tile parity and the q tiles triple-buffered, so
+// the last slot scatter of a tile (dK) runs under the next tile's records and
+// token math, and every copy is issued two tiles ahead of its use.
 template <typename T>
 __global__ void __launch_bounds__(tcb::kThreads, 1)
     k_bwd_tokens_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
@@ -361,35 +373,41 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t s_base = smem_u32(sm);
   uint64_t* bar_tab = reinterpret_cast<uint64_t*>(sm + tcb::OFF_MISC);
-  uint64_t* bar_q = bar_tab + 1;  // [2], by tile parity
-  uint64_t* bar_g = bar_tab + 3;
-  uint64_t* bar_mma = bar_tab + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + tcb::OFF_MISC + 64);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + tcb::OFF_MISC + 68);
+  uint64_t* bar_q = bar_tab + 1;  // [3], by tile mod 3
+  uint64_t* bar_g = bar_tab + 4;  // [2], by tile parity
+  uint64_t* bar_w = bar_tab + 6;  // [2], by tile parity
+  uint64_t* bar_mma = bar_tab + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + tcb::OFF_MISC + 96);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + tcb::OFF_MISC + 100);
   const float* dWs = reinterpret_cast<const float*>(sm + tcb::OFF_DW);
   float* coef = reinterpret_cast<float*>(sm + tcb::OFF_COEF);
+  float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
 
+  constexpr int kBT = tcb::kBTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
   const int t_beg = chunk * g.red_chunk_tokens;
   const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
-  const int ntiles = (t_end - t_beg + kTile - 1) / kTile;
+  const int ntiles = (t_end - t_beg + kBT - 1) / kBT;
   const bool has_slot_grad = r < g.R - 1;
   const bool first = (r == g.R - 1);
+  const size_t rec0 = ((size_t)r * g.BH + bh) * g.N;  // record row of token 0 of this (b, h)
   constexpr uint32_t ID_UPD = idesc_f16(tcb::Fmt<T>::v, 128, 64, 1, 1);
 
   if (tid == tcb::kIssuer) {
     mbar_init(bar_tab, 1);
-    mbar_init(&bar_q[0], 1);
-    mbar_init(&bar_q[1], 1);
-    mbar_init(bar_g, 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_q[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_g[i], 1);
+      mbar_init(&bar_w[i], 1);
+    }
     mbar_init(bar_mma, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
   {
     float4* p4 = reinterpret_cast<float4*>(sm + tcb::OFF_P);
-    for (int i = tid; i < 4 * 16384 / 16; i += tcb::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = tid; i < 2 * (int)tcb::kPBuf / 16; i += tcb::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tcb::kTmemCols);
@@ -401,28 +419,39 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   uint32_t ph_mma = 0;
-  // the issuer's bookkeeping of asynchronous copies
-  uint32_t ph_q[2] = {0, 0}, ph_g = 0;
-  bool tab_pending = false, q_pending[2] = {false, false}, g_pending = false;
-  auto load_q = [&](int tile_idx) {  // issuer
-    const int bsl = tile_idx & 1;
-    mbar_arrive_expect_tx(&bar_q[bsl], 16384);
-    tma_load_4d(sm + tcb::OFF_Q + bsl * 16384, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bsl]);
-    q_pending[bsl] = true;
+  // the issuer's bookkeeping of asynchronous copies: the last tile issued / waited for
+  int q_issued = -1, g_issued = -1, w_issued = -1, qg_done = -1, w_done = -1;
+  bool tab_pending = false;
+  auto load_q = [&](int j) {  // issuer
+    const int s = j % 3;
+    mbar_arrive_expect_tx(&bar_q[s], tcb::kTileBytes);
+    tma_load_4d(sm + tcb::OFF_Q + s * tcb::kTileBytes, &qmap, 0, t_beg + j * kBT, h, b, &bar_q[s]);
+    q_issued = j;
   };
-  auto load_g = [&](int tile_idx) {  // issuer
-    mbar_arrive_expect_tx(bar_g, 16384);
-    tma_load_4d(sm + tcb::OFF_G, &gmap, 0, t_beg + tile_idx * kTile, h, b, bar_g);
-    g_pending = true;
+  auto load_g = [&](int j) {  // issuer
+    const int s = j & 1;
+    mbar_arrive_expect_tx(&bar_g[s], tcb::kTileBytes);
+    tma_load_4d(sm + tcb::OFF_G + s * tcb::kTileBytes, &gmap, 0, t_beg + j * kBT, h, b, &bar_g[s]);
+    g_issued = j;
+  };
+  auto load_w = [&](int j) {  // issuer: the tile's softmax weights, 32 bytes per token
+    const int s = j & 1;
+    const int n = t_beg + j * kBT;
+    const uint32_t bytes = (uint32_t)min(kBT, t_end - n) * 32u;
+    mbar_arrive_expect_tx(&bar_w[s], bytes);
+    bulk_g2s(sm + tcb::OFF_TW + s * kBT * 32, sv.w + (rec0 + n) * 8, bytes, &bar_w[s]);
+    w_issued = j;
   };
   if (tid == tcb::kIssuer) {
     mbar_arrive_expect_tx(bar_tab, tcb::kTables + 1024);
     bulk_g2s(sm, tables + (size_t)bh * tcb::kTables, tcb::kTables, bar_tab);
     bulk_g2s(sm + tcb::OFF_DW, dWpad + (size_t)bh * tcb::kSlotsPad, 1024, bar_tab);
     tab_pending = true;
-    load_q(0);
-    load_g(0);
-    if (ntiles > 1) load_q(1);
+    for (int j = 0; j < 2 && j < ntiles; ++j) {
+      load_q(j);
+      load_g(j);
+      load_w(j);
+    }
   }
   // every thread reads the tables: wait for them once
   if (!tcb::timed_wait(bar_tab, 0)) {
@@ -436,17 +465,16 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const uint8_t* tK = sm + tcb::OFF_K;
   const uint8_t* tV = sm + tcb::OFF_V;
   const uint8_t* tS = sm + tcb::OFF_DS;
-  const uint32_t a_p = s_base + tcb::OFF_P, a_g = s_base + tcb::OFF_G;
-  auto p_entry = [&](int t, int m) -> uint16_t* {
-    return reinterpret_cast<uint16_t*>(sm + tcb::OFF_P + (m >> 6) * 16384 + sw128_offset(t, m & 63));
-  };
-  auto issue_scatter = [&](uint32_t a_b, uint32_t col, bool first_acc) {  // thread 0: D += P^T . B
+  // D += P^T . B over the tile's 64 tokens (issuer): two 128-slot halves, four k-steps of 16 tokens
+  auto issue_scatter = [&](uint32_t a_p, uint32_t a_b, uint32_t col, bool first_acc) {
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16(tmem + col + 64 * hh, smem_desc(a_p + 2 * hh * 16384 + kk * 2048, 16384, 1024, kSwizzle128B),
-                smem_desc(a_b + kk * 2048, 16384, 1024, kSwizzle128B), ID_UPD, (first_acc && kk == 0) ? 0u : 1u);
+      for (int kk = 0; kk < kBT / 16; ++kk)
+        mma_f16(tmem + col + 64 * hh,
+                smem_desc(a_p + 2 * hh * tcb::kPBlock + kk * 2048, tcb::kPBlock, 1024, kSwizzle128B),
+                smem_desc(a_b + kk * 2048, tcb::kTileBytes, 1024, kSwizzle128B), ID_UPD,
+                (first_acc && kk == 0) ? 0u : 1u);
   };
   auto wait_mma = [&]() {
     if (tcb::timed_wait(bar_mma, ph_mma)) ph_mma ^= 1;
@@ -454,145 +482,133 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     tc_fence_after();
   };
 
-  // Scatter phases over P (128 tokens x 256 slots, one term per phase):
+  // Scatter phases over P (64 tokens x 256 slots, one term per phase):
   //   fp16: dV += P^T.G (P = w) during the token math, then dK += P^T.Q (P = scale*da);
   //   bf16: weights and coefficients go in as two terms each (hi = rn(x), lo = rn(x - hi)),
   //         since bf16 alone rounds them to 2^-9: dV_hi during the math, then dV_lo, dK_hi, dK_lo.
+  // The last phase is not waited for: its completion is implied by the next tile's first.
   constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
   auto hi_bits = [](float x) -> uint16_t { return tcb::bits<T>(x); };
   auto lo_bits = [](float x) -> uint16_t {
     const uint16_t hb = tcb::bits<T>(x);
     return tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb)));
   };
-  float* tw = reinterpret_cast<float*>(sm + tcb::OFF_TW);
-  float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
-  uint8_t* tix = sm + tcb::OFF_TIX;
-  // records of a tile, one token per thread (threads 0..127), fetched a tile ahead
-  uint2 rix = make_uint2(0u, 0u);
-  float4 rw0 = make_float4(0.f, 0.f, 0.f, 0.f), rw1 = rw0;
-  auto fetch_recs = [&](int tile_idx) {
-    const int nn0 = t_beg + tile_idx * kTile;
-    if (tid < min(kTile, t_end - nn0)) {
-      const size_t trow = ((size_t)r * g.BH + bh) * g.N + nn0 + tid;
-      rix = reinterpret_cast<const uint2*>(sv.idx)[trow];
-      rw0 = reinterpret_cast<const float4*>(sv.w + trow * 8)[0];
-      rw1 = reinterpret_cast<const float4*>(sv.w + trow * 8)[1];
-    }
-  };
   auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
-  fetch_recs(0);
-  // dq of earlier rounds for this thread's tokens of a tile, fetched while the previous
-  // tile's last scatter runs (global loads in flight slow the math's table reads)
-  constexpr int kPasses = kTile / (4 * tcb::kMathWarps);
-  static_assert(kPasses * 4 * tcb::kMathWarps == kTile, "token passes");
-  float4 prev[kPasses][2];
-  auto fetch_prev = [&](int tile_idx) {
-    const int nn0 = t_beg + tile_idx * kTile;
-    const int nnt = min(kTile, t_end - nn0);
-#pragma unroll
-    for (int it = 0; it < kPasses; ++it) {
-      const int t = 4 * (tid >> 5) + it * 4 * tcb::kMathWarps + ((tid & 31) >> 3);
-      prev[it][0] = prev[it][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (!first && t < nnt) {
-        const float4* acc =
-            reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + nn0 + t) * g.D + 8 * (tid & 7));
-        prev[it][0] = acc[0];
-        prev[it][1] = acc[1];
-      }
+  // picks of token tid of a tile (threads 0..63), read two tiles ahead
+  auto fetch_ix = [&](int j) -> uint2 {
+    uint2 v = make_uint2(0u, 0u);
+    const int n = t_beg + j * kBT;
+    if (j < ntiles && tid < min(kBT, t_end - n)) v = reinterpret_cast<const uint2*>(sv.idx)[rec0 + n + tid];
+    return v;
+  };
+  uint2 rq0 = fetch_ix(0), rq1 = fetch_ix(1);
+  // dq of earlier rounds for this thread's token and head dims of a tile, read a tile ahead
+  const int grp = lane >> 3, c8 = lane & 7;
+  const int tok = 4 * warp + grp;  // the token of this lane group within a tile
+  float4 pv0 = make_float4(0.f, 0.f, 0.f, 0.f), pv1 = pv0;
+  auto fetch_prev = [&](int j) {
+    pv0 = pv1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int n = t_beg + j * kBT;
+    if (!first && j < ntiles && tok < min(kBT, t_end - n)) {
+      const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n + tok) * g.D + 8 * c8);
+      pv0 = acc[0];
+      pv1 = acc[1];
     }
   };
   fetch_prev(0);
-  uint2 old_ix = make_uint2(0u, 0u);  // thread t's token row of P in the previous tile
-  bool old_live = false;
+  // P entries of the tile two back, per P buffer (threads 0..63): cleared before the buffer is reused
+  uint2 oix0 = make_uint2(0u, 0u), oix1 = oix0;
+  bool olive0 = false, olive1 = false;
 
+  bool stop = false;
   for (int tile = 0; tile < ntiles; ++tile) {
-    const int n0 = t_beg + tile * kTile;
-    const int nt = min(kTile, t_end - n0);
-    if (tid == tcb::kIssuer && tile + 1 < ntiles) {
-      // the next tile's inputs into L2 a tile ahead: its grad_out tile is loaded (and its
-      // records and earlier-round dq read) only once this tile's consumers are done
-      const int nn0 = n0 + kTile;
-      const int nnt = min(kTile, t_end - nn0);
-      const size_t trow = ((size_t)r * g.BH + bh) * g.N + nn0;
-      tma_prefetch_4d(&gmap, 0, nn0, h, b);
-      if (nnt >= 2) bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(sv.idx) + trow * 8, (uint32_t)(nnt * 8) & ~15u);
-      bulk_prefetch_l2(sv.w + trow * 8, (uint32_t)nnt * 32);
-      if (!first) bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(nnt * g.D * 4));
-      if (gw && first) {  // 28 bytes per token: the 16-byte aligned run inside
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(gw + ((size_t)bh * g.N + nn0) * kTopK);
-        const uintptr_t hi = lo + (uintptr_t)nnt * kTopK * 4;
-        const uintptr_t a0 = (lo + 15) & ~(uintptr_t)15, a1 = hi & ~(uintptr_t)15;
-        if (a1 > a0) bulk_prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
-      }
+    const int n0 = t_beg + tile * kBT;
+    const int nt = min(kBT, t_end - n0);
+    const int pb = tile & 1;
+    const uint32_t a_p = s_base + tcb::OFF_P + pb * tcb::kPBuf;
+    uint8_t* pbuf = sm + tcb::OFF_P + pb * tcb::kPBuf;
+    auto p_entry = [&](int t, int m) -> uint16_t* {
+      return reinterpret_cast<uint16_t*>(pbuf + (m >> 6) * tcb::kPBlock + sw128_offset(t, m & 63));
+    };
+    uint8_t* tix = sm + tcb::OFF_TIX + pb * kBT * 8;
+    const float* tw = reinterpret_cast<const float*>(sm + tcb::OFF_TW + pb * kBT * 32);
+    if (tid == tcb::kIssuer && !first && tile + 1 < ntiles) {  // next tile's earlier-round dq into L2
+      const int nn0 = n0 + kBT;
+      bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(min(kBT, t_end - nn0) * g.D * 4));
     }
-    // ---- records into shared memory; P rows: clear the previous tile's entries, then w ----
-    if (tid < kTile) {
-      if (old_live) {
+    // ---- records: P[pb] entries of tile-2 cleared, then this tile's weights ----
+    // (tile-2's last scatter finished before tile-1's first did, which every thread has waited for)
+    const uint2 rix = rq0;
+    rq0 = rq1;
+    if (tid < kBT) {
+      const bool ol = pb ? olive1 : olive0;
+      const uint2 oix = pb ? oix1 : oix0;
+      if (ol) {
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(old_ix, j)) = 0;
+        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(oix, j)) = 0;
       }
-      old_live = tid < nt;
-      if (old_live) {
+      const bool live = tid < nt;
+      if (live) {
         reinterpret_cast<uint2*>(tix)[tid] = rix;
-        reinterpret_cast<float4*>(tw)[2 * tid] = rw0;
-        reinterpret_cast<float4*>(tw)[2 * tid + 1] = rw1;
-        const float wv[kTopK] = {rw0.x, rw0.y, rw0.z, rw0.w, rw1.x, rw1.y, rw1.z};
+        if (!tcb::timed_wait(&bar_w[pb], (tile >> 1) & 1)) {
+          atomicOr(&g_device_error, tcb::kErrWait);
+          *s_abort = 1;
+        } else if (tid == tcb::kIssuer) {
+          w_done = tile;
+        }
+        const float4 w0 = reinterpret_cast<const float4*>(tw + tid * 8)[0];
+        const float4 w1 = reinterpret_cast<const float4*>(tw + tid * 8)[1];
+        const float wv[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(rix, j)) = hi_bits(wv[j]);
-        old_ix = rix;
       }
+      if (pb) { olive1 = live; oix1 = rix; }
+      else { olive0 = live; oix0 = rix; }
     }
     if (gw && first) {
       const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
       for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
     }
-    if (tid == tcb::kIssuer) {  // q / grad_out tiles (read below and by the MMAs)
-      const int bsl = tile & 1;
-      if (q_pending[bsl]) {
-        if (tcb::timed_wait(&bar_q[bsl], ph_q[bsl])) { ph_q[bsl] ^= 1; q_pending[bsl] = false; }
-        else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
-      }
-      if (g_pending) {
-        if (tcb::timed_wait(bar_g, ph_g)) { ph_g ^= 1; g_pending = false; }
-        else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
+    if (tid == tcb::kIssuer) {  // this tile's q and grad_out tiles (read below and by the MMAs)
+      if (!tcb::timed_wait(&bar_q[tile % 3], (tile / 3) & 1) || !tcb::timed_wait(&bar_g[pb], (tile >> 1) & 1)) {
+        atomicOr(&g_device_error, tcb::kErrWait);
+        *s_abort = 1;
+      } else {
+        qg_done = tile;
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    if (__syncthreads_or(*s_abort != 0)) break;  // one decision for all threads
+    if (__syncthreads_or(*s_abort != 0)) { stop = true; break; }  // one decision for all threads
     tc_fence_after();
+    const uint32_t a_q = s_base + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
+    const uint32_t a_g = s_base + tcb::OFF_G + pb * tcb::kTileBytes;
     if (tid == tcb::kIssuer) {  // dV (first term) runs during the token math
-      issue_scatter(a_g, tcb::COL_DV, tile == 0);
+      issue_scatter(a_p, a_g, tcb::COL_DV, tile == 0);
       mma_commit(bar_mma);
     }
 
-    // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp, 2 passes ----
-    const uint32_t a_q = s_base + tcb::OFF_Q + (tile & 1) * 16384;
-    const uint8_t* sq = sm + tcb::OFF_Q + (tile & 1) * 16384;
-    const uint8_t* sgo = sm + tcb::OFF_G;
-    const int grp = lane >> 3, c8 = lane & 7;
-    const bool math_warp = warp < tcb::kMathWarps;
-    bool p_free = false;  // has this thread seen the first scatter complete?
-#pragma unroll
-    for (int it = 0; it < kPasses; ++it) {
-      const int t0 = 4 * warp + it * 4 * tcb::kMathWarps;
-      if (!math_warp || t0 >= nt) break;   // warp-uniform
-      const int t = t0 + grp;
-      const bool live = t < nt;            // group-uniform
-      const int n = n0 + (live ? t : 0);
+    // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp ----
+    const uint8_t* sq = sm + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
+    const uint8_t* sgo = sm + tcb::OFF_G + pb * tcb::kTileBytes;
+    const bool live = tok < nt;         // group-uniform
+    const bool busy = 4 * warp < nt;    // warp-uniform
+    int ix[kTopK];
+    float w[kTopK], c[kTopK];
+    if (busy) {
+      const int t = live ? tok : 0;
+      const int n = n0 + t;
       const uint2 pk = reinterpret_cast<const uint2*>(tix)[t];
-      int ix[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) ix[j] = pick_of(pk, j);
       const float4 w0 = reinterpret_cast<const float4*>(tw + t * 8)[0];
       const float4 w1 = reinterpret_cast<const float4*>(tw + t * 8)[1];
-      const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
+      w[0] = w0.x; w[1] = w0.y; w[2] = w0.z; w[3] = w0.w; w[4] = w1.x; w[5] = w1.y; w[6] = w1.z;
       // swizzled 128-byte rows of the TMA tiles: 16-byte chunk c8 of row t
       const uint32_t rq = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
       const uint4 qv = *reinterpret_cast<const uint4*>(sq + rq);
       const uint4 gv = *reinterpret_cast<const uint4*>(sgo + rq);
-      float dq[8] = {prev[it][0].x, prev[it][0].y, prev[it][0].z, prev[it][0].w,
-                     prev[it][1].x, prev[it][1].y, prev[it][1].z, prev[it][1].w};
+      float dq[8] = {pv0.x, pv0.y, pv0.z, pv0.w, pv1.x, pv1.y, pv1.z, pv1.w};
       float part[8];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
@@ -613,7 +629,6 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         if (gw && first) dw[j] += tgw[t * 8 + j];
         s = fmaf(w[j], dw[j], s);
       }
-      float c[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         c[j] = g.scale * (w[j] * (dw[j] - s));
@@ -632,34 +647,26 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
           acc[1] = make_float4(dq[4], dq[5], dq[6], dq[7]);
         }
       }
-      // this token's P entries take the next phase's values once the first scatter is done
-      if (!p_free) {
-        wait_mma();
-        p_free = true;
-      }
-      if (live && c8 < kTopK) {
-        float wl = 0.f, cl = 0.f;
-        int ml = 0;
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j)
-          if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
-        coef[t * 8 + c8] = cl;
-        *p_entry(t, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
-      }
     }
-    if (!p_free) wait_mma();  // warps without tokens in this tile, and the issuer
-
-    // the next tile's records and earlier-round dq, in flight during the last scatter
-    if (tile + 1 < ntiles) {
-      fetch_recs(tile + 1);
-      fetch_prev(tile + 1);
+    // the next tiles' records and earlier-round dq, in flight during the scatter phases
+    rq1 = fetch_ix(tile + 2);
+    fetch_prev(tile + 1);
+    wait_mma();  // dV (first term) done: P takes the next term
+    if (busy && live && c8 < kTopK) {
+      float wl = 0.f, cl = 0.f;
+      int ml = 0;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j)
+        if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
+      coef[tok * 8 + c8] = cl;
+      *p_entry(tok, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
     }
 
     // ---- remaining scatter phases: fp16 dK; bf16 dV_lo, dK_hi, dK_lo ----
-    bool stop = false;
 #pragma unroll 1
     for (int ph = 1; ph < 2 * kTerms; ++ph) {
       const bool is_k = ph >= kTerms;
+      const bool last = ph == 2 * kTerms - 1;
       if (ph >= 2) {  // bf16: rewrite P with the coefficient terms (thread per token)
         if (tid < nt) {
           const uint2 pk = reinterpret_cast<const uint2*>(tix)[tid];
@@ -676,18 +683,24 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       tc_fence_after();
       if (stop) break;
       if (tid == tcb::kIssuer) {
-        // the math and the dV phases are done with the grad_out tile: fetch the next one
-        if (ph == kTerms && tile + 1 < ntiles) load_g(tile + 1);
-        issue_scatter(is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
-        mma_commit(bar_mma);
+        if (ph == 1 && tile + 2 < ntiles) load_w(tile + 2);  // the math is done with this tile's weights
+        if (ph == kTerms && tile + 2 < ntiles) {
+          // the dV phases are done with G[pb]; Q buffer (tile+2) mod 3 was last read by the
+          // scatters of tile-1, which finished before this tile's first did
+          load_g(tile + 2);
+          load_q(tile + 2);
+        }
+        issue_scatter(a_p, is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
+        if (!last) mma_commit(bar_mma);
       }
-      wait_mma();
+      if (!last) wait_mma();
     }
     if (stop) break;
-    // this q buffer is free: fetch the tile after next into it
-    if (tid == tcb::kIssuer && tile + 2 < ntiles && !*s_abort) load_q(tile + 2);
   }
 
+  // every scatter finished before TMEM is read (also drains the MMAs of an aborted tile)
+  if (tid == tcb::kIssuer) mma_commit(bar_mma);
+  wait_mma();
   // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
   if (warp < 8 && !__any_sync(0xffffffffu, *s_abort != 0)) {
     const int quad = warp & 3;
@@ -712,12 +725,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       }
     }
   }
-  if (tid == tcb::kIssuer) {
+  if (tid == tcb::kIssuer) {  // copies still in flight after an abort: wait for them (bounded)
     if (tab_pending) tcb::timed_wait(bar_tab, 0);
-    for (int i = 0; i < 2; ++i)
-      if (q_pending[i]) tcb::timed_wait(&bar_q[i], ph_q[i]);
-    if (g_pending) tcb::timed_wait(bar_g, ph_g);
-    if (*s_abort) tcb::timed_wait(bar_mma, ph_mma);
+    for (int j = qg_done + 1; j <= q_issued; ++j) tcb::timed_wait(&bar_q[j % 3], (j / 3) & 1);
+    for (int j = qg_done + 1; j <= g_issued; ++j) tcb::timed_wait(&bar_g[j & 1], (j >> 1) & 1);
+    for (int j = w_done + 1; j <= w_issued; ++j) tcb::timed_wait(&bar_w[j & 1], (j >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -740,7 +752,7 @@ static bool make_rows_map(CUtensorMap* map, const Geom& g, const void* base, Str
   cuuint64_t dims[4] = {(cuuint64_t)g.D, (cuuint64_t)g.N, (cuuint64_t)g.H, (cuuint64_t)g.B};
   cuuint64_t strides[3] = {(cuuint64_t)st.s[2] * esz, (cuuint64_t)st.s[1] * esz,
                            (cuuint64_t)(st.s[0] ? st.s[0] : 1) * esz};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, tcb::kBTile, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt =
       tcb::Fmt<T>::v == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
