@@ -36,9 +36,9 @@ extern __device__ int g_device_error;
 namespace tcb {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kMathWarps = 16;              // token math
-constexpr int kThreads = 32 * kMathWarps;
-constexpr int kIssuer = 0;                  // the thread that issues the MMAs and copies
+constexpr int kMathWarps = 16;              // token math (and the tiles' records)
+constexpr int kThreads = 32 * kMathWarps + 32;  // + one issuer warp
+constexpr int kIssuer = 32 * kMathWarps;    // the thread that issues the MMAs and copies
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
@@ -361,9 +361,11 @@ __global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8
 // Token side of round r
 // ---------------------------------------------------------------------------
 // Tiles of 64 tokens, software-pipelined: P, the grad_out tiles and the weight
-// records are double-buffered by tile parity and the q tiles triple-buffered, so
-// the last slot scatter of a tile (dK) runs under the next tile's records and
-// token math, and every copy is issued two tiles ahead of its use.
+// records are double-buffered by tile parity and the q tiles triple-buffered.
+// Warps 0-15 do the records and the token math (eight lanes per token), warp 16
+// issues every copy and MMA: a tile's last scatter (dK) is issued together with
+// the next tile's first (dV) and runs under that tile's math, and every copy is
+// issued two tiles ahead of its use.
 template <typename T>
 __global__ void __launch_bounds__(tcb::kThreads, 1)
     k_bwd_tokens_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
@@ -494,31 +496,36 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     return tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb)));
   };
   auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
-  // picks of token tid of a tile (threads 0..63), read two tiles ahead
+  const int grp = lane >> 3, c8 = lane & 7;
+  const int tok = 4 * warp + grp;  // the token of this lane group within a tile (math warps)
+  // picks of this lane group's token of a tile, read two tiles ahead
   auto fetch_ix = [&](int j) -> uint2 {
     uint2 v = make_uint2(0u, 0u);
     const int n = t_beg + j * kBT;
-    if (j < ntiles && tid < min(kBT, t_end - n)) v = reinterpret_cast<const uint2*>(sv.idx)[rec0 + n + tid];
+    if (tid < tcb::kIssuer && j < ntiles && tok < min(kBT, t_end - n))
+      v = reinterpret_cast<const uint2*>(sv.idx)[rec0 + n + tok];
     return v;
   };
   uint2 rq0 = fetch_ix(0), rq1 = fetch_ix(1);
   // dq of earlier rounds for this thread's token and head dims of a tile, read a tile ahead
-  const int grp = lane >> 3, c8 = lane & 7;
-  const int tok = 4 * warp + grp;  // the token of this lane group within a tile
   float4 pv0 = make_float4(0.f, 0.f, 0.f, 0.f), pv1 = pv0;
   auto fetch_prev = [&](int j) {
     pv0 = pv1 = make_float4(0.f, 0.f, 0.f, 0.f);
     const int n = t_beg + j * kBT;
-    if (!first && j < ntiles && tok < min(kBT, t_end - n)) {
+    if (tid < tcb::kIssuer && !first && j < ntiles && tok < min(kBT, t_end - n)) {
       const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n + tok) * g.D + 8 * c8);
       pv0 = acc[0];
       pv1 = acc[1];
     }
   };
   fetch_prev(0);
-  // P entries of the tile two back, per P buffer (threads 0..63): cleared before the buffer is reused
-  uint2 oix0 = make_uint2(0u, 0u), oix1 = oix0;
-  bool olive0 = false, olive1 = false;
+  // this lane's P entry of the tile two back, per P buffer (-1: none): cleared before the buffer is reused
+  int oslot0 = -1, oslot1 = -1;
+  const bool math_thread = tid < tcb::kIssuer;
+  auto last_phase = [&](int j) {  // issuer: the deferred last scatter of tile j (fp16 dK; bf16 dK_lo)
+    issue_scatter(s_base + tcb::OFF_P + (j & 1) * tcb::kPBuf, s_base + tcb::OFF_Q + (j % 3) * tcb::kTileBytes,
+                  tcb::COL_DK, j == 0 && kTerms == 1);
+  };
 
   bool stop = false;
   for (int tile = 0; tile < ntiles; ++tile) {
@@ -536,45 +543,38 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       const int nn0 = n0 + kBT;
       bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(min(kBT, t_end - nn0) * g.D * 4));
     }
-    // ---- records: P[pb] entries of tile-2 cleared, then this tile's weights ----
+    // ---- records: P[pb] entries of tile-2 cleared, then this tile's weights (lane c8: pick c8) ----
     // (tile-2's last scatter finished before tile-1's first did, which every thread has waited for)
     const uint2 rix = rq0;
     rq0 = rq1;
-    if (tid < kBT) {
-      const bool ol = pb ? olive1 : olive0;
-      const uint2 oix = pb ? oix1 : oix0;
-      if (ol) {
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(oix, j)) = 0;
-      }
-      const bool live = tid < nt;
-      if (live) {
-        reinterpret_cast<uint2*>(tix)[tid] = rix;
+    if (math_thread) {
+      const int os = pb ? oslot1 : oslot0;
+      if (os >= 0) *p_entry(tok, os) = 0;
+      __syncwarp();  // every old entry of the token is cleared before any new one is written
+      int ns = -1;
+      if (tok < nt && c8 < kTopK) {
         if (!tcb::timed_wait(&bar_w[pb], (tile >> 1) & 1)) {
           atomicOr(&g_device_error, tcb::kErrWait);
           *s_abort = 1;
-        } else if (tid == tcb::kIssuer) {
-          w_done = tile;
         }
-        const float4 w0 = reinterpret_cast<const float4*>(tw + tid * 8)[0];
-        const float4 w1 = reinterpret_cast<const float4*>(tw + tid * 8)[1];
-        const float wv[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z};
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) *p_entry(tid, pick_of(rix, j)) = hi_bits(wv[j]);
+        ns = pick_of(rix, c8);
+        *p_entry(tok, ns) = hi_bits(tw[tok * 8 + c8]);
       }
-      if (pb) { olive1 = live; oix1 = rix; }
-      else { olive0 = live; oix0 = rix; }
+      if (tok < nt && c8 == 0) reinterpret_cast<uint2*>(tix)[tok] = rix;
+      if (pb) oslot1 = ns;
+      else oslot0 = ns;
     }
     if (gw && first) {
       const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
       for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
     }
-    if (tid == tcb::kIssuer) {  // this tile's q and grad_out tiles (read below and by the MMAs)
-      if (!tcb::timed_wait(&bar_q[tile % 3], (tile / 3) & 1) || !tcb::timed_wait(&bar_g[pb], (tile >> 1) & 1)) {
+    if (tid == tcb::kIssuer) {  // this tile's q, grad_out and weight copies (read below and by the MMAs)
+      if (!tcb::timed_wait(&bar_q[tile % 3], (tile / 3) & 1) || !tcb::timed_wait(&bar_g[pb], (tile >> 1) & 1) ||
+          !tcb::timed_wait(&bar_w[pb], (tile >> 1) & 1)) {
         atomicOr(&g_device_error, tcb::kErrWait);
         *s_abort = 1;
       } else {
-        qg_done = tile;
+        qg_done = w_done = tile;
       }
     }
     fence_proxy_async_smem();
@@ -583,7 +583,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     tc_fence_after();
     const uint32_t a_q = s_base + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
     const uint32_t a_g = s_base + tcb::OFF_G + pb * tcb::kTileBytes;
-    if (tid == tcb::kIssuer) {  // dV (first term) runs during the token math
+    if (tid == tcb::kIssuer) {  // the previous tile's last scatter and this tile's dV (first term)
+      if (tile > 0) last_phase(tile - 1);
       issue_scatter(a_p, a_g, tcb::COL_DV, tile == 0);
       mma_commit(bar_mma);
     }
@@ -592,7 +593,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     const uint8_t* sq = sm + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
     const uint8_t* sgo = sm + tcb::OFF_G + pb * tcb::kTileBytes;
     const bool live = tok < nt;         // group-uniform
-    const bool busy = 4 * warp < nt;    // warp-uniform
+    const bool busy = math_thread && 4 * warp < nt;  // warp-uniform
     int ix[kTopK];
     float w[kTopK], c[kTopK];
     if (busy) {
@@ -667,14 +668,10 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     for (int ph = 1; ph < 2 * kTerms; ++ph) {
       const bool is_k = ph >= kTerms;
       const bool last = ph == 2 * kTerms - 1;
-      if (ph >= 2) {  // bf16: rewrite P with the coefficient terms (thread per token)
-        if (tid < nt) {
-          const uint2 pk = reinterpret_cast<const uint2*>(tix)[tid];
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) {
-            const float x = coef[tid * 8 + j];
-            *p_entry(tid, pick_of(pk, j)) = (ph == 2) ? hi_bits(x) : lo_bits(x);
-          }
+      if (ph >= 2) {  // bf16: rewrite P with the coefficient terms (lane c8: pick c8)
+        if (math_thread && tok < nt && c8 < kTopK) {
+          const float x = coef[tok * 8 + c8];
+          *p_entry(tok, pick_of(reinterpret_cast<const uint2*>(tix)[tok], c8)) = (ph == 2) ? hi_bits(x) : lo_bits(x);
         }
       }
       fence_proxy_async_smem();
@@ -690,8 +687,10 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
           load_g(tile + 2);
           load_q(tile + 2);
         }
-        issue_scatter(a_p, is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
-        if (!last) mma_commit(bar_mma);
+        if (!last) {  // the last phase is issued with the next tile's first
+          issue_scatter(a_p, is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
+          mma_commit(bar_mma);
+        }
       }
       if (!last) wait_mma();
     }
@@ -699,7 +698,10 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   }
 
   // every scatter finished before TMEM is read (also drains the MMAs of an aborted tile)
-  if (tid == tcb::kIssuer) mma_commit(bar_mma);
+  if (tid == tcb::kIssuer) {
+    if (!stop && ntiles > 0) last_phase(ntiles - 1);
+    mma_commit(bar_mma);
+  }
   wait_mma();
   // ---- chunk partials of dK_r, dV_r (TMEM lanes are slots): warps 0-3 dV, 4-7 dK ----
   if (warp < 8 && !__any_sync(0xffffffffu, *s_abort != 0)) {
