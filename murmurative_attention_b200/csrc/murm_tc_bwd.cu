@@ -49,11 +49,11 @@ constexpr uint32_t kPBuf = 4 * kPBlock;              // P of one tile: 256 slots
 constexpr uint32_t OFF_DW = kTables;                 // fp32 [256]
 constexpr uint32_t OFF_P = OFF_DW + 1024;            // P[2] by tile parity (1024-aligned)
 constexpr uint32_t OFF_Q = OFF_P + 2 * kPBuf;        // q tiles [3] by tile mod 3 (MMA operand)
-constexpr uint32_t OFF_G = OFF_Q + 3 * kTileBytes;   // grad_out tiles [2] by tile parity
-constexpr uint32_t OFF_TW = OFF_G + 2 * kTileBytes;  // fp32 [2][64][8] weights of the tiles' tokens
-constexpr uint32_t OFF_COEF = OFF_TW + 2 * kBTile * 32;  // fp32 [64][8] scale*da per pick
-constexpr uint32_t OFF_TGW = OFF_COEF + kBTile * 32;     // fp32 [64][8] dL/d weights (last round)
-constexpr uint32_t OFF_TIX = OFF_TGW + kBTile * 32;      // u8 [2][64][8] picks
+constexpr uint32_t OFF_G = OFF_Q + 3 * kTileBytes;   // grad_out tiles [3] by tile mod 3
+constexpr uint32_t OFF_TW = OFF_G + 3 * kTileBytes;  // fp32 [3][64][8] weights of the tiles' tokens
+constexpr uint32_t OFF_COEF = OFF_TW + 3 * kBTile * 32;  // fp32 [64][8] scale*da per pick
+constexpr uint32_t OFF_TGW = OFF_COEF + kBTile * 32;     // fp32 [2][64][8] dL/d weights (last round)
+constexpr uint32_t OFF_TIX = OFF_TGW + 2 * kBTile * 32;  // u8 [2][64][8] picks
 constexpr uint32_t OFF_MISC = OFF_TIX + 2 * kBTile * 8;
 constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -360,12 +360,14 @@ __global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8
 // ---------------------------------------------------------------------------
 // Token side of round r
 // ---------------------------------------------------------------------------
-// Tiles of 64 tokens, software-pipelined: P, the grad_out tiles and the weight
-// records are double-buffered by tile parity and the q tiles triple-buffered.
-// Warps 0-15 do the records and the token math (eight lanes per token), warp 16
-// issues every copy and MMA: a tile's last scatter (dK) is issued together with
-// the next tile's first (dV) and runs under that tile's math, and every copy is
-// issued two tiles ahead of its use.
+// Tiles of 64 tokens, software-pipelined with one block barrier per tile (fp16):
+//   barrier(i) -> issuer: last scatter of tile i-1 + first scatter of tile i, copies of tile i+2
+//              -> warps 0-15: token math of tile i; wait for the scatters; coefficients of tile i
+//                 into P[i & 1] and the weights of tile i+1 into P[(i+1) & 1]
+//              -> barrier(i+1)
+// P and the picks are double-buffered by tile parity, the q / grad_out tiles and weight records
+// triple-buffered by tile mod 3; every copy is issued two tiles ahead of its use. Eight lanes
+// share a token (8 head dims each), a warp takes 4 tokens; warp 16 issues every copy and MMA.
 template <typename T>
 __global__ void __launch_bounds__(tcb::kThreads, 1)
     k_bwd_tokens_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
@@ -376,14 +378,13 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const uint32_t s_base = smem_u32(sm);
   uint64_t* bar_tab = reinterpret_cast<uint64_t*>(sm + tcb::OFF_MISC);
   uint64_t* bar_q = bar_tab + 1;  // [3], by tile mod 3
-  uint64_t* bar_g = bar_tab + 4;  // [2], by tile parity
-  uint64_t* bar_w = bar_tab + 6;  // [2], by tile parity
-  uint64_t* bar_mma = bar_tab + 8;
+  uint64_t* bar_g = bar_tab + 4;  // [3], by tile mod 3
+  uint64_t* bar_w = bar_tab + 7;  // [3], by tile mod 3
+  uint64_t* bar_mma = bar_tab + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + tcb::OFF_MISC + 96);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + tcb::OFF_MISC + 100);
   const float* dWs = reinterpret_cast<const float*>(sm + tcb::OFF_DW);
   float* coef = reinterpret_cast<float*>(sm + tcb::OFF_COEF);
-  float* tgw = reinterpret_cast<float*>(sm + tcb::OFF_TGW);
 
   constexpr int kBT = tcb::kBTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -394,12 +395,15 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const bool has_slot_grad = r < g.R - 1;
   const bool first = (r == g.R - 1);
   const size_t rec0 = ((size_t)r * g.BH + bh) * g.N;  // record row of token 0 of this (b, h)
+  const bool math_thread = tid < tcb::kIssuer;
+  const int grp = lane >> 3, c8 = lane & 7;
+  const int tok = 4 * warp + grp;  // the token of this lane group within a tile (math warps)
   constexpr uint32_t ID_UPD = idesc_f16(tcb::Fmt<T>::v, 128, 64, 1, 1);
 
   if (tid == tcb::kIssuer) {
     mbar_init(bar_tab, 1);
-    for (int i = 0; i < 3; ++i) mbar_init(&bar_q[i], 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bar_q[i], 1);
       mbar_init(&bar_g[i], 1);
       mbar_init(&bar_w[i], 1);
     }
@@ -422,7 +426,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   uint32_t ph_mma = 0;
   // the issuer's bookkeeping of asynchronous copies: the last tile issued / waited for
-  int q_issued = -1, g_issued = -1, w_issued = -1, qg_done = -1, w_done = -1;
+  int q_issued = -1, g_issued = -1, w_issued = -1, q_done = -1, g_done = -1, w_done = -1;
   bool tab_pending = false;
   auto load_q = [&](int j) {  // issuer
     const int s = j % 3;
@@ -431,18 +435,26 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     q_issued = j;
   };
   auto load_g = [&](int j) {  // issuer
-    const int s = j & 1;
+    const int s = j % 3;
     mbar_arrive_expect_tx(&bar_g[s], tcb::kTileBytes);
     tma_load_4d(sm + tcb::OFF_G + s * tcb::kTileBytes, &gmap, 0, t_beg + j * kBT, h, b, &bar_g[s]);
     g_issued = j;
   };
   auto load_w = [&](int j) {  // issuer: the tile's softmax weights, 32 bytes per token
-    const int s = j & 1;
+    const int s = j % 3;
     const int n = t_beg + j * kBT;
     const uint32_t bytes = (uint32_t)min(kBT, t_end - n) * 32u;
     mbar_arrive_expect_tx(&bar_w[s], bytes);
     bulk_g2s(sm + tcb::OFF_TW + s * kBT * 32, sv.w + (rec0 + n) * 8, bytes, &bar_w[s]);
     w_issued = j;
+  };
+  auto wait_copy = [&](uint64_t* bar, int j, int& done) {  // issuer
+    if (tcb::timed_wait(bar, (j / 3) & 1)) {
+      done = j;
+    } else {
+      atomicOr(&g_device_error, tcb::kErrWait);
+      *s_abort = 1;
+    }
   };
   if (tid == tcb::kIssuer) {
     mbar_arrive_expect_tx(bar_tab, tcb::kTables + 1024);
@@ -462,12 +474,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   } else if (tid == tcb::kIssuer) {
     tab_pending = false;
   }
-  __syncthreads();
 
   const uint8_t* tK = sm + tcb::OFF_K;
   const uint8_t* tV = sm + tcb::OFF_V;
   const uint8_t* tS = sm + tcb::OFF_DS;
-  // D += P^T . B over the tile's 64 tokens (issuer): two 128-slot halves, four k-steps of 16 tokens
+  // D += P^T . B over a tile's 64 tokens (issuer): two 128-slot halves, four k-steps of 16 tokens
   auto issue_scatter = [&](uint32_t a_p, uint32_t a_b, uint32_t col, bool first_acc) {
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh)
@@ -483,12 +494,28 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     else { atomicOr(&g_device_error, tcb::kErrWait); *s_abort = 1; }
     tc_fence_after();
   };
+  auto p_addr = [&](int j) { return s_base + tcb::OFF_P + (j & 1) * tcb::kPBuf; };
+  auto q_addr = [&](int j) { return s_base + tcb::OFF_Q + (j % 3) * tcb::kTileBytes; };
+  auto g_addr = [&](int j) { return s_base + tcb::OFF_G + (j % 3) * tcb::kTileBytes; };
+  auto p_entry = [&](int j, int t, int m) -> uint16_t* {  // P of tile j: token t, slot m
+    return reinterpret_cast<uint16_t*>(sm + tcb::OFF_P + (j & 1) * tcb::kPBuf + (m >> 6) * tcb::kPBlock +
+                                       sw128_offset(t, m & 63));
+  };
+  auto tix_of = [&](int j) { return reinterpret_cast<uint2*>(sm + tcb::OFF_TIX + (j & 1) * kBT * 8); };
+  auto tw_of = [&](int j) { return reinterpret_cast<const float*>(sm + tcb::OFF_TW + (j % 3) * kBT * 32); };
+  auto tgw_of = [&](int j) { return reinterpret_cast<float*>(sm + tcb::OFF_TGW + (j & 1) * kBT * 32); };
+  auto fill_tgw = [&](int j) {  // dL/d weights of tile j (last round, when given)
+    const int n = t_beg + j * kBT;
+    const float* src = gw + ((size_t)bh * g.N + n) * kTopK;
+    float* dst = tgw_of(j);
+    for (int e = tid; e < min(kBT, t_end - n) * kTopK; e += tcb::kThreads) dst[(e / kTopK) * 8 + e % kTopK] = src[e];
+  };
 
   // Scatter phases over P (64 tokens x 256 slots, one term per phase):
   //   fp16: dV += P^T.G (P = w) during the token math, then dK += P^T.Q (P = scale*da);
   //   bf16: weights and coefficients go in as two terms each (hi = rn(x), lo = rn(x - hi)),
   //         since bf16 alone rounds them to 2^-9: dV_hi during the math, then dV_lo, dK_hi, dK_lo.
-  // The last phase is not waited for: its completion is implied by the next tile's first.
+  // The last phase is issued with the next tile's first (and is waited for with it).
   constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
   auto hi_bits = [](float x) -> uint16_t { return tcb::bits<T>(x); };
   auto lo_bits = [](float x) -> uint16_t {
@@ -496,119 +523,104 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     return tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb)));
   };
   auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
-  const int grp = lane >> 3, c8 = lane & 7;
-  const int tok = 4 * warp + grp;  // the token of this lane group within a tile (math warps)
-  // picks of this lane group's token of a tile, read two tiles ahead
+  auto last_phase = [&](int j) {  // issuer: the deferred last scatter of tile j (fp16 dK; bf16 dK_lo)
+    issue_scatter(p_addr(j), q_addr(j), tcb::COL_DK, j == 0 && kTerms == 1);
+  };
+  // picks of this lane group's token of a tile
   auto fetch_ix = [&](int j) -> uint2 {
     uint2 v = make_uint2(0u, 0u);
     const int n = t_beg + j * kBT;
-    if (tid < tcb::kIssuer && j < ntiles && tok < min(kBT, t_end - n))
-      v = reinterpret_cast<const uint2*>(sv.idx)[rec0 + n + tok];
+    if (math_thread && j < ntiles && tok < min(kBT, t_end - n)) v = reinterpret_cast<const uint2*>(sv.idx)[rec0 + n + tok];
     return v;
   };
-  uint2 rq0 = fetch_ix(0), rq1 = fetch_ix(1);
   // dq of earlier rounds for this thread's token and head dims of a tile, read a tile ahead
   float4 pv0 = make_float4(0.f, 0.f, 0.f, 0.f), pv1 = pv0;
   auto fetch_prev = [&](int j) {
     pv0 = pv1 = make_float4(0.f, 0.f, 0.f, 0.f);
     const int n = t_beg + j * kBT;
-    if (tid < tcb::kIssuer && !first && j < ntiles && tok < min(kBT, t_end - n)) {
+    if (math_thread && !first && j < ntiles && tok < min(kBT, t_end - n)) {
       const float4* acc = reinterpret_cast<const float4*>(bs.dq + ((size_t)bh * g.N + n + tok) * g.D + 8 * c8);
       pv0 = acc[0];
       pv1 = acc[1];
     }
   };
-  fetch_prev(0);
-  // this lane's P entry of the tile two back, per P buffer (-1: none): cleared before the buffer is reused
-  int oslot0 = -1, oslot1 = -1;
-  const bool math_thread = tid < tcb::kIssuer;
-  auto last_phase = [&](int j) {  // issuer: the deferred last scatter of tile j (fp16 dK; bf16 dK_lo)
-    issue_scatter(s_base + tcb::OFF_P + (j & 1) * tcb::kPBuf, s_base + tcb::OFF_Q + (j % 3) * tcb::kTileBytes,
-                  tcb::COL_DK, j == 0 && kTerms == 1);
+  // Records of tile j into P[j & 1] (lane c8: pick c8): the entry of tile j-2 is cleared first.
+  // Tile j-2's last scatter finished before tile j-1's first did, which every thread has waited for.
+  int oslot0 = -1, oslot1 = -1;  // this lane's entry in P[0] / P[1] (-1: none)
+  auto records = [&](int j, uint2 rix) {
+    const int nn = min(kBT, t_end - (t_beg + j * kBT));
+    const int os = (j & 1) ? oslot1 : oslot0;
+    if (os >= 0) *p_entry(j, tok, os) = 0;
+    __syncwarp();  // every old entry of the token is cleared before any new one is written
+    int ns = -1;
+    if (tok < nn && c8 < kTopK) {
+      if (!tcb::timed_wait(&bar_w[j % 3], (j / 3) & 1)) {
+        atomicOr(&g_device_error, tcb::kErrWait);
+        *s_abort = 1;
+      }
+      ns = pick_of(rix, c8);
+      *p_entry(j, tok, ns) = hi_bits(tw_of(j)[tok * 8 + c8]);
+    }
+    if (tok < nn && c8 == 0) tix_of(j)[tok] = rix;
+    if (j & 1) oslot1 = ns;
+    else oslot0 = ns;
   };
+
+  fetch_prev(0);
+  if (math_thread && ntiles > 0) records(0, fetch_ix(0));
+  if (gw && first && ntiles > 0) fill_tgw(0);
+  uint2 rq = fetch_ix(1);  // picks for the next records
+  if (tid == tcb::kIssuer && ntiles > 0) {
+    wait_copy(&bar_q[0], 0, q_done);
+    wait_copy(&bar_g[0], 0, g_done);
+    wait_copy(&bar_w[0], 0, w_done);
+  }
 
   bool stop = false;
   for (int tile = 0; tile < ntiles; ++tile) {
     const int n0 = t_beg + tile * kBT;
     const int nt = min(kBT, t_end - n0);
-    const int pb = tile & 1;
-    const uint32_t a_p = s_base + tcb::OFF_P + pb * tcb::kPBuf;
-    uint8_t* pbuf = sm + tcb::OFF_P + pb * tcb::kPBuf;
-    auto p_entry = [&](int t, int m) -> uint16_t* {
-      return reinterpret_cast<uint16_t*>(pbuf + (m >> 6) * tcb::kPBlock + sw128_offset(t, m & 63));
-    };
-    uint8_t* tix = sm + tcb::OFF_TIX + pb * kBT * 8;
-    const float* tw = reinterpret_cast<const float*>(sm + tcb::OFF_TW + pb * kBT * 32);
-    if (tid == tcb::kIssuer && !first && tile + 1 < ntiles) {  // next tile's earlier-round dq into L2
-      const int nn0 = n0 + kBT;
-      bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(min(kBT, t_end - nn0) * g.D * 4));
-    }
-    // ---- records: P[pb] entries of tile-2 cleared, then this tile's weights (lane c8: pick c8) ----
-    // (tile-2's last scatter finished before tile-1's first did, which every thread has waited for)
-    const uint2 rix = rq0;
-    rq0 = rq1;
-    if (math_thread) {
-      const int os = pb ? oslot1 : oslot0;
-      if (os >= 0) *p_entry(tok, os) = 0;
-      __syncwarp();  // every old entry of the token is cleared before any new one is written
-      int ns = -1;
-      if (tok < nt && c8 < kTopK) {
-        if (!tcb::timed_wait(&bar_w[pb], (tile >> 1) & 1)) {
-          atomicOr(&g_device_error, tcb::kErrWait);
-          *s_abort = 1;
-        }
-        ns = pick_of(rix, c8);
-        *p_entry(tok, ns) = hi_bits(tw[tok * 8 + c8]);
-      }
-      if (tok < nt && c8 == 0) reinterpret_cast<uint2*>(tix)[tok] = rix;
-      if (pb) oslot1 = ns;
-      else oslot0 = ns;
-    }
-    if (gw && first) {
-      const float* src = gw + ((size_t)bh * g.N + n0) * kTopK;
-      for (int e = tid; e < nt * kTopK; e += tcb::kThreads) tgw[(e / kTopK) * 8 + e % kTopK] = src[e];
-    }
-    if (tid == tcb::kIssuer) {  // this tile's q, grad_out and weight copies (read below and by the MMAs)
-      if (!tcb::timed_wait(&bar_q[tile % 3], (tile / 3) & 1) || !tcb::timed_wait(&bar_g[pb], (tile >> 1) & 1) ||
-          !tcb::timed_wait(&bar_w[pb], (tile >> 1) & 1)) {
-        atomicOr(&g_device_error, tcb::kErrWait);
-        *s_abort = 1;
-      } else {
-        qg_done = w_done = tile;
-      }
-    }
     fence_proxy_async_smem();
     tc_fence_before();
     if (__syncthreads_or(*s_abort != 0)) { stop = true; break; }  // one decision for all threads
     tc_fence_after();
-    const uint32_t a_q = s_base + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
-    const uint32_t a_g = s_base + tcb::OFF_G + pb * tcb::kTileBytes;
-    if (tid == tcb::kIssuer) {  // the previous tile's last scatter and this tile's dV (first term)
+    if (tid == tcb::kIssuer) {
       if (tile > 0) last_phase(tile - 1);
-      issue_scatter(a_p, a_g, tcb::COL_DV, tile == 0);
+      issue_scatter(p_addr(tile), g_addr(tile), tcb::COL_DV, tile == 0);  // dV (first term)
       mma_commit(bar_mma);
+      if (tile + 2 < ntiles) {  // buffers (tile+2) mod 3 were last read by tile-1's math and dV phases
+        load_g(tile + 2);
+        load_w(tile + 2);
+      }
+      if (!first && tile + 1 < ntiles) {  // next tile's earlier-round dq into L2
+        const int nn0 = n0 + kBT;
+        bulk_prefetch_l2(bs.dq + ((size_t)bh * g.N + nn0) * g.D, (uint32_t)(min(kBT, t_end - nn0) * g.D * 4));
+      }
     }
 
     // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp ----
     const uint8_t* sq = sm + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
-    const uint8_t* sgo = sm + tcb::OFF_G + pb * tcb::kTileBytes;
-    const bool live = tok < nt;         // group-uniform
+    const uint8_t* sgo = sm + tcb::OFF_G + (tile % 3) * tcb::kTileBytes;
+    const uint2* tix = tix_of(tile);
+    const float* tw = tw_of(tile);
+    const float* tgw = tgw_of(tile);
+    const bool live = tok < nt;                      // group-uniform
     const bool busy = math_thread && 4 * warp < nt;  // warp-uniform
     int ix[kTopK];
     float w[kTopK], c[kTopK];
     if (busy) {
       const int t = live ? tok : 0;
       const int n = n0 + t;
-      const uint2 pk = reinterpret_cast<const uint2*>(tix)[t];
+      const uint2 pk = tix[t];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) ix[j] = pick_of(pk, j);
       const float4 w0 = reinterpret_cast<const float4*>(tw + t * 8)[0];
       const float4 w1 = reinterpret_cast<const float4*>(tw + t * 8)[1];
       w[0] = w0.x; w[1] = w0.y; w[2] = w0.z; w[3] = w0.w; w[4] = w1.x; w[5] = w1.y; w[6] = w1.z;
       // swizzled 128-byte rows of the TMA tiles: 16-byte chunk c8 of row t
-      const uint32_t rq = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
-      const uint4 qv = *reinterpret_cast<const uint4*>(sq + rq);
-      const uint4 gv = *reinterpret_cast<const uint4*>(sgo + rq);
+      const uint32_t rw = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
+      const uint4 qv = *reinterpret_cast<const uint4*>(sq + rw);
+      const uint4 gv = *reinterpret_cast<const uint4*>(sgo + rw);
       float dq[8] = {pv0.x, pv0.y, pv0.z, pv0.w, pv1.x, pv1.y, pv1.z, pv1.w};
       float part[8];
 #pragma unroll
@@ -649,30 +661,32 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
         }
       }
     }
-    // the next tiles' records and earlier-round dq, in flight during the scatter phases
-    rq1 = fetch_ix(tile + 2);
+    // the next tile's earlier-round dq, in flight during the scatter wait
     fetch_prev(tile + 1);
-    wait_mma();  // dV (first term) done: P takes the next term
-    if (busy && live && c8 < kTopK) {
+    wait_mma();  // tile-1's last scatter and this tile's first are done
+    if (tid == tcb::kIssuer && tile + 2 < ntiles) load_q(tile + 2);  // its buffer was last read by tile-1's dK
+    if (busy && live && c8 < kTopK) {  // P[tile & 1] takes the next term
       float wl = 0.f, cl = 0.f;
       int ml = 0;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j)
         if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
       coef[tok * 8 + c8] = cl;
-      *p_entry(tok, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
+      *p_entry(tile, tok, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
     }
+    // the next tile's weights into P[(tile+1) & 1] (free: tile-1's dK is done)
+    if (math_thread && tile + 1 < ntiles) {
+      records(tile + 1, rq);
+      rq = fetch_ix(tile + 2);
+    }
+    if (gw && first && tile + 1 < ntiles) fill_tgw(tile + 1);  // its buffer was last read by tile-1's math
 
-    // ---- remaining scatter phases: fp16 dK; bf16 dV_lo, dK_hi, dK_lo ----
+    // ---- bf16: dV_lo, dK_hi (the last phase, dK_lo, is issued with the next tile's first) ----
 #pragma unroll 1
-    for (int ph = 1; ph < 2 * kTerms; ++ph) {
+    for (int ph = 1; ph < 2 * kTerms - 1; ++ph) {
       const bool is_k = ph >= kTerms;
-      const bool last = ph == 2 * kTerms - 1;
-      if (ph >= 2) {  // bf16: rewrite P with the coefficient terms (lane c8: pick c8)
-        if (math_thread && tok < nt && c8 < kTopK) {
-          const float x = coef[tok * 8 + c8];
-          *p_entry(tok, pick_of(reinterpret_cast<const uint2*>(tix)[tok], c8)) = (ph == 2) ? hi_bits(x) : lo_bits(x);
-        }
+      if (ph >= 2 && math_thread && tok < nt && c8 < kTopK) {  // P takes the coefficient's high term
+        *p_entry(tile, tok, pick_of(tix[tok], c8)) = hi_bits(coef[tok * 8 + c8]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -680,24 +694,28 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       tc_fence_after();
       if (stop) break;
       if (tid == tcb::kIssuer) {
-        if (ph == 1 && tile + 2 < ntiles) load_w(tile + 2);  // the math is done with this tile's weights
-        if (ph == kTerms && tile + 2 < ntiles) {
-          // the dV phases are done with G[pb]; Q buffer (tile+2) mod 3 was last read by the
-          // scatters of tile-1, which finished before this tile's first did
-          load_g(tile + 2);
-          load_q(tile + 2);
-        }
-        if (!last) {  // the last phase is issued with the next tile's first
-          issue_scatter(a_p, is_k ? a_q : a_g, is_k ? tcb::COL_DK : tcb::COL_DV, tile == 0 && is_k && ph == kTerms);
-          mma_commit(bar_mma);
-        }
+        issue_scatter(p_addr(tile), is_k ? q_addr(tile) : g_addr(tile), is_k ? tcb::COL_DK : tcb::COL_DV,
+                      tile == 0 && is_k && ph == kTerms);
+        mma_commit(bar_mma);
       }
-      if (!last) wait_mma();
+      wait_mma();
     }
     if (stop) break;
+    if (kTerms == 2 && math_thread && tok < nt && c8 < kTopK)  // bf16: the coefficient's low term
+      *p_entry(tile, tok, pick_of(tix[tok], c8)) = lo_bits(coef[tok * 8 + c8]);
+    if (tid == tcb::kIssuer && tile + 1 < ntiles) {  // the next tile's copies (issued two tiles ago)
+      wait_copy(&bar_q[(tile + 1) % 3], tile + 1, q_done);
+      wait_copy(&bar_g[(tile + 1) % 3], tile + 1, g_done);
+      wait_copy(&bar_w[(tile + 1) % 3], tile + 1, w_done);
+    }
   }
 
-  // every scatter finished before TMEM is read (also drains the MMAs of an aborted tile)
+  // the last tile's last scatter, once its P entries are written; every scatter finished before
+  // TMEM is read (this also drains the MMAs of an aborted tile)
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (tid == tcb::kIssuer) {
     if (!stop && ntiles > 0) last_phase(ntiles - 1);
     mma_commit(bar_mma);
@@ -729,9 +747,9 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   }
   if (tid == tcb::kIssuer) {  // copies still in flight after an abort: wait for them (bounded)
     if (tab_pending) tcb::timed_wait(bar_tab, 0);
-    for (int j = qg_done + 1; j <= q_issued; ++j) tcb::timed_wait(&bar_q[j % 3], (j / 3) & 1);
-    for (int j = qg_done + 1; j <= g_issued; ++j) tcb::timed_wait(&bar_g[j & 1], (j >> 1) & 1);
-    for (int j = w_done + 1; j <= w_issued; ++j) tcb::timed_wait(&bar_w[j & 1], (j >> 1) & 1);
+    for (int j = q_done + 1; j <= q_issued; ++j) tcb::timed_wait(&bar_q[j % 3], (j / 3) & 1);
+    for (int j = g_done + 1; j <= g_issued; ++j) tcb::timed_wait(&bar_g[j % 3], (j / 3) & 1);
+    for (int j = w_done + 1; j <= w_issued; ++j) tcb::timed_wait(&bar_w[j % 3], (j / 3) & 1);
   }
   tc_fence_before();
   __syncthreads();
