@@ -46,8 +46,10 @@ constexpr int kThreads = kRowThreads + 32;
 constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns: scores | slot sums S (2 halves) | weight sums W (2 halves) | exchange | attend output O
-constexpr uint32_t COL_S = 0, COL_U = 256, COL_W = 384, COL_X = 416, COL_O = 448;
+// TMEM columns: scores | slot sums S and weight sums W (2 halves of 80: 64 S columns, then 16
+// columns that each hold W) | exchange | attend output O
+constexpr uint32_t COL_S = 0, COL_U = 256, COL_X = 416, COL_O = 448;
+constexpr uint32_t kUW = 80;  // columns per half of the slot-sum accumulator
 constexpr uint32_t kQBytes = 128 * 128;
 
 enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
@@ -101,7 +103,7 @@ template <typename T> struct Layout {
   static constexpr uint32_t OFF_P = OFF_V + kImg;
   static constexpr uint32_t OFF_Q = OFF_P + 4 * 16384;
   static constexpr uint32_t OFF_ONES = OFF_Q + Cfg<T>::kQBufs * kQBytes;
-  static constexpr uint32_t OFF_XCH = OFF_ONES + 512;  // [7][kRowThreads] packed ranks: per-thread top-7 lists
+  static constexpr uint32_t OFF_XCH = OFF_ONES + 2048;  // [7][kRowThreads] packed ranks: per-thread top-7 lists
   static constexpr uint32_t OFF_MISC = OFF_XCH + kTopK * kRowThreads * 8;
   static constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
@@ -414,8 +416,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const int ntiles = (t_end - t_beg + kTile - 1) / kTile;
   constexpr uint32_t ID_SEL = idesc_f16(C::fmt, 128, 256, 0, 0);
   constexpr uint32_t ID_ATT = idesc_f16(C::fmt, 128, 64, 0, 1);
-  constexpr uint32_t ID_UPD = idesc_f16(C::fmt, 128, 64, 1, 1);
-  constexpr uint32_t ID_W = idesc_f16(C::fmt, 128, 16, 1, 0);
+  // S += P^T.[Q | 1]: N = 80, the last 16 columns of B are ones, so they accumulate W
+  constexpr uint32_t ID_UPD = idesc_f16(C::fmt, 128, tc::kUW, 1, 1);
 
   // ---- set-up: barriers, zeroed P, ones, TMEM ----
   if (tid == 0) {
@@ -431,7 +433,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     float4* p4 = reinterpret_cast<float4*>(sm + L::OFF_P);
     for (int i = tid; i < 4 * 16384 / 16; i += tc::kThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint16_t* ones = reinterpret_cast<uint16_t*>(sm + L::OFF_ONES);
-    if (tid < 256) ones[tid] = C::one();  // 256 x 16-bit
+    for (int i = tid; i < 1024; i += tc::kThreads) ones[i] = C::one();  // 16 rows x 64 of 16-bit ones
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tc::kTmemCols);
@@ -480,12 +482,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   };
   // operand descriptors (start addresses moved per MMA by SDesc::at)
   const tc::SDesc d_qk = tc::sdesc(s_base + L::OFF_Q, 16, 1024, kSwizzle128B);      // Q, K-major (SELECT A)
-  const tc::SDesc d_qmn = tc::sdesc(s_base + L::OFF_Q, 16384, 1024, kSwizzle128B);  // Q, MN-major (update B)
   const tc::SDesc d_key = tc::sdesc(s_base, 16, 1024, kSwizzle128B);                // key terms (SELECT B)
   const tc::SDesc d_pk = tc::sdesc(a_p, 16, 1024, kSwizzle128B);                    // P, K-major (attend A)
   const tc::SDesc d_pmn = tc::sdesc(a_p, 16384, 1024, kSwizzle128B);                // P, MN-major (update A)
   const tc::SDesc d_v = tc::sdesc(a_v, 16384, 1024, kSwizzle128B);                  // V (attend B)
-  const uint64_t d_ones = smem_desc(a_ones, 256, 128, kSwizzleNone);
   auto issue_select = [&](int tile_idx) {  // issuer
     const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
     tc_fence_after();
@@ -496,16 +496,19 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         mma_f16(tmem + tc::COL_S, d_qk.at(q_off + k * 32), d_key.at(s * tc::kImg + k * 32), ID_SEL, (s | k) != 0);
     mma_commit(bar_s);
   };
-  auto issue_update = [&](int tile_idx, bool first) {  // issuer: S += P^T.Q, W += P^T.1
-    const uint32_t q_off = q_slot(tile_idx) * tc::kQBytes;
+  // issuer: [S | W] += P^T.[Q | 1]. B is MN-major with two 64-column atoms: the q tile's rows
+  // kk*16.. and, LBO bytes further on, 16 rows of ones (the descriptor's LBO is set per MMA so
+  // that the second atom always starts at the ones; only its first 16 columns are read).
+  auto issue_update = [&](int tile_idx, bool first) {
+    const uint32_t q_at = s_base + L::OFF_Q + q_slot(tile_idx) * tc::kQBytes;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint64_t a = d_pmn.at(2 * hh * 16384 + kk * 2048);
-        const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-        mma_f16(tmem + tc::COL_U + 64 * hh, a, d_qmn.at(q_off + kk * 2048), ID_UPD, acc);
-        mma_f16(tmem + tc::COL_W + 16 * hh, a, d_ones, ID_W, acc);
+        const uint32_t b_at = q_at + kk * 2048;
+        const uint64_t bq = smem_desc(b_at, a_ones - b_at, 1024, kSwizzle128B);
+        mma_f16(tmem + tc::COL_U + tc::kUW * hh, a, bq, ID_UPD, (first && kk == 0) ? 0u : 1u);
       }
     }
   };
@@ -899,8 +902,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       for (int hh = 0; hh < 2; ++hh) {
         const int m = 128 * hh + row;
         float s32[32], wv[16];
-        tmem_ld32(tmem + lane_base + tc::COL_U + 64 * hh + 32 * part, s32);
-        tmem_ld16(tmem + lane_base + tc::COL_W + 16 * hh, wv);
+        tmem_ld32(tmem + lane_base + tc::COL_U + tc::kUW * hh + 32 * part, s32);
+        tmem_ld16(tmem + lane_base + tc::COL_U + tc::kUW * hh + 64, wv);
         tmem_wait_ld();
         if (m < g.M) {
           float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * part);
