@@ -49,6 +49,33 @@ void launch_end(cudaStream_t st);
     ::murm::launch_end(stream);                                          \
   } while (0)
 
+// Programmatic dependent launch: the kernel may be scheduled while its predecessor on the
+// stream is still running (once every predecessor block has called pdl_trigger() or exited);
+// it runs its prologue (barriers, shared memory, TMEM), then pdl_wait() returns once the
+// predecessor has completed and its writes are visible. Used by the tensor-core round loops,
+// whose kernels all follow that pattern.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+#define MURM_LAUNCH_PDL(name, kernel, grid, block, smem, stream, ...)                \
+  do {                                                                               \
+    ::murm::launch_begin(name, stream);                                              \
+    ::murm::launch_pdl(kernel, dim3(grid), dim3(block), smem, stream, __VA_ARGS__);  \
+    ::murm::launch_end(stream);                                                      \
+  } while (0)
+
 // Shared pieces of the round loop (murm_simt.cu).
 template <typename T>
 void launch_load_slots(const Geom& g, const FwdPtrs& p, const Saved& sv, cudaStream_t st);

@@ -49,6 +49,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------------------
+// programmatic dependent launch
+// ---------------------------------------------------------------------------
+// Blocks until the preceding grid on the stream has completed and its memory is visible
+// (returns at once when the kernel was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next programmatic dependent grid be scheduled once every block of this grid has
+// called it (or exited); its blocks still wait in pdl_wait() for this grid to complete.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // bulk copies (TMA engine)
 // ---------------------------------------------------------------------------
 // 1-D bulk copy global -> shared; size multiple of 16, both addresses 16-aligned.

@@ -272,6 +272,8 @@ __device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k
 template <typename T>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv,
                                                                         Strides3 svs, Saved sv, uint8_t* images) {
+  pdl_wait();  // the previous step's kernels may still read the state and images
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, l = threadIdx.x & 15;
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
   const int m = blockIdx.y * kSlotRows + (threadIdx.x >> 4);
@@ -307,6 +309,8 @@ __device__ __forceinline__ float4 diffuse4(float4 x, float4 l, float4 r, float g
 // one halo row on each side; 16 threads per row, every chunk load of a row in flight at once.
 template <typename T>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
+  pdl_wait();  // the round's chunk partials
+  pdl_trigger();
   __shared__ float4 kn[kSlotHalo][tc::kRowLanes];
   __shared__ float4 vn[kSlotHalo][tc::kRowLanes];
   const int bh = blockIdx.x, rr = threadIdx.x >> 4, l = threadIdx.x & 15;
@@ -443,6 +447,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // everything above touched only this CTA's shared memory and TMEM: it overlaps the previous
+  // kernel, whose outputs (the round's state and operand images) are read from here on
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * quadrant) << 16;
   const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
@@ -999,13 +1007,13 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
     cudaFuncSetAttribute(k_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Layout<T>::kSmem);
     attr = true;
   }
-  MURM_LAUNCH("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
+  MURM_LAUNCH_PDL("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
               static_cast<const T*>(p.sv), p.svs, sv, images);
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
+    MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
     if (r + 1 < g.R)
-      MURM_LAUNCH("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs);
+      MURM_LAUNCH_PDL("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs);
   }
   return cudaGetLastError();
 }

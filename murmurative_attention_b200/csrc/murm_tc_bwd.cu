@@ -233,6 +233,8 @@ template <typename T>
 __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
     k_bwd_slots(Geom g, int r, int has_dir, int has_part, Saved sv, BwdScratch bs, uint8_t* tables, float* dWpad,
                 T* gsk, Strides3 gsks, T* gsv, Strides3 gsvs) {
+  pdl_wait();  // the token kernel's chunk partials
+  pdl_trigger();
   const float* dir_k = bs.dK[r & 1];
   const float* dir_v = bs.dV[r & 1];
   float* nxt_k = bs.dK[(r + 1) & 1];  // direct parts of round r-1
@@ -339,6 +341,8 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
 // Tables of the last round (no slot gradient flows into it): K, V; dS = 0, dW = 0.
 template <typename T>
 __global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8_t* tables, float* dWpad) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x;
   const size_t st = ((size_t)(g.R - 1) * g.BH + bh) * g.M * g.D;
   uint8_t* tab = tables + (size_t)bh * tcb::kTables;
@@ -423,6 +427,10 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // everything above touched only this CTA's shared memory and TMEM: it overlaps the previous
+  // kernel, whose outputs (tables, dW, dq of later rounds) are read from here on
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   uint32_t ph_mma = 0;
   // the issuer's bookkeeping of asynchronous copies: the last tile issued / waited for
@@ -810,12 +818,12 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
   uint8_t* tables = bs.tables;
   float* dWpad = reinterpret_cast<float*>(tables + (size_t)g.BH * tcb::kTables);
   const int slot_blocks = (g.M + kSlotRows - 1) / kSlotRows;
-  MURM_LAUNCH("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad);
+  MURM_LAUNCH_PDL("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad);
   for (int r = g.R - 1; r >= 0; --r) {
-    MURM_LAUNCH("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
+    MURM_LAUNCH_PDL("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
                 qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,
                 static_cast<T*>(p.gq), p.gqs, sv, bs, tables, dWpad);
-    MURM_LAUNCH("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), tcb::kRowLanes * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
+    MURM_LAUNCH_PDL("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), tcb::kRowLanes * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
                 sv, bs, tables, dWpad, static_cast<T*>(p.gsk), p.gsks, static_cast<T*>(p.gsv), p.gsvs);
   }
   return cudaGetLastError();
