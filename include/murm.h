@@ -143,6 +143,39 @@ MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* st
 #define MURM_NOSCRATCH_BYTES (64u << 20)
 MURM_API murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* args, void* stream);
 
+/* Forward and backward over HOST buffers: the drop-in for a caller whose tensors
+ * live in host memory — the reference's CPU path (src/murmurative/reference.py:
+ * 138-191 called on CPU tensors, then its autograd backward with grad_out).
+ * All tensors are contiguous: q, grad_out, out, grad_q [B,H,N,d]; slots_k,
+ * slots_v, grad_slots_k, grad_slots_v [B,H,M,d]; indices int64 and weights
+ * fp32 [B,H,N,7] (either may be NULL). The (batch, head) pairs are split into
+ * `groups` (0: automatic — groups of at least 8 pairs, at least two groups)
+ * that go through a three-stage pipeline — copy in on one
+ * stream, murm_slot_murmurate_fwd + _bwd on `stream`, copy out on another —
+ * so the host<->device copies overlap the kernels and each other. Host
+ * buffers should be page-locked (cudaHostAlloc / pinned) for the copies to
+ * overlap. `workspace` is one device block of murm_host_step_sizes() bytes,
+ * 256-byte aligned. The call is asynchronous: the results are in the host
+ * buffers once `stream` has completed. Calls are serialised internally. */
+typedef struct murm_host_step_args {
+  murm_shape shape;
+  const void* q;
+  const void* slots_k;
+  const void* slots_v;
+  const void* grad_out;
+  void* out;
+  int64_t* indices;
+  float* weights;
+  void* grad_q;
+  void* grad_slots_k;
+  void* grad_slots_v;
+  int32_t groups;
+  void* workspace;   size_t workspace_bytes;
+} murm_host_step_args;
+
+MURM_API murm_status murm_host_step_sizes(const murm_shape* shape, int32_t groups, size_t* workspace_bytes);
+MURM_API murm_status murm_slot_murmurate_host_step(const murm_host_step_args* args, void* stream);
+
 /* ------------------------------------------------------------------------
  * Per-phase operations: the reference's op surface one round at a time
  * (torch-ext/torch_binding.cpp:6-33 slot_select_attend, slot_update,

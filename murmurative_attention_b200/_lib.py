@@ -190,6 +190,17 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class HostStepArgs(ctypes.Structure):
+    _fields_ = [
+        ("shape", Shape),
+        ("q", ctypes.c_void_p), ("slots_k", ctypes.c_void_p), ("slots_v", ctypes.c_void_p),
+        ("grad_out", ctypes.c_void_p), ("out", ctypes.c_void_p), ("indices", ctypes.c_void_p),
+        ("weights", ctypes.c_void_p), ("grad_q", ctypes.c_void_p), ("grad_slots_k", ctypes.c_void_p),
+        ("grad_slots_v", ctypes.c_void_p), ("groups", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 # Every symbol include/murm.h declares; tests check the library exports them all.
 EXPORTS = (
     "murm_slot_murmurate_sizes",
@@ -213,6 +224,8 @@ EXPORTS = (
     "murm_decode_step",
     "murm_slot_sums_fwd",
     "murm_slot_sums_bwd",
+    "murm_host_step_sizes",
+    "murm_slot_murmurate_host_step",
 )
 
 STATUS_NAMES = {
@@ -270,6 +283,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
             fn.restype = ctypes.c_int
+        lib.murm_host_step_sizes.argtypes = [ctypes.POINTER(Shape), ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]
+        lib.murm_host_step_sizes.restype = ctypes.c_int
+        lib.murm_slot_murmurate_host_step.argtypes = [ctypes.POINTER(HostStepArgs), ctypes.c_void_p]
+        lib.murm_slot_murmurate_host_step.restype = ctypes.c_int
         if lib.murm_abi_version() != 1:
             raise RuntimeError("murmurative_attention_b200: libmurm_b200.so ABI version mismatch; rebuild it")
         _lib = lib

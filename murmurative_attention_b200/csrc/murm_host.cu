@@ -1,0 +1,211 @@
+// murm_host.cu — forward + backward over host buffers, copies overlapped with compute.
+//
+// murm_slot_murmurate_host_step is the drop-in for a caller whose tensors live in host
+// memory (the reference's CPU path: reference.py:138-191 and its autograd backward).
+// The (batch, head) pairs are independent, so the call splits them into groups and runs a
+// three-stage pipeline: inputs are copied in on one stream, each group's forward and backward
+// run on the caller's stream, results are copied out on a third, so the host<->device copies
+// (both directions at once) overlap the kernels. The forward of a group waits only for its q
+// and slots (grad_out follows during it), and its outputs start copying out while its
+// backward runs.
+// No kernels of its own: each group goes through murm_slot_murmurate_fwd / _bwd.
+#include <mutex>
+#include <vector>
+
+#include "murm_kernels.cuh"
+
+namespace murm {
+namespace {
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t elem_bytes(int dtype) { return dtype == MURM_F32 ? 4 : 2; }
+
+// One device's copy streams and events, created on first use and kept for the process.
+struct HostPipe {
+  cudaStream_t in = nullptr, out = nullptr;
+  std::vector<cudaEvent_t> ev;  // [0] start, [1] done, then 4 per group (see kEvents)
+};
+std::mutex g_pipe_mu;
+std::mutex g_call_mu;
+std::vector<HostPipe> g_pipes;
+
+cudaError_t pipe_for(int device, int groups, HostPipe** out) {
+  std::lock_guard<std::mutex> lk(g_pipe_mu);
+  if ((int)g_pipes.size() <= device) g_pipes.resize(device + 1);
+  HostPipe& p = g_pipes[device];
+  cudaError_t e = cudaSuccess;
+  if (!p.in) e = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking);
+  if (e == cudaSuccess && !p.out) e = cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking);
+  while (e == cudaSuccess && (int)p.ev.size() < 2 + 4 * groups) {
+    cudaEvent_t ev;
+    e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) p.ev.push_back(ev);
+  }
+  *out = &p;
+  return e;
+}
+
+struct HostLayout {
+  int groups, per;                  // number of groups, (b,h) pairs per group (last may be smaller)
+  size_t q, go, sk, sv, out, idx, w, gq, gsk, gsv;  // offsets of the full-size device copies
+  size_t saved, fws, bws;           // one group's saved block and workspaces
+  size_t saved_bytes, fws_bytes, bws_bytes, total;
+};
+
+murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
+  if (!s) return report_error(MURM_ERR_INVALID_ARGUMENT, "shape is NULL");
+  const int64_t bh = (int64_t)s->batch * s->heads;
+  if (bh < 1) return report_error(MURM_ERR_INVALID_ARGUMENT, "batch * heads must be >= 1");
+  // automatic: groups of at least 8 (b,h) pairs (smaller ones leave the round kernels' grids
+  // short of work), and at least two groups so that copies overlap compute
+  int64_t G = groups > 0 ? groups : (bh / 8 > 2 ? bh / 8 : (bh < 2 ? bh : 2));
+  if (G > bh) G = bh;
+  if (G > 64) G = 64;
+  L->per = (int)((bh + G - 1) / G);
+  L->groups = (int)((bh + L->per - 1) / L->per);
+  murm_shape gs = *s;
+  gs.batch = 1;
+  gs.heads = L->per;
+  if (murm_status st = murm_slot_murmurate_sizes(&gs, &L->saved_bytes, &L->fws_bytes, &L->bws_bytes)) return st;
+  const size_t es = elem_bytes(s->dtype);
+  const size_t tok = (size_t)bh * s->tokens, slot = (size_t)bh * s->slots;
+  size_t o = 0;
+  auto take = [&](size_t b) { const size_t at = o; o += align256(b); return at; };
+  L->q = take(tok * s->head_dim * es);
+  L->go = take(tok * s->head_dim * es);
+  L->sk = take(slot * s->head_dim * es);
+  L->sv = take(slot * s->head_dim * es);
+  L->out = take(tok * s->head_dim * es);
+  L->idx = take(tok * MURM_TOP_K * 8);
+  L->w = take(tok * MURM_TOP_K * 4);
+  L->gq = take(tok * s->head_dim * es);
+  L->gsk = take(slot * s->head_dim * es);
+  L->gsv = take(slot * s->head_dim * es);
+  L->saved = take(L->saved_bytes);
+  L->fws = take(L->fws_bytes);
+  L->bws = take(L->bws_bytes);
+  L->total = o;
+  return MURM_OK;
+}
+
+}  // namespace
+}  // namespace murm
+
+using namespace murm;
+
+extern "C" {
+
+murm_status murm_host_step_sizes(const murm_shape* shape, int32_t groups, size_t* workspace_bytes) {
+  HostLayout L;
+  if (murm_status s = plan(shape, groups, &L)) return s;
+  if (workspace_bytes) *workspace_bytes = L.total;
+  return MURM_OK;
+}
+
+murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* stream) {
+  if (!a) return report_error(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
+  HostLayout L;
+  if (murm_status s = plan(&a->shape, a->groups, &L)) return s;
+  if (!a->q || !a->slots_k || !a->slots_v || !a->grad_out || !a->out || !a->grad_q || !a->grad_slots_k ||
+      !a->grad_slots_v)
+    return report_error(MURM_ERR_INVALID_ARGUMENT, "q, slots, grad_out, out and the three gradients are required");
+  if (!a->workspace || (reinterpret_cast<uintptr_t>(a->workspace) & 255) || a->workspace_bytes < L.total)
+    return report_error(MURM_ERR_WORKSPACE, "host-step workspace too small or not 256-byte aligned");
+  const murm_shape& s = a->shape;
+  const size_t es = elem_bytes(s.dtype);
+  const int64_t N = s.tokens, M = s.slots, D = s.head_dim;
+  const size_t tokb = (size_t)N * D * es, slotb = (size_t)M * D * es;  // bytes per (b,h) pair
+  const size_t recn = (size_t)N * MURM_TOP_K;
+  char* ws = static_cast<char*>(a->workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return report_error(MURM_ERR_CUDA, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> call_lk(g_call_mu);  // one device's streams and events: one call at a time
+  HostPipe* pp = nullptr;
+  if (cudaError_t e = pipe_for(dev, L.groups, &pp))
+    return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
+  HostPipe& P = *pp;
+  const int64_t bh = (int64_t)s.batch * s.heads;
+  auto H2D = [&](size_t dev_off, const void* host, size_t off, size_t bytes) {
+    return cudaMemcpyAsync(ws + dev_off + off, static_cast<const char*>(host) + off, bytes, cudaMemcpyHostToDevice,
+                           P.in);
+  };
+  auto D2H = [&](void* host, size_t dev_off, size_t off, size_t bytes) {
+    return cudaMemcpyAsync(static_cast<char*>(host) + off, ws + dev_off + off, bytes, cudaMemcpyDeviceToHost, P.out);
+  };
+  cudaError_t e = cudaEventRecord(P.ev[0], st);  // the copies start after the caller's earlier work
+  if (!e) e = cudaStreamWaitEvent(P.in, P.ev[0], 0);
+  if (!e) e = cudaStreamWaitEvent(P.out, P.ev[0], 0);
+  for (int g = 0; g < L.groups && !e; ++g) {
+    const int64_t p0 = (int64_t)g * L.per, np = (p0 + L.per <= bh) ? L.per : bh - p0;
+    // per group: q + slots copied in, grad_out copied in, forward done, backward done
+    cudaEvent_t ev_qs = P.ev[2 + 4 * g], ev_go = P.ev[3 + 4 * g], ev_f = P.ev[4 + 4 * g], ev_b = P.ev[5 + 4 * g];
+    // ---- stage 1: inputs of group g ----
+    if (!e) e = H2D(L.q, a->q, p0 * tokb, np * tokb);
+    if (!e) e = H2D(L.sk, a->slots_k, p0 * slotb, np * slotb);
+    if (!e) e = H2D(L.sv, a->slots_v, p0 * slotb, np * slotb);
+    if (!e) e = cudaEventRecord(ev_qs, P.in);
+    if (!e) e = H2D(L.go, a->grad_out, p0 * tokb, np * tokb);
+    if (!e) e = cudaEventRecord(ev_go, P.in);
+    if (e) break;
+    // ---- stage 2: forward, then backward, of group g on the caller's stream ----
+    if ((e = cudaStreamWaitEvent(st, ev_qs, 0))) break;
+    murm_shape gs = s;
+    gs.batch = 1;
+    gs.heads = (int32_t)np;
+    const int64_t ts[3] = {np * N * D, N * D, D}, ss[3] = {np * M * D, M * D, D};
+    murm_fwd_args f{};
+    f.shape = gs;
+    f.q = ws + L.q + p0 * tokb;
+    f.slots_k = ws + L.sk + p0 * slotb;
+    f.slots_v = ws + L.sv + p0 * slotb;
+    f.out = ws + L.out + p0 * tokb;
+    for (int i = 0; i < 3; ++i) {
+      f.q_stride[i] = f.out_stride[i] = ts[i];
+      f.sk_stride[i] = f.sv_stride[i] = ss[i];
+    }
+    f.indices = reinterpret_cast<int64_t*>(ws + L.idx) + p0 * recn;
+    f.weights = reinterpret_cast<float*>(ws + L.w) + p0 * recn;
+    f.saved = ws + L.saved;
+    f.saved_bytes = L.saved_bytes;
+    f.workspace = ws + L.fws;
+    f.workspace_bytes = L.fws_bytes;
+    if (murm_status ms = murm_slot_murmurate_fwd(&f, st)) return ms;
+    if ((e = cudaEventRecord(ev_f, st))) break;
+    if ((e = cudaStreamWaitEvent(st, ev_go, 0))) break;
+    murm_bwd_args bw{};
+    bw.shape = gs;
+    bw.q = f.q;
+    bw.grad_out = ws + L.go + p0 * tokb;
+    bw.saved = f.saved;
+    bw.saved_bytes = f.saved_bytes;
+    bw.grad_q = ws + L.gq + p0 * tokb;
+    bw.grad_slots_k = ws + L.gsk + p0 * slotb;
+    bw.grad_slots_v = ws + L.gsv + p0 * slotb;
+    for (int i = 0; i < 3; ++i) {
+      bw.q_stride[i] = bw.go_stride[i] = bw.gq_stride[i] = ts[i];
+      bw.gsk_stride[i] = bw.gsv_stride[i] = ss[i];
+    }
+    bw.workspace = ws + L.bws;
+    bw.workspace_bytes = L.bws_bytes;
+    if (murm_status ms = murm_slot_murmurate_bwd(&bw, st)) return ms;
+    if ((e = cudaEventRecord(ev_b, st))) break;
+    // ---- stage 3: the forward's results during the backward, then the gradients ----
+    if ((e = cudaStreamWaitEvent(P.out, ev_f, 0))) break;
+    e = D2H(a->out, L.out, p0 * tokb, np * tokb);
+    if (!e && a->indices) e = D2H(a->indices, L.idx, p0 * recn * 8, np * recn * 8);
+    if (!e && a->weights) e = D2H(a->weights, L.w, p0 * recn * 4, np * recn * 4);
+    if (!e) e = cudaStreamWaitEvent(P.out, ev_b, 0);
+    if (!e) e = D2H(a->grad_q, L.gq, p0 * tokb, np * tokb);
+    if (!e) e = D2H(a->grad_slots_k, L.gsk, p0 * slotb, np * slotb);
+    if (!e) e = D2H(a->grad_slots_v, L.gsv, p0 * slotb, np * slotb);
+  }
+  // the caller's stream completes after the last copy out
+  if (!e) e = cudaEventRecord(P.ev[1], P.out);
+  if (!e) e = cudaStreamWaitEvent(st, P.ev[1], 0);
+  if (e) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
+  return MURM_OK;
+}
+
+}  // extern "C"

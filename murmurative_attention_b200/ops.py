@@ -182,3 +182,62 @@ def slot_murmurate(q: torch.Tensor, slots_k: torch.Tensor, slots_v: torch.Tensor
         raise ValueError(f"top_k must be {_lib.TOP_K} (the reference hard-codes k=7), got {top_k}")
     return _SlotMurmurate.apply(q, slots_k, slots_v, int(rounds), int(top_k), bool(causal), float(alpha),
                                 float(gamma), scale)
+
+
+def slot_murmurate_host_step(q: torch.Tensor, slots_k: torch.Tensor, slots_v: torch.Tensor,
+                             grad_out: torch.Tensor, rounds: int = 3, top_k: int = 7, causal: bool = False, *,
+                             alpha: float = 0.9, gamma: float = 0.15, scale: Optional[float] = None,
+                             groups: int = 0, outputs: Optional[Tuple[torch.Tensor, ...]] = None,
+                             device: Optional[torch.device] = None):
+    """Forward and backward of :func:`slot_murmurate` for tensors in host memory.
+
+    The drop-in for the reference's CPU path: ``out, idx, w = slot_murmurate(q, slots_k, slots_v)``
+    on CPU tensors followed by ``out.backward(grad_out)`` (reference.py:138-191 and its autograd
+    backward). q, grad_out [B, H, N, d] and slots_k, slots_v [B, H, M, d] are contiguous CPU
+    tensors of one dtype (pinned memory lets the copies overlap the kernels). The (batch, head)
+    pairs run in ``groups`` (0: automatic) through a copy-in / compute / copy-out pipeline on the GPU
+    (``murm_slot_murmurate_host_step``). Returns CPU tensors
+    ``(out, indices, weights, grad_q, grad_slots_k, grad_slots_v)``, written into ``outputs``
+    when given (six tensors of those shapes and dtypes); blocks until they are filled.
+    """
+    lib = _lib.load_library()
+    if top_k != _lib.TOP_K:
+        raise ValueError(f"top_k must be {_lib.TOP_K} (the reference hard-codes k=7), got {top_k}")
+    for name, t in (("q", q), ("slots_k", slots_k), ("slots_v", slots_v), ("grad_out", grad_out)):
+        _dtype_code(t, name)
+        if t.dim() != 4 or t.is_cuda or not t.is_contiguous():
+            raise RuntimeError(f"{name} must be a contiguous 4-D CPU tensor, got shape {tuple(t.shape)} on "
+                               f"{t.device}")
+        if t.dtype != q.dtype:
+            raise TypeError(f"every tensor must have q's dtype {q.dtype}; {name} is {t.dtype}")
+    B, H, N, D = q.shape
+    if grad_out.shape != q.shape:
+        raise RuntimeError(f"grad_out must have q's shape {tuple(q.shape)}, got {tuple(grad_out.shape)}")
+    if slots_k.shape != slots_v.shape or tuple(slots_k.shape[:2]) != (B, H) or slots_k.shape[3] != D:
+        raise RuntimeError(f"slots_k/slots_v must be [B={B}, H={H}, M, d={D}], got {tuple(slots_k.shape)} and "
+                           f"{tuple(slots_v.shape)}")
+    if not torch.cuda.is_available():
+        raise RuntimeError("murmurative CUDA kernels require a CUDA-capable device, but none is available.")
+    M = slots_k.shape[2]
+    shape = _make_shape(q, M, rounds, top_k, causal, alpha, gamma, scale)
+    if outputs is None:
+        pin = q.is_pinned()
+        outputs = (torch.empty(q.shape, dtype=q.dtype, pin_memory=pin),
+                   torch.empty(B, H, N, _lib.TOP_K, dtype=torch.int64, pin_memory=pin),
+                   torch.empty(B, H, N, _lib.TOP_K, dtype=torch.float32, pin_memory=pin),
+                   torch.empty(q.shape, dtype=q.dtype, pin_memory=pin),
+                   torch.empty(slots_k.shape, dtype=q.dtype, pin_memory=pin),
+                   torch.empty(slots_k.shape, dtype=q.dtype, pin_memory=pin))
+    out, idx, w, gq, gsk, gsv = outputs
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    nbytes = ctypes.c_size_t()
+    _lib.check(lib.murm_host_step_sizes(ctypes.byref(shape), int(groups), ctypes.byref(nbytes)))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=dev)
+    args = _lib.HostStepArgs(shape, q.data_ptr(), slots_k.data_ptr(), slots_v.data_ptr(), grad_out.data_ptr(),
+                             out.data_ptr(), idx.data_ptr(), w.data_ptr(), gq.data_ptr(), gsk.data_ptr(),
+                             gsv.data_ptr(), int(groups), ws.data_ptr(), nbytes.value)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(lib.murm_slot_murmurate_host_step(ctypes.byref(args), ctypes.c_void_p(stream.cuda_stream)))
+        stream.synchronize()
+    return outputs

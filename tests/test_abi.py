@@ -145,3 +145,34 @@ def test_phase_null_args_rejected_without_gpu():
                  "murm_slot_diffusion_fwd", "murm_slot_diffusion_bwd", "murm_decode_step",
                  "murm_slot_sums_fwd", "murm_slot_sums_bwd"):
         assert getattr(lib, name)(None, None) == 1, name
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_host_step_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "host.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "murm.h"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu\\n\", sizeof(murm_host_step_args),"
+        " offsetof(murm_host_step_args, grad_out), offsetof(murm_host_step_args, groups),"
+        " offsetof(murm_host_step_args, workspace_bytes)); return 0;}\n")
+    exe = tmp_path / "host"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    H = _lib.HostStepArgs
+    assert got == [ctypes.sizeof(H), H.grad_out.offset, H.groups.offset, H.workspace_bytes.offset]
+
+
+def test_host_step_sizes_and_validation():
+    lib = _lib.load_library()
+    shape = _lib.Shape(1, 16, 8192, 256, 64, 3, 7, 0, 0.9, 0.15, 0.0, _lib.MURM_F16)
+    n1, n2 = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.murm_host_step_sizes(ctypes.byref(shape), 1, ctypes.byref(n1)) == 0
+    assert lib.murm_host_step_sizes(ctypes.byref(shape), 4, ctypes.byref(n2)) == 0
+    # full-size device copies of every input and output, plus one group's scratch
+    io = 16 * 8192 * 64 * 2 * 4 + 16 * 256 * 64 * 2 * 4 + 16 * 8192 * 7 * (8 + 4)
+    assert n1.value > io and io < n2.value < n1.value
+    bad = _lib.Shape(1, 16, 8192, 256, 64, 3, 5, 0, 0.9, 0.15, 0.0, _lib.MURM_F16)
+    assert lib.murm_host_step_sizes(ctypes.byref(bad), 0, ctypes.byref(n1)) == 2
+    assert lib.murm_slot_murmurate_host_step(None, None) == 1
+    args = _lib.HostStepArgs(shape)  # no buffers
+    assert lib.murm_slot_murmurate_host_step(ctypes.byref(args), None) == 1
