@@ -149,7 +149,7 @@ MURM_API murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* args
  * All tensors are contiguous: q, grad_out, out, grad_q [B,H,N,d]; slots_k,
  * slots_v, grad_slots_k, grad_slots_v [B,H,M,d]; indices int64 and weights
  * fp32 [B,H,N,7] (either may be NULL). The (batch, head) pairs are split into
- * `groups` (0: automatic — groups of at least 8 pairs, at least two groups)
+ * `groups` (0: automatic — groups of at least 4 pairs, 2 to 8 groups)
  * that go through a three-stage pipeline — copy in on one
  * stream, murm_slot_murmurate_fwd + _bwd on `stream`, copy out on another —
  * so the host<->device copies overlap the kernels and each other. Host

@@ -3,11 +3,12 @@
 // murm_slot_murmurate_host_step is the drop-in for a caller whose tensors live in host
 // memory (the reference's CPU path: reference.py:138-191 and its autograd backward).
 // The (batch, head) pairs are independent, so the call splits them into groups and runs a
-// three-stage pipeline: inputs are copied in on one stream, each group's forward and backward
-// run on the caller's stream, results are copied out on a third, so the host<->device copies
-// (both directions at once) overlap the kernels. The forward of a group waits only for its q
-// and slots (grad_out follows during it), and its outputs start copying out while its
-// backward runs.
+// three-stage pipeline: inputs are copied in on one stream, the groups' forwards and then
+// their backwards run on the caller's stream, results are copied out on a third, so the
+// host<->device copies (both directions at once) overlap the kernels. q and the slots of
+// every group go in first and grad_out after them; the forwards' outputs (out, indices,
+// weights: most of the bytes out) start copying out as soon as the first forward is done,
+// and the gradients follow the backwards.
 // No kernels of its own: each group goes through murm_slot_murmurate_fwd / _bwd.
 #include <mutex>
 #include <vector>
@@ -49,7 +50,7 @@ cudaError_t pipe_for(int device, int groups, HostPipe** out) {
 struct HostLayout {
   int groups, per;                  // number of groups, (b,h) pairs per group (last may be smaller)
   size_t q, go, sk, sv, out, idx, w, gq, gsk, gsv;  // offsets of the full-size device copies
-  size_t saved, fws, bws;           // one group's saved block and workspaces
+  size_t saved, fws, bws;           // every group's saved block; one group's workspaces
   size_t saved_bytes, fws_bytes, bws_bytes, total;
 };
 
@@ -57,9 +58,9 @@ murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
   if (!s) return report_error(MURM_ERR_INVALID_ARGUMENT, "shape is NULL");
   const int64_t bh = (int64_t)s->batch * s->heads;
   if (bh < 1) return report_error(MURM_ERR_INVALID_ARGUMENT, "batch * heads must be >= 1");
-  // automatic: groups of at least 8 (b,h) pairs (smaller ones leave the round kernels' grids
-  // short of work), and at least two groups so that copies overlap compute
-  int64_t G = groups > 0 ? groups : (bh / 8 > 2 ? bh / 8 : (bh < 2 ? bh : 2));
+  // automatic: groups of at least 4 (b,h) pairs (smaller ones leave the round kernels' grids
+  // short of work), at least two groups so that copies overlap compute, at most 8
+  int64_t G = groups > 0 ? groups : (bh / 4 > 8 ? 8 : (bh / 4 > 2 ? bh / 4 : (bh < 2 ? bh : 2)));
   if (G > bh) G = bh;
   if (G > 64) G = 64;
   L->per = (int)((bh + G - 1) / G);
@@ -82,7 +83,7 @@ murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
   L->gq = take(tok * s->head_dim * es);
   L->gsk = take(slot * s->head_dim * es);
   L->gsv = take(slot * s->head_dim * es);
-  L->saved = take(L->saved_bytes);
+  L->saved = take(align256(L->saved_bytes) * L->groups);
   L->fws = take(L->fws_bytes);
   L->bws = take(L->bws_bytes);
   L->total = o;
@@ -137,26 +138,42 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
   cudaError_t e = cudaEventRecord(P.ev[0], st);  // the copies start after the caller's earlier work
   if (!e) e = cudaStreamWaitEvent(P.in, P.ev[0], 0);
   if (!e) e = cudaStreamWaitEvent(P.out, P.ev[0], 0);
+  auto pairs = [&](int g, int64_t* p0, int64_t* np) {
+    *p0 = (int64_t)g * L.per;
+    *np = (*p0 + L.per <= bh) ? L.per : bh - *p0;
+  };
+  // per group: q + slots copied in, grad_out copied in, forward done, backward done
+  auto ev = [&](int g, int k) { return P.ev[2 + 4 * g + k]; };
+  // ---- copies in: q and slots of every group, then grad_out ----
   for (int g = 0; g < L.groups && !e; ++g) {
-    const int64_t p0 = (int64_t)g * L.per, np = (p0 + L.per <= bh) ? L.per : bh - p0;
-    // per group: q + slots copied in, grad_out copied in, forward done, backward done
-    cudaEvent_t ev_qs = P.ev[2 + 4 * g], ev_go = P.ev[3 + 4 * g], ev_f = P.ev[4 + 4 * g], ev_b = P.ev[5 + 4 * g];
-    // ---- stage 1: inputs of group g ----
-    if (!e) e = H2D(L.q, a->q, p0 * tokb, np * tokb);
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    e = H2D(L.q, a->q, p0 * tokb, np * tokb);
     if (!e) e = H2D(L.sk, a->slots_k, p0 * slotb, np * slotb);
     if (!e) e = H2D(L.sv, a->slots_v, p0 * slotb, np * slotb);
-    if (!e) e = cudaEventRecord(ev_qs, P.in);
-    if (!e) e = H2D(L.go, a->grad_out, p0 * tokb, np * tokb);
-    if (!e) e = cudaEventRecord(ev_go, P.in);
-    if (e) break;
-    // ---- stage 2: forward, then backward, of group g on the caller's stream ----
-    if ((e = cudaStreamWaitEvent(st, ev_qs, 0))) break;
+    if (!e) e = cudaEventRecord(ev(g, 0), P.in);
+  }
+  for (int g = 0; g < L.groups && !e; ++g) {
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    e = H2D(L.go, a->grad_out, p0 * tokb, np * tokb);
+    if (!e) e = cudaEventRecord(ev(g, 1), P.in);
+  }
+  if (e) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
+  // ---- forwards, then backwards, on the caller's stream ----
+  const int64_t ts[3] = {(int64_t)L.per * N * D, N * D, D}, ss[3] = {(int64_t)L.per * M * D, M * D, D};
+  auto group_shape = [&](int64_t np) {
     murm_shape gs = s;
     gs.batch = 1;
     gs.heads = (int32_t)np;
-    const int64_t ts[3] = {np * N * D, N * D, D}, ss[3] = {np * M * D, M * D, D};
+    return gs;
+  };
+  for (int g = 0; g < L.groups && !e; ++g) {
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    if ((e = cudaStreamWaitEvent(st, ev(g, 0), 0))) break;
     murm_fwd_args f{};
-    f.shape = gs;
+    f.shape = group_shape(np);
     f.q = ws + L.q + p0 * tokb;
     f.slots_k = ws + L.sk + p0 * slotb;
     f.slots_v = ws + L.sv + p0 * slotb;
@@ -167,19 +184,23 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     }
     f.indices = reinterpret_cast<int64_t*>(ws + L.idx) + p0 * recn;
     f.weights = reinterpret_cast<float*>(ws + L.w) + p0 * recn;
-    f.saved = ws + L.saved;
+    f.saved = ws + L.saved + align256(L.saved_bytes) * g;
     f.saved_bytes = L.saved_bytes;
     f.workspace = ws + L.fws;
     f.workspace_bytes = L.fws_bytes;
     if (murm_status ms = murm_slot_murmurate_fwd(&f, st)) return ms;
-    if ((e = cudaEventRecord(ev_f, st))) break;
-    if ((e = cudaStreamWaitEvent(st, ev_go, 0))) break;
+    e = cudaEventRecord(ev(g, 2), st);
+  }
+  for (int g = 0; g < L.groups && !e; ++g) {
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    if ((e = cudaStreamWaitEvent(st, ev(g, 1), 0))) break;
     murm_bwd_args bw{};
-    bw.shape = gs;
-    bw.q = f.q;
+    bw.shape = group_shape(np);
+    bw.q = ws + L.q + p0 * tokb;
     bw.grad_out = ws + L.go + p0 * tokb;
-    bw.saved = f.saved;
-    bw.saved_bytes = f.saved_bytes;
+    bw.saved = ws + L.saved + align256(L.saved_bytes) * g;
+    bw.saved_bytes = L.saved_bytes;
     bw.grad_q = ws + L.gq + p0 * tokb;
     bw.grad_slots_k = ws + L.gsk + p0 * slotb;
     bw.grad_slots_v = ws + L.gsv + p0 * slotb;
@@ -190,13 +211,21 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     bw.workspace = ws + L.bws;
     bw.workspace_bytes = L.bws_bytes;
     if (murm_status ms = murm_slot_murmurate_bwd(&bw, st)) return ms;
-    if ((e = cudaEventRecord(ev_b, st))) break;
-    // ---- stage 3: the forward's results during the backward, then the gradients ----
-    if ((e = cudaStreamWaitEvent(P.out, ev_f, 0))) break;
-    e = D2H(a->out, L.out, p0 * tokb, np * tokb);
+    e = cudaEventRecord(ev(g, 3), st);
+  }
+  // ---- copies out: each forward's results, then each backward's gradients ----
+  for (int g = 0; g < L.groups && !e; ++g) {
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    e = cudaStreamWaitEvent(P.out, ev(g, 2), 0);
+    if (!e) e = D2H(a->out, L.out, p0 * tokb, np * tokb);
     if (!e && a->indices) e = D2H(a->indices, L.idx, p0 * recn * 8, np * recn * 8);
     if (!e && a->weights) e = D2H(a->weights, L.w, p0 * recn * 4, np * recn * 4);
-    if (!e) e = cudaStreamWaitEvent(P.out, ev_b, 0);
+  }
+  for (int g = 0; g < L.groups && !e; ++g) {
+    int64_t p0, np;
+    pairs(g, &p0, &np);
+    e = cudaStreamWaitEvent(P.out, ev(g, 3), 0);
     if (!e) e = D2H(a->grad_q, L.gq, p0 * tokb, np * tokb);
     if (!e) e = D2H(a->grad_slots_k, L.gsk, p0 * slotb, np * slotb);
     if (!e) e = D2H(a->grad_slots_v, L.gsv, p0 * slotb, np * slotb);
