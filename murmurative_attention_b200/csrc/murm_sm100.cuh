@@ -32,6 +32,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Bounded wait for the phase with the given parity: about one second on %globaltimer, read only
+// once the first poll has failed (the read costs ~0.1 us). Returns false on expiry (the caller
+// records an error and winds down).
+__device__ __forceinline__ bool mbar_timed_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 1000000000ull) return false;
+  }
+}
 // Bounded wait: returns false when the phase did not complete within
 // `limit` polls (the caller records an error and winds down).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 26)) {

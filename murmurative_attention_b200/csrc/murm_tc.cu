@@ -109,20 +109,7 @@ template <typename T> struct Layout {
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
-  // About one second of polling, measured on the global timer.
-  uint64_t t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 256; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > 1000000000ull) return false;
-  }
-}
+__device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) { return mbar_timed_wait(bar, parity); }
 
 template <typename T>
 __device__ __forceinline__ uint16_t to_bits(float x) {

@@ -61,20 +61,7 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t COL_DV = 0, COL_DK = 128;
 enum : int { kErrWait = 8 };
 
-__device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
-  // About one second of polling, measured on the global timer.
-  uint64_t t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 256; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > 1000000000ull) return false;
-  }
-}
+__device__ __forceinline__ bool timed_wait(uint64_t* bar, uint32_t parity) { return mbar_timed_wait(bar, parity); }
 
 // acc += sum over i = 0..7 of a_i * b_i for two runs of eight 16-bit values (one uint4
 // each), in order; each product is exact and added with one rounding (fp32 fma on the
