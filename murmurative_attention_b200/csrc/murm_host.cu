@@ -47,11 +47,14 @@ cudaError_t pipe_for(int device, int groups, HostPipe** out) {
   return e;
 }
 
+constexpr int kMaxGroups = 64;
 struct HostLayout {
-  int groups, per;                  // number of groups, (b,h) pairs per group (last may be smaller)
+  int groups;
+  int64_t start[kMaxGroups + 1];    // group g holds the (b,h) pairs [start[g], start[g+1])
   size_t q, go, sk, sv, out, idx, w, gq, gsk, gsv;  // offsets of the full-size device copies
-  size_t saved, fws, bws;           // every group's saved block; one group's workspaces
-  size_t saved_bytes, fws_bytes, bws_bytes, total;
+  size_t saved[kMaxGroups];         // each group's saved block (kept from its forward to its backward)
+  size_t saved_bytes[kMaxGroups];
+  size_t fws, bws, fws_bytes, bws_bytes, total;  // workspaces sized for the largest group
 };
 
 murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
@@ -59,16 +62,28 @@ murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
   const int64_t bh = (int64_t)s->batch * s->heads;
   if (bh < 1) return report_error(MURM_ERR_INVALID_ARGUMENT, "batch * heads must be >= 1");
   // automatic: groups of at least 4 (b,h) pairs (smaller ones leave the round kernels' grids
-  // short of work), at least two groups so that copies overlap compute, at most 8
-  int64_t G = groups > 0 ? groups : (bh / 4 > 8 ? 8 : (bh / 4 > 2 ? bh / 4 : (bh < 2 ? bh : 2)));
-  if (G > bh) G = bh;
-  if (G > 64) G = 64;
-  L->per = (int)((bh + G - 1) / G);
-  L->groups = (int)((bh + L->per - 1) / L->per);
-  murm_shape gs = *s;
-  gs.batch = 1;
-  gs.heads = L->per;
-  if (murm_status st = murm_slot_murmurate_sizes(&gs, &L->saved_bytes, &L->fws_bytes, &L->bws_bytes)) return st;
+  // short of work), at least two groups so that copies overlap compute, at most 8. (Groups that
+  // grow from a small first one, to start the copies out earlier, measured no faster.)
+  int64_t want = groups > 0 ? groups : (bh / 4 > 8 ? 8 : (bh / 4 > 2 ? bh / 4 : 2));
+  if (want > bh) want = bh;
+  if (want > kMaxGroups) want = kMaxGroups;
+  const int64_t per = (bh + want - 1) / want;
+  int G = 0;
+  L->start[0] = 0;
+  for (int64_t p = 0; p < bh; p += per) L->start[++G] = p + per < bh ? p + per : bh;
+  L->groups = G;
+  size_t fws_max = 0, bws_max = 0;
+  for (int g = 0; g < G; ++g) {
+    murm_shape gs = *s;
+    gs.batch = 1;
+    gs.heads = (int32_t)(L->start[g + 1] - L->start[g]);
+    size_t f = 0, b = 0;
+    if (murm_status st = murm_slot_murmurate_sizes(&gs, &L->saved_bytes[g], &f, &b)) return st;
+    fws_max = f > fws_max ? f : fws_max;
+    bws_max = b > bws_max ? b : bws_max;
+  }
+  L->fws_bytes = fws_max;
+  L->bws_bytes = bws_max;
   const size_t es = elem_bytes(s->dtype);
   const size_t tok = (size_t)bh * s->tokens, slot = (size_t)bh * s->slots;
   size_t o = 0;
@@ -83,7 +98,7 @@ murm_status plan(const murm_shape* s, int32_t groups, HostLayout* L) {
   L->gq = take(tok * s->head_dim * es);
   L->gsk = take(slot * s->head_dim * es);
   L->gsv = take(slot * s->head_dim * es);
-  L->saved = take(align256(L->saved_bytes) * L->groups);
+  for (int g = 0; g < G; ++g) L->saved[g] = take(L->saved_bytes[g]);
   L->fws = take(L->fws_bytes);
   L->bws = take(L->bws_bytes);
   L->total = o;
@@ -139,8 +154,8 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
   if (!e) e = cudaStreamWaitEvent(P.in, P.ev[0], 0);
   if (!e) e = cudaStreamWaitEvent(P.out, P.ev[0], 0);
   auto pairs = [&](int g, int64_t* p0, int64_t* np) {
-    *p0 = (int64_t)g * L.per;
-    *np = (*p0 + L.per <= bh) ? L.per : bh - *p0;
+    *p0 = L.start[g];
+    *np = L.start[g + 1] - L.start[g];
   };
   // per group: q + slots copied in, grad_out copied in, forward done, backward done
   auto ev = [&](int g, int k) { return P.ev[2 + 4 * g + k]; };
@@ -161,7 +176,7 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
   }
   if (e) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
   // ---- forwards, then backwards, on the caller's stream ----
-  const int64_t ts[3] = {(int64_t)L.per * N * D, N * D, D}, ss[3] = {(int64_t)L.per * M * D, M * D, D};
+  const int64_t ts[3] = {bh * N * D, N * D, D}, ss[3] = {bh * M * D, M * D, D};  // batch stride unused (B = 1)
   auto group_shape = [&](int64_t np) {
     murm_shape gs = s;
     gs.batch = 1;
@@ -184,8 +199,8 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     }
     f.indices = reinterpret_cast<int64_t*>(ws + L.idx) + p0 * recn;
     f.weights = reinterpret_cast<float*>(ws + L.w) + p0 * recn;
-    f.saved = ws + L.saved + align256(L.saved_bytes) * g;
-    f.saved_bytes = L.saved_bytes;
+    f.saved = ws + L.saved[g];
+    f.saved_bytes = L.saved_bytes[g];
     f.workspace = ws + L.fws;
     f.workspace_bytes = L.fws_bytes;
     if (murm_status ms = murm_slot_murmurate_fwd(&f, st)) return ms;
@@ -199,8 +214,8 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     bw.shape = group_shape(np);
     bw.q = ws + L.q + p0 * tokb;
     bw.grad_out = ws + L.go + p0 * tokb;
-    bw.saved = ws + L.saved + align256(L.saved_bytes) * g;
-    bw.saved_bytes = L.saved_bytes;
+    bw.saved = ws + L.saved[g];
+    bw.saved_bytes = L.saved_bytes[g];
     bw.grad_q = ws + L.gq + p0 * tokb;
     bw.grad_slots_k = ws + L.gsk + p0 * slotb;
     bw.grad_slots_v = ws + L.gsv + p0 * slotb;
