@@ -771,25 +771,23 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
         if (__any_sync(0xffffffffu, exact_scan)) {
-          // exact full scan of the row's 256 columns from TMEM
+          // Rows with fewer than 7 finite group maxima have fewer than 7 finite scores: causal
+          // rows n < 6, lim = n + 1 <= 6 (every column below 7 is in a group of its own). Their
+          // picks are all lim finite columns and then the first masked ones in slot order (equal
+          // -inf keys, lower slot first), so only columns below lim + 7 <= 13 need a look.
+          float w32[32];
+          tmem_ld32(tmem + lane_base + tc::COL_S, w32);
+          tmem_wait_ld();
+          if (exact_scan) {  // rare path: kept compact (not unrolled)
+            const int mend = min(g.M, lim + kTopK);
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            float w32[32];
-            tmem_ld32(tmem + lane_base + tc::COL_S + 32 * c, w32);
-            tmem_wait_ld();
-            if (exact_scan) {  // rare path: kept compact (not unrolled)
-#pragma unroll 1
-              for (int i = 0; i < 32; ++i) {
-                const int m = 32 * c + i;
-                if (m < lim) {
-                  tc::offer7_asc(tkey, tslot, rank_key(w32[i]), m);
-                } else if (m < g.M) {
-                  if (m - lim < kTopK) {
+            for (int m = 0; m < mend; ++m) {
+              if (m < lim) {
+                tc::offer7_asc(tkey, tslot, rank_key(w32[m]), m);
+              } else {
 #pragma unroll
-                    for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[i] : mraw[j];
-                  }
-                  tc::offer7_asc(tkey, tslot, kNegInfKey, m);
-                }
+                for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[m] : mraw[j];
+                tc::offer7_asc(tkey, tslot, kNegInfKey, m);
               }
             }
           }
