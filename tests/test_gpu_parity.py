@@ -112,6 +112,8 @@ CASES = [
     (1, 2, 256, 64, 256, 1, True, torch.float16),
     (2, 2, 200, 64, 128, 3, False, torch.bfloat16),
     (1, 4, 520, 64, 256, 3, True, torch.bfloat16),
+    (1, 2, 40, 64, 9, 2, True, torch.float16),      # tensor-core path, causal, M < 13 (rows n < 6 pick masked slots)
+    (1, 1, 20, 64, 7, 3, True, torch.bfloat16),     # tensor-core path, causal, minimum slots
 ]
 
 
