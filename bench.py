@@ -337,7 +337,10 @@ def roofline(prof, prof_steps, peaks):
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                 "peak_source": f"{peaks['source']} (burst dense bf16)",
                 "work_per_launch": f"select GEMM 2*M*d*tokens = {flops:.4g} FLOP",
-                "avg_launch_ms": round(avg_ms, 5), "launches": launches}
+                "avg_launch_ms": round(avg_ms, 5), "launches": launches,
+                "limiter": "neither bound is reached: the CUDA-core top-7 selection between the MMAs limits it "
+                           "(ncu: ALU pipe ~50% of active cycles, issue ~37%, tensor pipe ~17%; "
+                           "profiles/k_fwd_tc_northstar.md)"}
     # memory-bound kernels: algorithmic bytes of the whole step spread over its launches
     per_launch = algorithmic_bytes() / (launches / prof_steps)
     achieved = per_launch / (avg_ms / 1e3) / 1e9
