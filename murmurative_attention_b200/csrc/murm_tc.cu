@@ -729,16 +729,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         for (int k = 0; k < 2; ++k) {
           uint32_t msk = scan ? tc::ge_mask32(x[k], thr) : 0u;
           while (__any_sync(0xffffffffu, msk != 0)) {
-            // uniform body, two columns per pass, lowest first; a lane with no bit left offers
-            // key 0 (no change). The two select-tree reads are independent (they overlap).
+            // uniform body, lowest column first; a lane with no bit left offers key 0 (no change)
             const int bit = __ffs(msk) - 1;
-            const uint32_t m1 = msk & (msk - 1);
-            const int bit2 = __ffs(m1) - 1;
             const uint32_t key = rank_key(tc::pick32(x[k], bit & 31));
-            const uint32_t key2 = rank_key(tc::pick32(x[k], bit2 & 31));
             tc::offer7_asc(tkey, tslot, msk ? key : 0u, col0 + 32 * (c + k) + bit);
-            tc::offer7_asc(tkey, tslot, m1 ? key2 : 0u, col0 + 32 * (c + k) + bit2);
-            msk = m1 & (m1 - 1);
+            msk &= msk - 1;
           }
         }
       };
