@@ -25,7 +25,7 @@ size_t elem_bytes(int dtype) { return dtype == MURM_F32 ? 4 : 2; }
 // One device's copy streams and events, created on first use and kept for the process.
 struct HostPipe {
   cudaStream_t in = nullptr, out = nullptr;
-  std::vector<cudaEvent_t> ev;  // [0] start, [1] done, then 4 per group (see kEvents)
+  std::vector<cudaEvent_t> ev;  // [0] start, [1] copies out done, [2] copies in done, then 4 per group
 };
 std::mutex g_pipe_mu;
 std::mutex g_call_mu;
@@ -38,7 +38,7 @@ cudaError_t pipe_for(int device, int groups, HostPipe** out) {
   cudaError_t e = cudaSuccess;
   if (!p.in) e = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking);
   if (e == cudaSuccess && !p.out) e = cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking);
-  while (e == cudaSuccess && (int)p.ev.size() < 2 + 4 * groups) {
+  while (e == cudaSuccess && (int)p.ev.size() < 3 + 4 * groups) {
     cudaEvent_t ev;
     e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     if (e == cudaSuccess) p.ev.push_back(ev);
@@ -158,7 +158,20 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     *np = L.start[g + 1] - L.start[g];
   };
   // per group: q + slots copied in, grad_out copied in, forward done, backward done
-  auto ev = [&](int g, int k) { return P.ev[2 + 4 * g + k]; };
+  auto ev = [&](int g, int k) { return P.ev[3 + 4 * g + k]; };
+  // every exit leaves the caller's stream behind both copy streams, so that work the caller
+  // orders after this call (freeing the workspace, reading the host buffers) sees them finished
+  auto join = [&]() {
+    cudaError_t j = cudaEventRecord(P.ev[2], P.in);
+    if (!j) j = cudaStreamWaitEvent(st, P.ev[2], 0);
+    if (!j) j = cudaEventRecord(P.ev[1], P.out);
+    if (!j) j = cudaStreamWaitEvent(st, P.ev[1], 0);
+    return j;
+  };
+  auto fail_cuda = [&](cudaError_t err) {
+    join();
+    return report_error(MURM_ERR_CUDA, cudaGetErrorString(err));
+  };
   // ---- copies in: q and slots of every group, then grad_out ----
   for (int g = 0; g < L.groups && !e; ++g) {
     int64_t p0, np;
@@ -174,7 +187,7 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     e = H2D(L.go, a->grad_out, p0 * tokb, np * tokb);
     if (!e) e = cudaEventRecord(ev(g, 1), P.in);
   }
-  if (e) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
+  if (e) return fail_cuda(e);
   // ---- forwards, then backwards, on the caller's stream ----
   const int64_t ts[3] = {bh * N * D, N * D, D}, ss[3] = {bh * M * D, M * D, D};  // batch stride unused (B = 1)
   auto group_shape = [&](int64_t np) {
@@ -203,7 +216,10 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     f.saved_bytes = L.saved_bytes[g];
     f.workspace = ws + L.fws;
     f.workspace_bytes = L.fws_bytes;
-    if (murm_status ms = murm_slot_murmurate_fwd(&f, st)) return ms;
+    if (murm_status ms = murm_slot_murmurate_fwd(&f, st)) {
+      join();
+      return ms;
+    }
     e = cudaEventRecord(ev(g, 2), st);
   }
   for (int g = 0; g < L.groups && !e; ++g) {
@@ -225,7 +241,10 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     }
     bw.workspace = ws + L.bws;
     bw.workspace_bytes = L.bws_bytes;
-    if (murm_status ms = murm_slot_murmurate_bwd(&bw, st)) return ms;
+    if (murm_status ms = murm_slot_murmurate_bwd(&bw, st)) {
+      join();
+      return ms;
+    }
     e = cudaEventRecord(ev(g, 3), st);
   }
   // ---- copies out: each forward's results, then each backward's gradients ----
@@ -245,10 +264,9 @@ murm_status murm_slot_murmurate_host_step(const murm_host_step_args* a, void* st
     if (!e) e = D2H(a->grad_slots_k, L.gsk, p0 * slotb, np * slotb);
     if (!e) e = D2H(a->grad_slots_v, L.gsv, p0 * slotb, np * slotb);
   }
+  if (e) return fail_cuda(e);
   // the caller's stream completes after the last copy out
-  if (!e) e = cudaEventRecord(P.ev[1], P.out);
-  if (!e) e = cudaStreamWaitEvent(st, P.ev[1], 0);
-  if (e) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
+  if ((e = join())) return report_error(MURM_ERR_CUDA, cudaGetErrorString(e));
   return MURM_OK;
 }
 

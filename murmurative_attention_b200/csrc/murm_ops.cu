@@ -712,6 +712,156 @@ __global__ void __launch_bounds__(256) k_decode(murm_decode_args a) {
   }
 }
 
+// Decode step with 16-byte pool accesses (pool rows whose byte size and strides are multiples
+// of 16): the pool stays in its own dtype in shared memory (half the footprint of an fp32
+// copy, so several heads share an SM), rows of C 16-byte chunks with chunk c of row m at
+// c ^ (m & swz), so that a warp's threads, one slot each, read different banks. Same
+// arithmetic, in the same order, as k_decode.
+template <typename T>
+__global__ void __launch_bounds__(256) k_decode_v(murm_decode_args a) {
+  extern __shared__ uint4 smv[];
+  constexpr int E = 16 / (int)sizeof(T);  // elements per chunk
+  const int M = a.slots, D = a.head_dim, C = D / E;
+  const int swz = ((C & (C - 1)) == 0) ? (C < 8 ? C - 1 : 7) : 0;
+  uint4* sK = smv;                                  // [M][C]
+  uint4* sV = sK + (size_t)M * C;                   // [M][C]
+  float* qv = reinterpret_cast<float*>(sV + (size_t)M * C);  // [D]
+  float* kv = qv + D;                               // [D] token key
+  float* vv = kv + D;                               // [D] token value
+  uint32_t* keys = reinterpret_cast<uint32_t*>(vv + D);  // [M]
+  int* pick_s = reinterpret_cast<int*>(keys + M);        // [8]
+  float* w_s = reinterpret_cast<float*>(pick_s + 8);     // [8]
+  const int bh = blockIdx.x, b = bh / a.heads, h = bh - b * a.heads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto at = [&](int m, int c) { return m * C + (c ^ (m & swz)); };
+  auto elem = [&](const uint4* arr, int m, int d) -> T* {
+    return reinterpret_cast<T*>(const_cast<uint4*>(arr) + at(m, d / E)) + (d % E);
+  };
+  const T* gk = static_cast<const T*>(a.slot_keys);
+  const T* gv = static_cast<const T*>(a.slot_values);
+  for (int e = tid; e < M * C; e += blockDim.x) {
+    const int m = e / C, c = e - m * C;
+    sK[at(m, c)] = *reinterpret_cast<const uint4*>(gk + off3(a.sk_stride, b, h, m) + c * E);
+    sV[at(m, c)] = *reinterpret_cast<const uint4*>(gv + off3(a.sv_stride, b, h, m) + c * E);
+  }
+  const int64_t qo = (int64_t)b * a.q_stride[0] + (int64_t)h * a.q_stride[1];
+  const int64_t ko = (int64_t)b * a.k_stride[0] + (int64_t)h * a.k_stride[1];
+  const int64_t vo = (int64_t)b * a.v_stride[0] + (int64_t)h * a.v_stride[1];
+  for (int d = tid; d < D; d += blockDim.x) {
+    qv[d] = ld<T>(a.q, qo + d);
+    kv[d] = ld<T>(a.k, ko + d);
+    vv[d] = ld<T>(a.v, vo + d);
+  }
+  __syncthreads();
+  const int64_t pos = a.causal ? a.positions[b] : 0;
+  for (int m = tid; m < M; m += blockDim.x) {  // selection scores (reference.py:19, 27-31)
+    float s = 0.f;
+    for (int c = 0; c < C; ++c) {
+      const uint4 u = sK[at(m, c)];
+      const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < E; ++i) s = fmaf(qv[c * E + i], Elem<T>::load(t + i), s);
+    }
+    keys[m] = rank_key((a.causal && m > pos) ? -INFINITY : s);
+  }
+  __syncthreads();
+  const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
+  if (warp == 0) {
+    uint32_t tk[kTopK];
+    int ts[kTopK];
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
+    for (int m = lane; m < M; m += 32) offer7(tk, ts, keys[m], m);
+    warp_top7(tk, ts);
+    float sc[kTopK], mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {  // attend scores without the mask (reference.py:61)
+      float p = 0.f;
+      for (int d = lane; d < D; d += 32) p = fmaf(qv[d], Elem<T>::load(elem(sK, ts[j], d)), p);
+      sc[j] = warp_sum(p) * scale;
+      mx = fmaxf(mx, sc[j]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) {
+      sc[j] = expf(sc[j] - mx);
+      sum += sc[j];
+    }
+    if (lane < kTopK) {
+      int pj = ts[0];
+      float wj = sc[0];
+#pragma unroll
+      for (int j = 1; j < kTopK; ++j)
+        if (lane == j) { pj = ts[j]; wj = sc[j]; }
+      wj = wj / sum;
+      pick_s[lane] = pj;
+      w_s[lane] = wj;
+      if (a.indices) a.indices[(int64_t)bh * kTopK + lane] = pj;
+      if (a.weights) a.weights[(int64_t)bh * kTopK + lane] = wj;
+    }
+  }
+  __syncthreads();
+  // out = x + sum_j w_j V[i_j] (with the values before this token's update)
+  const int64_t oo = (int64_t)b * a.out_stride[0] + (int64_t)h * a.out_stride[1];
+  const int64_t xo = a.x ? (int64_t)b * a.x_stride[0] + (int64_t)h * a.x_stride[1] : 0;
+  for (int d = tid; d < D; d += blockDim.x) {
+    float o = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) o = fmaf(w_s[j], Elem<T>::load(elem(sV, pick_s[j], d)), o);
+    st<T>(a.out, oo + d, (a.x ? ld<T>(a.x, xo + d) : 0.f) + o);
+  }
+  __syncthreads();
+  // update of the picked (distinct) slots with this one token (reference.py:93-115)
+  const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
+  for (int e = tid; e < kTopK * D; e += blockDim.x) {
+    const int j = e / D, d = e - j * D, m = pick_s[j];
+    const float wj = w_s[j];
+    if (wj > 0.f) {
+      const float den = __fadd_rn(wj, kEmaEps);
+      const float uk = __fdiv_rn(__fmul_rn(kv[d], wj), den), uv = __fdiv_rn(__fmul_rn(vv[d], wj), den);
+      T* pk = elem(sK, m, d);
+      T* pv = elem(sV, m, d);
+      Elem<T>::store(pk, __fadd_rn(__fmul_rn(al, Elem<T>::load(pk)), __fmul_rn(om, uk)));
+      Elem<T>::store(pv, __fadd_rn(__fmul_rn(al, Elem<T>::load(pv)), __fmul_rn(om, uv)));
+    }
+  }
+  __syncthreads();
+  // diffusion of the whole pool, written back 16 bytes at a time (reference.py:128-133)
+  const float gm = (float)a.gamma;
+  T* ok = static_cast<T*>(a.slot_keys);
+  T* ov = static_cast<T*>(a.slot_values);
+  for (int e = tid; e < M * C; e += blockDim.x) {
+    const int m = e / C, c = e - m * C;
+    const bool inner = m > 0 && m < M - 1;
+    const uint4 k0 = sK[at(m, c)], v0 = sV[at(m, c)];
+    uint4 kl = k0, kr = k0, vl = v0, vr = v0;
+    if (inner) {
+      kl = sK[at(m - 1, c)]; kr = sK[at(m + 1, c)];
+      vl = sV[at(m - 1, c)]; vr = sV[at(m + 1, c)];
+    }
+    uint4 ko4, vo4;
+    const T *tk0 = reinterpret_cast<const T*>(&k0), *tkl = reinterpret_cast<const T*>(&kl),
+            *tkr = reinterpret_cast<const T*>(&kr), *tv0 = reinterpret_cast<const T*>(&v0),
+            *tvl = reinterpret_cast<const T*>(&vl), *tvr = reinterpret_cast<const T*>(&vr);
+    T* tko = reinterpret_cast<T*>(&ko4);
+    T* tvo = reinterpret_cast<T*>(&vo4);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      float k = Elem<T>::load(tk0 + i), v = Elem<T>::load(tv0 + i);
+      if (inner) {
+        k = __fadd_rn(k, __fmul_rn(gm, __fsub_rn(__fadd_rn(Elem<T>::load(tkl + i), Elem<T>::load(tkr + i)),
+                                                  __fmul_rn(2.f, k))));
+        v = __fadd_rn(v, __fmul_rn(gm, __fsub_rn(__fadd_rn(Elem<T>::load(tvl + i), Elem<T>::load(tvr + i)),
+                                                  __fmul_rn(2.f, v))));
+      }
+      Elem<T>::store(tko + i, k);
+      Elem<T>::store(tvo + i, v);
+    }
+    *reinterpret_cast<uint4*>(ok + off3(a.sk_stride, b, h, m) + c * E) = ko4;
+    *reinterpret_cast<uint4*>(ov + off3(a.sv_stride, b, h, m) + c * E) = vo4;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1073,15 +1223,21 @@ MURM_API murm_status murm_decode_step(const murm_decode_args* a, void* stream) {
   if (!std::isfinite(a->alpha) || !std::isfinite(a->gamma) || !std::isfinite(a->scale))
     return ph::bad(MURM_ERR_INVALID_ARGUMENT, "alpha, gamma and scale must be finite");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  auto go = [&](auto kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    MURM_LAUNCH("decode_step", kern, dim3(a->batch * a->heads), 256, smem, st, *a);
+  // 16-byte pool accesses when every pool row starts on a 16-byte boundary
+  const size_t es = a->dtype == MURM_F32 ? 4 : 2;
+  bool vec = ((size_t)a->head_dim * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a->slot_keys) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(a->slot_values) & 15) == 0;
+  for (int i = 0; i < 3; ++i) vec = vec && (a->sk_stride[i] * (int64_t)es) % 16 == 0 && (a->sv_stride[i] * (int64_t)es) % 16 == 0;
+  const size_t smem_v = (size_t)a->slots * a->head_dim * es * 2 + (size_t)a->head_dim * 12 + (size_t)a->slots * 4 + 64;
+  auto go = [&](auto kern, size_t bytes) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    MURM_LAUNCH("decode_step", kern, dim3(a->batch * a->heads), 256, bytes, st, *a);
     return ph::launched("decode step");
   };
   switch (a->dtype) {
-    case MURM_F32: return go(ph::k_decode<float>);
-    case MURM_F16: return go(ph::k_decode<__half>);
-    case MURM_BF16: return go(ph::k_decode<__nv_bfloat16>);
+    case MURM_F32: return vec ? go(ph::k_decode_v<float>, smem_v) : go(ph::k_decode<float>, smem);
+    case MURM_F16: return vec ? go(ph::k_decode_v<__half>, smem_v) : go(ph::k_decode<__half>, smem);
+    case MURM_BF16: return vec ? go(ph::k_decode_v<__nv_bfloat16>, smem_v) : go(ph::k_decode<__nv_bfloat16>, smem);
   }
   return ph::bad(MURM_ERR_DTYPE, "unsupported dtype code %d", a->dtype);
 }
