@@ -112,16 +112,30 @@ __device__ __forceinline__ int64_t off4(const int64_t* s, int b, int h, int n, i
 // consecutive slots), and each warp's q row.
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args a, int Mp) {
+__global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args a, int Mp, int vec) {
   extern __shared__ float sh[];
   const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
   float* Kt = sh;                       // [D][Mp]
   float* qs = sh + (size_t)D * Mp;      // [kWarps][D]
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < M * D; e += blockDim.x) {
-    const int m = e / D, d = e - m * D;
-    Kt[(size_t)d * Mp + m] = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+  if (vec) {  // 16-byte loads (rows 16-byte aligned), several in flight per thread
+    constexpr int E = 16 / (int)sizeof(T);
+    const int C = D / E;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < M * C; e += blockDim.x) {
+      const int m = e / C, c = e - m * C;
+      const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const T*>(a.slot_keys) +
+                                                      off3(a.sk_stride, b, h, m) + c * E);
+      const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < E; ++i) Kt[(size_t)(c * E + i) * Mp + m] = Elem<T>::load(t + i);
+    }
+  } else {
+    for (int e = threadIdx.x; e < M * D; e += blockDim.x) {
+      const int m = e / D, d = e - m * D;
+      Kt[(size_t)d * Mp + m] = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+    }
   }
   __syncthreads();
   const int em = (a.effective_m > 0 && a.effective_m < M) ? a.effective_m : M;
@@ -142,13 +156,30 @@ __global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args 
       int ts[kTopK];
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
-      for (int m = lane; m < M; m += 32) {
-        float s = 0.f;
-        for (int d = 0; d < D; ++d) s = fmaf(q[d], Kt[(size_t)d * Mp + m], s);
-        if (a.position_bias) s += ld<T>(a.position_bias, off4(a.bias_stride, b, h, n, m));     // reference.py:21-22
-        bool masked = m >= em || (a.causal && m > n);                                            // :27-36
-        if (a.mask) masked = masked || a.mask[off4(a.mask_stride, b, h, n, m)] == 0;               // :24-25
-        offer7(tk, ts, rank_key(masked ? -INFINITY : s), m);
+      // 8 slots per lane at a time (m = m0 + lane + 32 j): independent dot products over the
+      // same q[d] (each in d order), offered in slot order
+      for (int m0 = 0; m0 < M; m0 += 256) {
+        float sj[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sj[j] = 0.f;
+        const int mc = min(M - 1, m0 + lane);  // clamped columns: reads stay inside Kt
+        for (int d = 0; d < D; ++d) {
+          const float qd = q[d];
+          const float* row = Kt + (size_t)d * Mp;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sj[j] = fmaf(qd, row[min(M - 1, mc + 32 * j)], sj[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int m = m0 + lane + 32 * j;
+          if (m < M) {
+            float s = sj[j];
+            if (a.position_bias) s += ld<T>(a.position_bias, off4(a.bias_stride, b, h, n, m));     // reference.py:21-22
+            bool masked = m >= em || (a.causal && m > n);                                            // :27-36
+            if (a.mask) masked = masked || a.mask[off4(a.mask_stride, b, h, n, m)] == 0;               // :24-25
+            offer7(tk, ts, rank_key(masked ? -INFINITY : s), m);
+          }
+        }
       }
       warp_top7(tk, ts);
 #pragma unroll
@@ -952,7 +983,10 @@ murm_status sa_fwd(const murm_select_attend_args& a, cudaStream_t st) {
   const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
   cudaFuncSetAttribute(k_sa_fwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const dim3 grid((a.shape.tokens + kWarps * kTokPerWarp - 1) / (kWarps * kTokPerWarp), a.shape.batch * a.shape.heads);
-  MURM_LAUNCH("phase_select_attend", k_sa_fwd<T>, grid, 32 * kWarps, smem, st, a, Mp);
+  const int64_t es = (int64_t)sizeof(T);
+  int vec = (a.shape.head_dim * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.slot_keys) & 15) == 0;
+  for (int i = 0; i < 3; ++i) vec = vec && (a.sk_stride[i] * es) % 16 == 0;
+  MURM_LAUNCH("phase_select_attend", k_sa_fwd<T>, grid, 32 * kWarps, smem, st, a, Mp, vec);
   return launched("select_attend forward");
 }
 
