@@ -373,6 +373,65 @@ __global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args 
   }
 }
 
+// Over a slot's (token, pick) entries [e0, e1) in token order: acc1 += f1 * A[t] and
+// acc2 += f2 * B[t] (lane's dims d = lane + 32 u), with f1, f2 per-pair factors
+// (f[(rec0 + t) * stride + pick]) and, when fsum is given, *fsum += f2. The loads of four
+// entries are issued before their sums, so that four rows are in flight; the sums are taken in
+// entry order all the same.
+template <typename T>
+__device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_t rec0, const float* f1, int s1,
+                                          const float* f2, int s2, const T* A, const int64_t* as, const T* Bp,
+                                          const int64_t* bs, int b, int h, int D, int lane,
+                                          float (&acc1)[kMaxD / 32], float (&acc2)[kMaxD / 32], float* fsum) {
+  constexpr int U = kMaxD / 32;
+  int e = e0;
+  for (; e + 4 <= e1; e += 4) {
+    int tt[4], jj[4];
+    float x1[4], x2[4], ra[4][U], rb[4][U];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int en = ent[e + r];
+      tt[r] = en >> 3;
+      jj[r] = en & 7;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      x1[r] = f1[(rec0 + tt[r]) * s1 + jj[r]];
+      x2[r] = f2[(rec0 + tt[r]) * s2 + jj[r]];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int d = lane + 32 * u;
+        ra[r][u] = d < D ? Elem<T>::load(A + off3(as, b, h, tt[r]) + d) : 0.f;
+        rb[r][u] = d < D ? Elem<T>::load(Bp + off3(bs, b, h, tt[r]) + d) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      if (fsum) *fsum += x2[r];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (lane + 32 * u < D) {
+          acc1[u] = fmaf(x1[r], ra[r][u], acc1[u]);
+          acc2[u] = fmaf(x2[r], rb[r][u], acc2[u]);
+        }
+      }
+    }
+  }
+  for (; e < e1; ++e) {
+    const int t = ent[e] >> 3, j = ent[e] & 7;
+    const float y1 = f1[(rec0 + t) * s1 + j], y2 = f2[(rec0 + t) * s2 + j];
+    if (fsum) *fsum += y2;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        acc1[u] = fmaf(y1, Elem<T>::load(A + off3(as, b, h, t) + d), acc1[u]);
+        acc2[u] = fmaf(y2, Elem<T>::load(Bp + off3(bs, b, h, t) + d), acc2[u]);
+      }
+    }
+  }
+}
+
 // slot side: a warp per (b,h, slot), its pairs in token order:
 //   dK[m] = sum coef * q[t],  dV[m] = sum w * g[t]
 template <typename T>
@@ -388,19 +447,8 @@ __global__ void __launch_bounds__(256) k_sa_bwd_slot(murm_select_attend_bwd_args
   float dk[kMaxD / 32], dv[kMaxD / 32];
 #pragma unroll
   for (int u = 0; u < kMaxD / 32; ++u) dk[u] = dv[u] = 0.f;
-  for (int e = off[m]; e < off[m + 1]; ++e) {
-    const int t = ent[e] >> 3, j = ent[e] & 7;
-    const float cf = coef[((int64_t)bh * N + t) * 8 + j];
-    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
-#pragma unroll
-    for (int u = 0; u < kMaxD / 32; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) {
-        dk[u] = fmaf(cf, ld<T>(a.q, off3(a.q_stride, b, h, t) + d), dk[u]);
-        dv[u] = fmaf(wt, ld<T>(a.grad_out, off3(a.go_stride, b, h, t) + d), dv[u]);
-      }
-    }
-  }
+  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, coef, 8, a.weights, kTopK, static_cast<const T*>(a.q),
+               a.q_stride, static_cast<const T*>(a.grad_out), a.go_stride, b, h, D, lane, dk, dv, nullptr);
 #pragma unroll
   for (int u = 0; u < kMaxD / 32; ++u) {
     const int d = lane + 32 * u;
@@ -429,19 +477,9 @@ __global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const 
   float W = 0.f;
 #pragma unroll
   for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
-  for (int e = off[m]; e < off[m + 1]; ++e) {
-    const int t = ent[e] >> 3, j = ent[e] & 7;
-    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
-    W += wt;
-#pragma unroll
-    for (int u = 0; u < kMaxD / 32; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) {
-        sk[u] = fmaf(wt, ld<T>(a.token_keys, off3(a.tk_stride, b, h, t) + d), sk[u]);
-        sv[u] = fmaf(wt, ld<T>(a.token_values, off3(a.tv_stride, b, h, t) + d), sv[u]);
-      }
-    }
-  }
+  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+               static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
+               b, h, D, lane, sk, sv, &W);
   const bool valid = W > 0.f;                       // reference.py:105
   const float den = __fadd_rn(W, kEmaEps);          // :106-107
   const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
@@ -479,19 +517,9 @@ __global__ void __launch_bounds__(256) k_sums_fwd(murm_slot_sums_args a, const i
   float W = 0.f;
 #pragma unroll
   for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
-  for (int e = off[m]; e < off[m + 1]; ++e) {
-    const int t = ent[e] >> 3, j = ent[e] & 7;
-    const float wt = a.weights[((int64_t)bh * N + t) * kTopK + j];
-    W += wt;
-#pragma unroll
-    for (int u = 0; u < kMaxD / 32; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) {
-        sk[u] = fmaf(wt, ld<T>(a.token_keys, off3(a.tk_stride, b, h, t) + d), sk[u]);
-        sv[u] = fmaf(wt, ld<T>(a.token_values, off3(a.tv_stride, b, h, t) + d), sv[u]);
-      }
-    }
-  }
+  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+               static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
+               b, h, D, lane, sk, sv, &W);
   const size_t so = ((size_t)bh * M + m) * D;
 #pragma unroll
   for (int u = 0; u < kMaxD / 32; ++u) {
