@@ -30,13 +30,6 @@ struct Dims {
 
 __device__ __forceinline__ int clampi(int64_t v, int M) { return (int)(v < 0 ? 0 : (v >= M ? M - 1 : v)); }
 
-// 64-bit rank: larger = earlier in (score desc, slot asc); 0 = empty.
-__device__ __forceinline__ uint64_t rank64(uint32_t key, int slot) {
-  return ((uint64_t)key << 32) | (uint32_t)~slot;
-}
-__device__ __forceinline__ uint64_t mx64(uint64_t a, uint64_t b) { return a > b ? a : b; }
-__device__ __forceinline__ uint64_t mn64(uint64_t a, uint64_t b) { return a > b ? b : a; }
-
 // Insert into a 7-entry list kept in rank order; offers must come in ascending slot
 // order (then equal keys never displace an earlier slot).
 __device__ __forceinline__ void offer7(uint32_t (&k)[kTopK], int (&s)[kTopK], uint32_t xk, int xs) {
@@ -52,36 +45,32 @@ __device__ __forceinline__ void offer7(uint32_t (&k)[kTopK], int (&s)[kTopK], ui
   s[0] = gt[0] ? xs : s[0];
 }
 
-// The warp's best 7 of all lanes' lists: butterfly of bitonic merges of 64-bit ranks.
+// The warp's best 7 of all lanes' lists (each in rank order), in 7 rounds: the largest head
+// key over the lanes (one reduction), the lowest slot among the heads with that key (another),
+// and the lane holding that entry moves its list up. Every lane returns the same list.
 __device__ __forceinline__ void warp_top7(uint32_t (&k)[kTopK], int (&s)[kTopK]) {
-  uint64_t a[8];
+  uint32_t ok[kTopK];
+  int os[kTopK];
 #pragma unroll
-  for (int j = 0; j < kTopK; ++j) a[j] = rank64(k[j], s[j]);
-  a[7] = 0;
+  for (int r = 0; r < kTopK; ++r) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, k[0]);
+    const uint32_t slot = __reduce_min_sync(0xffffffffu, k[0] == best ? (uint32_t)s[0] : 0xffffffffu);
+    ok[r] = best;
+    os[r] = (int)slot;
+    if (k[0] == best && (uint32_t)s[0] == slot) {
 #pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    uint64_t b[8], c[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) b[j] = __shfl_xor_sync(0xffffffffu, a[j], o);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) c[i] = mx64(a[i], b[7 - i]);
-#pragma unroll
-    for (int st = 4; st >= 1; st >>= 1)
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if ((i & st) == 0) {
-          const uint64_t x = c[i], y = c[i + st];
-          c[i] = mx64(x, y);
-          c[i + st] = mn64(x, y);
-        }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = c[j];
-    a[7] = 0;
+      for (int j = 0; j < kTopK - 1; ++j) {
+        k[j] = k[j + 1];
+        s[j] = s[j + 1];
+      }
+      k[kTopK - 1] = 0u;
+      s[kTopK - 1] = 0;
+    }
   }
 #pragma unroll
   for (int j = 0; j < kTopK; ++j) {
-    k[j] = (uint32_t)(a[j] >> 32);
-    s[j] = (int)~(uint32_t)a[j];
+    k[j] = ok[j];
+    s[j] = os[j];
   }
 }
 
