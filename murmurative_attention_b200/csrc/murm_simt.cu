@@ -138,8 +138,12 @@ __global__ void k_load_slots(Geom g, const T* sk, Strides3 sks, const T* sv, Str
 // K1: select (top-7) + attend for one round, thread per token.
 //   reference.py:19-38 scores / causal mask / topk;  reference.py:56-68 attend.
 // ---------------------------------------------------------------------------
+// Thread-per-token kernels whose blocks hold a (b,h)'s slot tables in shared memory (one block
+// per SM) run kSimtTPB threads, so that an SM has 16 warps to hide latency with.
+constexpr int kSimtTPB = 4 * kTile;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kTile) k_select_attend(Geom g, int r, const T* q, Strides3 qs, T* out,
+__global__ void __launch_bounds__(kSimtTPB) k_select_attend(Geom g, int r, const T* q, Strides3 qs, T* out,
                                                          Strides3 os, int64_t* indices, float* weights,
                                                          Saved sv) {
   extern __shared__ __align__(16) float smem[];
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kTile) k_select_attend(Geom g, int r, const T*
   copy_to_smem(Vs, sv.V + slot_off, g.M * D);
   __syncthreads();
 
-  const int n = blockIdx.x * kTile + threadIdx.x;
+  const int n = blockIdx.x * kSimtTPB + threadIdx.x;
   if (n >= g.N) return;
   float qv[D];
   load_row<T, D>(row_ptr(q, qs, b, h, n), qv);
@@ -378,7 +382,7 @@ __global__ void __launch_bounds__(256) k_bwd_prep(Geom g, int r, Saved sv, const
 //   dq   += sum_j w_j dS[i_j] + scale da_j K[i_j]
 //   coef_j = scale da_j   (used by the scatter kernel for dK)
 template <typename T, int D>
-__global__ void __launch_bounds__(kTile) k_bwd_tokens(Geom g, int r, int has_slot_grad, const T* q,
+__global__ void __launch_bounds__(kSimtTPB) k_bwd_tokens(Geom g, int r, int has_slot_grad, const T* q,
                                                       Strides3 qs, const T* go, Strides3 gos, const float* gw,
                                                       T* gq, Strides3 gqs, Saved sv, BwdScratch bs) {
   extern __shared__ __align__(16) float smem[];
@@ -396,7 +400,7 @@ __global__ void __launch_bounds__(kTile) k_bwd_tokens(Geom g, int r, int has_slo
     for (int i = threadIdx.x; i < g.M; i += blockDim.x) dWs[i] = bs.dW[(size_t)bh * g.M + i];
   }
   __syncthreads();
-  const int n = blockIdx.x * kTile + threadIdx.x;
+  const int n = blockIdx.x * kSimtTPB + threadIdx.x;
   if (n >= g.N) return;
 
   const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
@@ -604,7 +608,8 @@ static cudaError_t run_fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv
     MURM_LAUNCH("load_slots", k_load_slots<T>, dim3(g.BH, 4), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
                                                     static_cast<const T*>(p.sv), p.svs, sv.K, sv.V);
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH("select_attend_simt", (k_select_attend<T, D>), dim3(g.fwd_chunks, g.BH), kTile, smem_sa, st, 
+    MURM_LAUNCH("select_attend_simt", (k_select_attend<T, D>), dim3((g.N + kSimtTPB - 1) / kSimtTPB, g.BH), kSimtTPB,
+                smem_sa, st, 
         g, r, q, p.qs, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv);
     if (r + 1 < g.R) {
       MURM_LAUNCH("update_partial", (k_update_partial<T, D>), dim3(g.red_chunks, g.BH), 256, smem_up, st, g, r, q, p.qs, sv, fs);
@@ -645,7 +650,8 @@ static cudaError_t run_bwd_simt(const Geom& g, const BwdPtrs& p, const Saved& sv
   for (int r = g.R - 1; r >= 0; --r) {
     const int has_slot_grad = r < g.R - 1;
     if (has_slot_grad) MURM_LAUNCH("bwd_prep", k_bwd_prep, g.BH, 256, 0, st, g, r, sv, bs.dK[cur], bs.dV[cur], bs);
-    MURM_LAUNCH("bwd_tokens", (k_bwd_tokens<T, D>), dim3(g.fwd_chunks, g.BH), kTile, smem_tok, st, 
+    MURM_LAUNCH("bwd_tokens", (k_bwd_tokens<T, D>), dim3((g.N + kSimtTPB - 1) / kSimtTPB, g.BH), kSimtTPB,
+                smem_tok, st, 
         g, r, has_slot_grad, q, p.qs, go, p.gos, p.gw, static_cast<T*>(p.gq), p.gqs, sv, bs);
     MURM_LAUNCH("bwd_scatter", (k_bwd_scatter<T, D>), dim3(g.red_chunks, g.BH), 256, smem_sc, st, g, r, q, p.qs, go, p.gos, sv, bs);
     MURM_LAUNCH("bwd_finalize", k_bwd_finalize<T>, dim3(g.BH, fin_y), 256, 0, st, g, r, bs, has_slot_grad, bs.dK[cur ^ 1],
