@@ -88,6 +88,13 @@ Geom make_geom(const murm_shape* s) {
   const int tiles_per = (tiles + red - 1) / red;
   g.red_chunk_tokens = tiles_per * kTile;
   g.red_chunks = (g.N + g.red_chunk_tokens - 1) / g.red_chunk_tokens;
+  // the backward token kernel splits each (b,h) at its own 64-token granularity: on 16 pairs of
+  // 8192 tokens, 9 chunks of at most 15 tiles (144 CTAs) instead of 8 of 16
+  const int btiles = (g.N + kBwdTile - 1) / kBwdTile;
+  int bred = kSmCount / g.BH;
+  bred = bred < 1 ? 1 : (bred > btiles ? btiles : bred);
+  g.bwd_chunk_tokens = ((btiles + bred - 1) / bred) * kBwdTile;
+  g.bwd_chunks = (g.N + g.bwd_chunk_tokens - 1) / g.bwd_chunk_tokens;
   return g;
 }
 
@@ -121,8 +128,9 @@ Sizes make_sizes(const Geom& g) {
   o = 0;
   z.bdK0 = take(slot); z.bdK1 = take(slot); z.bdV0 = take(slot); z.bdV1 = take(slot);
   z.bdS = take(slot); z.bdW = take(BH * M * 4); z.bdKdir = take(slot); z.bdVdir = take(slot);
-  z.bdKpart = take(BH * g.red_chunks * M * D * 4);
-  z.bdVpart = take(BH * g.red_chunks * M * D * 4);
+  const size_t bparts = (size_t)(g.bwd_chunks > g.red_chunks ? g.bwd_chunks : g.red_chunks);
+  z.bdKpart = take(BH * bparts * M * D * 4);
+  z.bdVpart = take(BH * bparts * M * D * 4);
   z.bcoef = take(BH * N * 8 * 4);
   z.bdq = take(BH * N * D * 4);
   z.btab = take(tc_bwd_tables_bytes(g));

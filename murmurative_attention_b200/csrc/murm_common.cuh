@@ -19,6 +19,7 @@ constexpr int kTopK = MURM_TOP_K;  // reference.py:38 hard-codes k = 7
 constexpr int kMaxSlots = 256;     // indices are stored as one byte per pick
 constexpr float kEmaEps = 1e-8f;   // reference.py:106-107
 constexpr int kTile = 128;         // tokens per tile (one thread or TMEM lane each)
+constexpr int kBwdTile = 64;       // tokens per tile of the tensor-core backward token kernel
 constexpr int kSlotRows = 16;              // slot rows per block of the slot-side kernels
 constexpr int kSlotHalo = kSlotRows + 2;   // plus one diffusion halo row on each side: a warp each
 constexpr int kSlotBlocks = 256 / kSlotRows;  // covers the 256 padded slot rows of the operand images
@@ -85,6 +86,7 @@ struct Geom {
   // token chunks: chunk c covers tokens [c*chunk_tokens, min(N, (c+1)*chunk_tokens))
   int fwd_chunks, fwd_chunk_tokens;   // select/attend kernels (one tile per CTA)
   int red_chunks, red_chunk_tokens;   // reduction kernels (many tiles per CTA)
+  int bwd_chunks, bwd_chunk_tokens;   // tensor-core backward token kernel (64-token tiles)
 };
 
 // Round records kept from forward to backward and scratch areas. All fp32
@@ -109,7 +111,7 @@ struct BwdScratch {
   float* dW;     // [BH][M]    gradient w.r.t. the weight sum
   float* dKdir;  // [BH][M][D] direct (EMA-kept) part of dK
   float* dVdir;
-  float* dKpart; // [BH][red_chunks][M][D]
+  float* dKpart; // [BH][chunks][M][D] (red_chunks, or bwd_chunks on the tensor-core path)
   float* dVpart;
   float* coef;   // [BH][N][8] scale * dlogit per pick
   float* dq;     // [BH][N][D] running dL/dq over rounds

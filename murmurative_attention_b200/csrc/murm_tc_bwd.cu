@@ -42,7 +42,7 @@ constexpr int kIssuer = 32 * kMathWarps;    // the thread that issues the MMAs a
 constexpr uint32_t kTable = kSlotsPad * kD * 2;  // one [256][64] 16-bit table
 constexpr uint32_t OFF_K = 0, OFF_V = kTable, OFF_DS = 2 * kTable;
 constexpr uint32_t kTables = 3 * kTable;
-constexpr int kBTile = 64;                           // tokens per tile of the token kernel
+constexpr int kBTile = kBwdTile;                     // tokens per tile of the token kernel
 constexpr uint32_t kTileBytes = kBTile * 128;        // one [64][64] 16-bit swizzled TMA tile
 constexpr uint32_t kPBlock = kBTile * 128;           // P block: [64 tokens][64 slots], swizzled
 constexpr uint32_t kPBuf = 4 * kPBlock;              // P of one tile: 256 slots
@@ -242,17 +242,17 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
         v = tcb::ld4(dir_v + e);
       }
       if (has_part) {
-        for (int ch = 0; ch < g.red_chunks; ch += 8) {  // added in chunk order
+        for (int ch = 0; ch < g.bwd_chunks; ch += 8) {  // added in chunk order
           float4 a[8], c[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const size_t po = ((size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1)) * MD + (size_t)m * g.D + 4 * l;
+            const size_t po = ((size_t)bh * g.bwd_chunks + min(ch + u, g.bwd_chunks - 1)) * MD + (size_t)m * g.D + 4 * l;
             a[u] = tcb::ld4(bs.dKpart + po);
             c[u] = tcb::ld4(bs.dVpart + po);
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            if (ch + u < g.red_chunks) {
+            if (ch + u < g.bwd_chunks) {
               tcb::add4(k, a[u]);
               tcb::add4(v, c[u]);
             }
@@ -380,8 +380,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   constexpr int kBT = tcb::kBTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
-  const int t_beg = chunk * g.red_chunk_tokens;
-  const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
+  const int t_beg = chunk * g.bwd_chunk_tokens;
+  const int t_end = min(g.N, t_beg + g.bwd_chunk_tokens);
   const int ntiles = (t_end - t_beg + kBT - 1) / kBT;
   const bool has_slot_grad = r < g.R - 1;
   const bool first = (r == g.R - 1);
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     const uint32_t lb = (uint32_t)(32 * quad) << 16;
     const bool is_k = warp >= 4;
     float* dst_base = is_k ? bs.dKpart : bs.dVpart;
-    const size_t po = (size_t)bh * g.red_chunks + chunk;
+    const size_t po = (size_t)bh * g.bwd_chunks + chunk;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int m = 128 * hh + 32 * quad + lane;
@@ -807,7 +807,7 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
   const int slot_blocks = (g.M + kSlotRows - 1) / kSlotRows;
   MURM_LAUNCH_PDL("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad);
   for (int r = g.R - 1; r >= 0; --r) {
-    MURM_LAUNCH_PDL("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.red_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
+    MURM_LAUNCH_PDL("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.bwd_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
                 qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,
                 static_cast<T*>(p.gq), p.gqs, sv, bs, tables, dWpad);
     MURM_LAUNCH_PDL("bwd_slots", k_bwd_slots<T>, dim3(g.BH, slot_blocks), tcb::kRowLanes * kSlotHalo, 0, st, g, r, r < g.R - 1 ? 1 : 0, 1,
