@@ -8,9 +8,10 @@
 //      never leave the SM.
 //   2. top-7 per token, exact, ties to the lowest slot (two threads per token
 //      row, 128 slot columns each): the 7th largest of 32 group maxima (groups
-//      of 8 slots at stride 16) bounds the 7th score from below, the few scores
-//      above the bound are compacted to shared memory and ranked exactly; rows
-//      where the bound is not finite take an exact full scan.
+//      of 8 slots at stride 16) bounds the 7th score from below; each thread
+//      ranks its few scores above the bound into a 7-entry list (bit masks and
+//      select-tree reads of registers), and the two lists are merged through
+//      shared memory; rows where the bound is not finite take an exact scan.
 //   3. softmax over the 7 picks (reference.py:61-63) in fp32.
 //   4. the picks' weights w are written into a zeroed 128 x 256 tile P in shared
 //      memory as two 16-bit terms, first w_hi = rn(w) and then w_lo = rn(w - w_hi):
@@ -18,14 +19,14 @@
 //      accumulates the slot update sums S += P^T . Q and W += P^T . 1
 //      (reference.py:93-103) over both terms in TMEM across all tiles of the
 //      chunk — fp32-level sums, deterministic, no atomics.
-// The chunk's S/W partials go to global memory; k_update_finalize (murm_simt.cu)
-// combines chunks in index order, applies the EMA and the diffusion.
+// The chunk's S/W partials go to global memory; k_tc_finalize combines chunks in
+// index order, applies the EMA and the diffusion.
 //
 // Shared memory (from a 1024-byte aligned base; operand tiles use the 128-byte
 // swizzle, rows of 64 16-bit elements):
-//   K terms (32K each) | V 32K | P 64K (4 slot blocks) | Q tiles (16K each) | ONES 1K | CAND | misc
-//   fp16: 2 key terms, 2 Q buffers (prefetch), 24 candidates per row
-//   bf16: 3 key terms, 1 Q buffer, 16 candidates per row
+//   K terms (32K each) | V 32K | P 64K (4 slot blocks) | Q tiles (16K each) | ONES 2K |
+//   XCH 14K (the threads' top-7 lists) | misc
+//   fp16: 2 key terms, 3 Q buffers; bf16: 3 key terms, 1 Q buffer
 #include <cstdlib>
 #include <cudaTypedefs.h>
 
