@@ -42,6 +42,7 @@ murm_status report_error(murm_status s, const char* msg) {
 namespace {
 
 constexpr int kSmCount = 148;  // B200; fixes the chunking so sizes() is device-independent
+static_assert(kSmCount == kMaxSplitCtas, "the forward split plans one CTA per SM");
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -95,6 +96,9 @@ Geom make_geom(const murm_shape* s) {
   bred = bred < 1 ? 1 : (bred > btiles ? btiles : bred);
   g.bwd_chunk_tokens = ((btiles + bred - 1) / bred) * kBwdTile;
   g.bwd_chunks = (g.N + g.bwd_chunk_tokens - 1) / g.bwd_chunk_tokens;
+  FwdSplit split;
+  plan_fwd_split(g.BH, g.N, kSmCount, &split);  // the same plan as the forward launch (kMaxSplitCtas)
+  g.ft_parts = max_fwd_parts(split);
   return g;
 }
 
@@ -120,8 +124,9 @@ Sizes make_sizes(const Geom& g) {
   z.sw = take(R * BH * N * 8 * 4);
   z.saved = o;
   o = 0;
-  z.fS = take(BH * g.red_chunks * M * D * 4);
-  z.fW = take(BH * g.red_chunks * M * 4);
+  const size_t fparts = (size_t)(g.ft_parts > g.red_chunks ? g.ft_parts : g.red_chunks);
+  z.fS = take(BH * fparts * M * D * 4);
+  z.fW = take(BH * fparts * M * 4);
   // operand images of the tensor-core path (16-bit dtypes, head_dim 64)
   z.fImg = take(tc_images_bytes(g));
   z.fwd_ws = o;

@@ -87,7 +87,76 @@ struct Geom {
   int fwd_chunks, fwd_chunk_tokens;   // select/attend kernels (one tile per CTA)
   int red_chunks, red_chunk_tokens;   // reduction kernels (many tiles per CTA)
   int bwd_chunks, bwd_chunk_tokens;   // tensor-core backward token kernel (64-token tiles)
+  int ft_parts;                       // tensor-core forward: slot-sum partials per (b,h) (FwdSplit)
 };
+
+// The tensor-core forward's split of the flat list of (b,h) x 128-token tiles ("units": unit u is
+// tile u % tpb of pair u / tpb) over at most one CTA per SM. CTA c takes units
+// [start[c], start[c+1]): a run that may finish one pair and start the next. A change of pair
+// costs a CTA a pipeline drain and refill and new operand images, about one tile, so the host
+// plan charges it as one: each CTA gets at most K tiles, or K - 1 when its run changes pair once,
+// with the smallest K whose plan fits in the SMs. Each pair gets one slot-sum partial per CTA
+// that covers some of its tiles, numbered from 0 in token order.
+constexpr int kMaxSplitCtas = 148;
+struct FwdSplit {
+  int G;    // CTAs
+  int tpb;  // tiles per (b,h)
+  int start[kMaxSplitCtas + 1];
+  __host__ __device__ int cta_of(int u) const {  // the CTA whose run holds unit u
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] <= u) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo;
+  }
+  __host__ __device__ int first_cta(int bh) const { return cta_of(bh * tpb); }
+  __host__ __device__ int parts(int bh) const { return cta_of(bh * tpb + tpb - 1) - first_cta(bh) + 1; }
+};
+// Host: the plan for BH pairs of N tokens over at most `sms` CTAs (sms <= kMaxSplitCtas).
+inline void plan_fwd_split(int BH, int N, int sms, FwdSplit* s) {
+  const int tpb = (N + kTile - 1) / kTile;
+  const int U = BH * tpb;  // B*H*N*D < 2^31 is checked, so this fits
+  const int pen = 1;       // tiles charged for a change of pair
+  for (int K = (U + sms - 1) / sms;; ++K) {
+    int c = 0, u = 0;
+    while (u < U && c < sms) {
+      s->start[c++] = u;
+      int b = K;
+      const int rest = (u / tpb + 1) * tpb - u;  // tiles left in this pair
+      const int t = rest < b ? rest : b;
+      u += t;
+      b -= t;
+      if (b > pen && u < U) {  // at a pair boundary with budget left: whole pairs, then part of one
+        int k = b / (pen + tpb);
+        if (k > (U - u) / tpb) k = (U - u) / tpb;
+        u += k * tpb;
+        b -= k * (pen + tpb);
+        if (u < U && b > pen) u += b - pen;  // b - pen < tpb tiles of the next pair
+      }
+    }
+    if (u >= U) {
+      s->G = c;
+      s->tpb = tpb;
+      s->start[c] = U;
+      return;
+    }
+  }
+}
+// A bound on the partials of any pair under a plan: the CTAs whose runs start in the pair, plus
+// one whose run started in an earlier pair and reaches into it (counted over the G CTAs, not the
+// pairs, of which there may be many).
+inline int max_fwd_parts(const FwdSplit& s) {
+  int m = 1, bh_prev = -1, count = 0;
+  for (int c = 0; c < s.G; ++c) {
+    const int bh = s.start[c] / s.tpb;
+    count = (bh == bh_prev) ? count + 1 : 1;
+    bh_prev = bh;
+    m = count > m ? count : m;
+  }
+  return m + 1;
+}
 
 // Round records kept from forward to backward and scratch areas. All fp32
 // slot tensors are [BH][M][D] row-major; token tensors [BH][N][...].
@@ -100,8 +169,8 @@ struct Saved {
   float* w;      // [R][BH][N][8] softmax weights (7 used)
 };
 struct FwdScratch {
-  float* Spart;     // [BH][red_chunks][M][D]
-  float* Wpart;     // [BH][red_chunks][M]
+  float* Spart;     // [BH][parts][M][D] (parts: red_chunks, or ft_parts on the tensor-core path)
+  float* Wpart;     // [BH][parts][M]
   uint8_t* images;  // [BH][3][256][64] 16-bit operand images (tensor-core path)
 };
 struct BwdScratch {

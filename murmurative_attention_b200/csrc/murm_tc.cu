@@ -1,6 +1,9 @@
 // murm_tc.cu — tensor-core (tcgen05/TMEM/TMA) forward round for fp16/bf16, head_dim 64.
 //
-// One CTA owns one (batch, head) and a chunk of 128-token tiles. Per tile:
+// One CTA per SM; the (batch, head) x 128-token tile list is split over them by
+// FwdSplit (murm_common.cuh), so a CTA takes a run of tiles that may finish one
+// (batch, head) and start the next: one segment per (batch, head), each with its
+// own operand images and slot-sum partial. Per tile:
 //   1. select  (reference.py:19-38): S = Q . [K_1; ...; K_s]^T on tcgen05 into a
 //      128 x 256 fp32 TMEM tile. The fp32 slot keys are split into s 16-bit
 //      terms (K = K_1 + K_2 (+ K_3) + O(2^-22..2^-24 |K|): two fp16 terms, three
@@ -18,9 +21,9 @@
 //      tcgen05 computes the attend output O = P_hi . V (reference.py:65-66) and
 //      accumulates the slot update sums S += P^T . Q and W += P^T . 1
 //      (reference.py:93-103) over both terms in TMEM across all tiles of the
-//      chunk — fp32-level sums, deterministic, no atomics.
-// The chunk's S/W partials go to global memory; k_tc_finalize combines chunks in
-// index order, applies the EMA and the diffusion.
+//      segment — fp32-level sums, deterministic, no atomics.
+// A segment's S/W partials go to global memory; k_tc_finalize combines the partials
+// of a (batch, head) in token order, applies the EMA and the diffusion.
 //
 // Shared memory (from a 1024-byte aligned base; operand tiles use the 128-byte
 // swizzle, rows of 64 16-bit elements):
@@ -291,12 +294,13 @@ __device__ __forceinline__ float4 diffuse4(float4 x, float4 l, float4 r, float g
                      diffuse1(x.w, l.w, r.w, gamma));
 }
 
-// Finalize round r: combine the chunk partials in chunk order, EMA (reference.py:105-113)
+// Finalize round r: combine the segment partials in token order, EMA (reference.py:105-113)
 // and diffusion (reference.py:128-133) -> state entering round r+1, U_r, W_r and
 // the images of round r+1. grid (BH, 256/16): a block owns 16 slot rows and recomputes
 // one halo row on each side; 16 threads per row, every chunk load of a row in flight at once.
 template <typename T>
-__global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs) {
+__global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs,
+                                                                                      const __grid_constant__ FwdSplit split) {
   pdl_wait();  // the round's chunk partials
   pdl_trigger();
   __shared__ float4 kn[kSlotHalo][tc::kRowLanes];
@@ -314,18 +318,19 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
       v = tc::ld4(sv.V + e);
       float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
       float W = 0.f;
-      for (int ch = 0; ch < g.red_chunks; ch += 8) {  // eight loads in flight, added in chunk order
+      const int nparts = split.parts(bh);
+      for (int ch = 0; ch < nparts; ch += 8) {  // eight loads in flight, added in token order
         float4 a[8];
         float wv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const size_t po = (size_t)bh * g.red_chunks + min(ch + u, g.red_chunks - 1);
+          const size_t po = (size_t)bh * g.ft_parts + min(ch + u, nparts - 1);
           a[u] = tc::ld4(fs.Spart + (po * g.M + m) * tc::kD + 4 * l);
           wv[u] = fs.Wpart[po * g.M + m];
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          if (ch + u < g.red_chunks) {
+          if (ch + u < nparts) {
             S.x = __fadd_rn(S.x, a[u].x);
             S.y = __fadd_rn(S.y, a[u].y);
             S.z = __fadd_rn(S.z, a[u].z);
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
 template <typename T>
 __global__ void __launch_bounds__(tc::kThreads, 1)
     k_fwd_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
-             float* weights, Saved sv, FwdScratch fs, const uint8_t* images) {
+             float* weights, Saved sv, FwdScratch fs, const uint8_t* images, const __grid_constant__ FwdSplit split) {
   using C = tc::Cfg<T>;
   using L = tc::Layout<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -402,10 +407,22 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const int quadrant = warp & 3;
   // entry j of thread t's top-7 list at [j][t]: a warp touches consecutive words (no bank conflicts)
   uint64_t* xch = reinterpret_cast<uint64_t*>(sm + L::OFF_XCH);
-  const int bh = blockIdx.y, b = bh / g.H, h = bh - b * g.H, chunk = blockIdx.x;
-  const int t_beg = chunk * g.red_chunk_tokens;
-  const int t_end = min(g.N, t_beg + g.red_chunk_tokens);
-  const int ntiles = (t_end - t_beg + kTile - 1) / kTile;
+  // this CTA's run of the flat (b,h) x tile list, one segment per (b,h) it meets
+  const int cta = blockIdx.x;
+  const int u_end = split.start[cta + 1];
+  int bh = 0, b = 0, h = 0, part_idx = 0, t_beg = 0, t_end = 0, ntiles = 0;
+  auto set_segment = [&](int u) {  // the segment that starts at unit u
+    bh = u / split.tpb;
+    b = bh / g.H;
+    h = bh - b * g.H;
+    const int base = bh * split.tpb;
+    const int t0 = u - base, t1 = min(split.tpb, u_end - base);
+    t_beg = t0 * kTile;
+    t_end = min(g.N, t1 * kTile);
+    ntiles = t1 - t0;
+    part_idx = cta - split.first_cta(bh);
+  };
+  auto next_segment = [&]() -> int { return (bh + 1) * split.tpb; };
   constexpr uint32_t ID_SEL = idesc_f16(C::fmt, 128, 256, 0, 0);
   constexpr uint32_t ID_ATT = idesc_f16(C::fmt, 128, 64, 0, 1);
   // S += P^T.[Q | 1]: N = 80, the last 16 columns of B are ones, so they accumulate W
@@ -448,6 +465,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint32_t ph_s = 0, ph_a = 0, ph_b = 0;
   // the issuer's bookkeeping of asynchronous copies
   bool img_pending = false, q_pending[3] = {false, false, false};
+  uint32_t img_phase = 0;
   uint32_t q_phase[3] = {0, 0, 0};
 
   auto fail = [&](int code) {
@@ -518,21 +536,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   constexpr bool kEarlySelect = C::kQBufs >= 3;
   if (issuer_warp) {
     // ================= issuer warp =================
-    uint32_t n_s = 0, n_a = 0, n_b = 0;  // commits per barrier (for the wind-down)
-    if (lane == 0) {  // prologue: operand images, first token tiles, first SELECT
-      mbar_arrive_expect_tx(bar_img, L::kImages);
-      bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
-      img_pending = true;
-      for (int i = 0; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
-      if (!tc::timed_wait(bar_img, 0)) fail(tc::kErrImgWait);
-      else img_pending = false;
-      if (ntiles > 0 && !*s_abort && wait_q(0)) {
-        issue_select(0);
-        ++n_s;
-      }
-    }
-    __syncwarp();
-    uint32_t ph_b_own = 0;  // MMA_B phases this lane waits for itself (one Q buffer)
+    uint32_t n_s = 0, n_a = 0, n_b = 0;  // commits per barrier
+    // every committed group is complete (bounded waits): before a segment overwrites the
+    // operand images and Q buffers, and before TMEM is freed
+    auto drain = [&]() -> bool {
+      bool ok = true;
+      if (n_s) ok = tc::timed_wait(bar_s, (n_s - 1) & 1) && ok;
+      if (n_a) ok = tc::timed_wait(bar_a, (n_a - 1) & 1) && ok;
+      if (n_b) ok = tc::timed_wait(bar_b, (n_b - 1) & 1) && ok;
+      return ok;
+    };
     auto mma_b = [&](int tile_idx) {  // ---- MMA_B(tile_idx) ----
       tc::issuer_wait<tc::kBarPlo>();
       if (lane == 0 && !*s_abort) {
@@ -541,17 +554,43 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         mma_commit(bar_b);
         ++n_b;
         if (!kEarlySelect && tile_idx + 1 < ntiles) {  // one Q buffer: free once MMA_B is done
-          if (tc::timed_wait(bar_b, ph_b_own)) ph_b_own ^= 1; else fail(tc::kErrMmaWait);
-          tc_fence_after();
-          issue_q(tile_idx + 1);
-          if (wait_q(tile_idx + 1)) {
-            issue_select(tile_idx + 1);
-            ++n_s;
+          if (!tc::timed_wait(bar_b, (n_b - 1) & 1)) {
+            fail(tc::kErrMmaWait);
+          } else {
+            tc_fence_after();
+            issue_q(tile_idx + 1);
+            if (wait_q(tile_idx + 1)) {
+              issue_select(tile_idx + 1);
+              ++n_s;
+            }
           }
         }
       }
       __syncwarp();
     };
+    for (int u = split.start[cta]; u < u_end; u = next_segment()) {
+    set_segment(u);
+    if (lane == 0 && !*s_abort) {  // segment prologue: operand images, first token tiles, first SELECT
+      if (!drain()) {
+        fail(tc::kErrMmaWait);
+      } else {
+        mbar_arrive_expect_tx(bar_img, L::kImages);
+        bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
+        img_pending = true;
+        for (int i = 0; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
+        if (!tc::timed_wait(bar_img, img_phase)) {
+          fail(tc::kErrImgWait);
+        } else {
+          img_pending = false;
+          img_phase ^= 1;
+        }
+        if (ntiles > 0 && !*s_abort && wait_q(0)) {
+          issue_select(0);
+          ++n_s;
+        }
+      }
+    }
+    __syncwarp();
     for (int tile = 0; tile < ntiles; ++tile) {
       if (kEarlySelect) {
         if (tile > 0) mma_b(tile - 1);
@@ -582,11 +621,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       if (!kEarlySelect) mma_b(tile);
     }
     if (kEarlySelect && ntiles > 0) mma_b(ntiles - 1);
-    if (lane == 0) {  // every committed group completes before TMEM is freed (bounded waits)
-      if (n_s) tc::timed_wait(bar_s, (n_s - 1) & 1);
-      if (n_a) tc::timed_wait(bar_a, (n_a - 1) & 1);
-      if (n_b) tc::timed_wait(bar_b, (n_b - 1) & 1);
-    }
+    }  // segments
+    if (lane == 0) drain();
   } else {
     // ================= row warps =================
     // A tile's state kept for its completion (second weight term, records, output)
@@ -644,6 +680,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       tc_fence_before();  // the output's TMEM reads come before the next MMA_A
     };
 
+    for (int u = split.start[cta]; u < u_end; u = next_segment()) {
+    set_segment(u);
     for (int tile = 0; tile < ntiles; ++tile) {
       const int n0 = t_beg + tile * kTile;
       const int n = n0 + row;
@@ -889,9 +927,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     if (kEarlySelect && ntiles > 0) complete();
     if (ntiles > 0) wait_live(bar_b, ph_b);
 
-    // ---- chunk partials: TMEM lanes are slots here ----
+    // ---- the segment's partials: TMEM lanes are slots here ----
     if (!__any_sync(0xffffffffu, *s_abort != 0)) {
-      const size_t po = (size_t)bh * g.red_chunks + chunk;
+      const size_t po = (size_t)bh * g.ft_parts + part_idx;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int m = 128 * hh + row;
@@ -907,10 +945,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
       }
     }
+    }  // segments
   }
   // ---- wind down: wait (bounded) for copies still in flight, free TMEM ----
   if (issuer_warp && lane == 0) {
-    if (img_pending) tc::timed_wait(bar_img, 0);
+    if (img_pending) tc::timed_wait(bar_img, img_phase);
     for (int i = 0; i < 3; ++i)
       if (q_pending[i]) tc::timed_wait(&bar_q[i], q_phase[i]);
   }
@@ -995,11 +1034,14 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
   }
   MURM_LAUNCH_PDL("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
               static_cast<const T*>(p.sv), p.svs, sv, images);
+  FwdSplit split;  // the plan the workspace was sized for (make_geom)
+  plan_fwd_split(g.BH, g.N, kMaxSplitCtas, &split);
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(g.red_chunks, g.BH), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
-                qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images);
+    MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
+                qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images, split);
     if (r + 1 < g.R)
-      MURM_LAUNCH_PDL("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs);
+      MURM_LAUNCH_PDL("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs,
+                      split);
   }
   return cudaGetLastError();
 }
