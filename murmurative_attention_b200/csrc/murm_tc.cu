@@ -297,7 +297,7 @@ __device__ __forceinline__ float4 diffuse4(float4 x, float4 l, float4 r, float g
 // Finalize round r: combine the segment partials in token order, EMA (reference.py:105-113)
 // and diffusion (reference.py:128-133) -> state entering round r+1, U_r, W_r and
 // the images of round r+1. grid (BH, 256/16): a block owns 16 slot rows and recomputes
-// one halo row on each side; 16 threads per row, every chunk load of a row in flight at once.
+// one halo row on each side; 16 threads per row, up to 12 partial loads of a row in flight at once.
 template <typename T>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs,
                                                                                       const __grid_constant__ FwdSplit split) {
@@ -319,17 +319,18 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
       float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
       float W = 0.f;
       const int nparts = split.parts(bh);
-      for (int ch = 0; ch < nparts; ch += 8) {  // eight loads in flight, added in token order
-        float4 a[8];
-        float wv[8];
+      constexpr int kW = 12;  // loads in flight: one round for up to 12 partials (north-star: 10)
+      for (int ch = 0; ch < nparts; ch += kW) {  // added in token order
+        float4 a[kW];
+        float wv[kW];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kW; ++u) {
           const size_t po = (size_t)bh * g.ft_parts + min(ch + u, nparts - 1);
           a[u] = tc::ld4(fs.Spart + (po * g.M + m) * tc::kD + 4 * l);
           wv[u] = fs.Wpart[po * g.M + m];
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kW; ++u) {
           if (ch + u < nparts) {
             S.x = __fadd_rn(S.x, a[u].x);
             S.y = __fadd_rn(S.y, a[u].y);
