@@ -96,9 +96,9 @@ Geom make_geom(const murm_shape* s) {
   bred = bred < 1 ? 1 : (bred > btiles ? btiles : bred);
   g.bwd_chunk_tokens = ((btiles + bred - 1) / bred) * kBwdTile;
   g.bwd_chunks = (g.N + g.bwd_chunk_tokens - 1) / g.bwd_chunk_tokens;
-  FwdSplit split;
-  plan_fwd_split(g.BH, g.N, kSmCount, &split);  // the same plan as the forward launch (kMaxSplitCtas)
-  g.ft_parts = max_fwd_parts(split);
+  TileSplit split;  // the plan of the forward launch (kMaxSplitCtas CTAs)
+  plan_split(g.BH, g.N, kTile, kSmCount, &split);
+  g.ft_parts = max_parts(split);
   return g;
 }
 

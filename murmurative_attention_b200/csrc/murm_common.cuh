@@ -87,10 +87,10 @@ struct Geom {
   int fwd_chunks, fwd_chunk_tokens;   // select/attend kernels (one tile per CTA)
   int red_chunks, red_chunk_tokens;   // reduction kernels (many tiles per CTA)
   int bwd_chunks, bwd_chunk_tokens;   // tensor-core backward token kernel (64-token tiles)
-  int ft_parts;                       // tensor-core forward: slot-sum partials per (b,h) (FwdSplit)
+  int ft_parts;                       // tensor-core forward: slot-sum partials per (b,h) (TileSplit)
 };
 
-// The tensor-core forward's split of the flat list of (b,h) x 128-token tiles ("units": unit u is
+// The tensor-core forward's split of the flat list of (b,h) x token tiles ("units": unit u is
 // tile u % tpb of pair u / tpb) over at most one CTA per SM. CTA c takes units
 // [start[c], start[c+1]): a run that may finish one pair and start the next. A change of pair
 // costs a CTA a pipeline drain and refill and new operand images, about one tile, so the host
@@ -98,7 +98,7 @@ struct Geom {
 // with the smallest K whose plan fits in the SMs. Each pair gets one slot-sum partial per CTA
 // that covers some of its tiles, numbered from 0 in token order.
 constexpr int kMaxSplitCtas = 148;
-struct FwdSplit {
+struct TileSplit {
   int G;    // CTAs
   int tpb;  // tiles per (b,h)
   int start[kMaxSplitCtas + 1];
@@ -114,9 +114,10 @@ struct FwdSplit {
   __host__ __device__ int first_cta(int bh) const { return cta_of(bh * tpb); }
   __host__ __device__ int parts(int bh) const { return cta_of(bh * tpb + tpb - 1) - first_cta(bh) + 1; }
 };
-// Host: the plan for BH pairs of N tokens over at most `sms` CTAs (sms <= kMaxSplitCtas).
-inline void plan_fwd_split(int BH, int N, int sms, FwdSplit* s) {
-  const int tpb = (N + kTile - 1) / kTile;
+// Host: the plan for BH pairs of N tokens in tiles of `tile` tokens over at most `sms` CTAs
+// (sms <= kMaxSplitCtas).
+inline void plan_split(int BH, int N, int tile, int sms, TileSplit* s) {
+  const int tpb = (N + tile - 1) / tile;
   const int U = BH * tpb;  // B*H*N*D < 2^31 is checked, so this fits
   const int pen = 1;       // tiles charged for a change of pair
   for (int K = (U + sms - 1) / sms;; ++K) {
@@ -147,7 +148,7 @@ inline void plan_fwd_split(int BH, int N, int sms, FwdSplit* s) {
 // A bound on the partials of any pair under a plan: the CTAs whose runs start in the pair, plus
 // one whose run started in an earlier pair and reaches into it (counted over the G CTAs, not the
 // pairs, of which there may be many).
-inline int max_fwd_parts(const FwdSplit& s) {
+inline int max_parts(const TileSplit& s) {
   int m = 1, bh_prev = -1, count = 0;
   for (int c = 0; c < s.G; ++c) {
     const int bh = s.start[c] / s.tpb;

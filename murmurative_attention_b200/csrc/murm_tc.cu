@@ -1,7 +1,7 @@
 // murm_tc.cu — tensor-core (tcgen05/TMEM/TMA) forward round for fp16/bf16, head_dim 64.
 //
 // One CTA per SM; the (batch, head) x 128-token tile list is split over them by
-// FwdSplit (murm_common.cuh), so a CTA takes a run of tiles that may finish one
+// TileSplit (murm_common.cuh), so a CTA takes a run of tiles that may finish one
 // (batch, head) and start the next: one segment per (batch, head), each with its
 // own operand images and slot-sum partial. Per tile:
 //   1. select  (reference.py:19-38): S = Q . [K_1; ...; K_s]^T on tcgen05 into a
@@ -300,7 +300,7 @@ __device__ __forceinline__ float4 diffuse4(float4 x, float4 l, float4 r, float g
 // one halo row on each side; 16 threads per row, up to 12 partial loads of a row in flight at once.
 template <typename T>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Geom g, int r, Saved sv, FwdScratch fs,
-                                                                                      const __grid_constant__ FwdSplit split) {
+                                                                                      const __grid_constant__ TileSplit split) {
   pdl_wait();  // the round's chunk partials
   pdl_trigger();
   __shared__ float4 kn[kSlotHalo][tc::kRowLanes];
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
 template <typename T>
 __global__ void __launch_bounds__(tc::kThreads, 1)
     k_fwd_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
-             float* weights, Saved sv, FwdScratch fs, const uint8_t* images, const __grid_constant__ FwdSplit split) {
+             float* weights, Saved sv, FwdScratch fs, const uint8_t* images, const __grid_constant__ TileSplit split) {
   using C = tc::Cfg<T>;
   using L = tc::Layout<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -1035,8 +1035,8 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
   }
   MURM_LAUNCH_PDL("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
               static_cast<const T*>(p.sv), p.svs, sv, images);
-  FwdSplit split;  // the plan the workspace was sized for (make_geom)
-  plan_fwd_split(g.BH, g.N, kMaxSplitCtas, &split);
+  TileSplit split;  // the plan the workspace was sized for (make_geom)
+  plan_split(g.BH, g.N, kTile, kMaxSplitCtas, &split);
   for (int r = 0; r < g.R; ++r) {
     MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
                 qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images, split);
