@@ -36,6 +36,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import torch
@@ -86,24 +87,85 @@ def load_peaks():
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons while the timed steps run. NVML is read every 2 ms from a
+    thread (reads only: the timed region is tens of milliseconds, shorter than nvidia-smi's
+    sampling period); without NVML, nvidia-smi every 100 ms. Any failure only drops the record."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device_index):
         self.proc = None
+        self.thread = None
         self.dev = device_index
+        self.samples = []  # (sm MHz, reason names)
+        self.max_mhz = None
+        self.halt = threading.Event()
+
+    def _uuid(self):
+        return "GPU-" + str(torch.cuda.get_device_properties(self.dev).uuid)
+
+    def _start_nvml(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(self._uuid())
+        except Exception:  # older bindings take bytes
+            h = pynvml.nvmlDeviceGetHandleByUUID(self._uuid().encode())
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        bits = ((pynvml.nvmlClocksEventReasonHwSlowdown, "hw_slowdown"),
+                (pynvml.nvmlClocksEventReasonHwThermalSlowdown, "hw_thermal_slowdown"),
+                (pynvml.nvmlClocksEventReasonSwThermalSlowdown, "sw_thermal_slowdown"),
+                (pynvml.nvmlClocksEventReasonSwPowerCap, "sw_power_cap"))
+
+        def run():
+            try:
+                while not self.halt.is_set():
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, tuple(n for b, n in bits if mask & b)))
+                    time.sleep(0.002)
+            except Exception:
+                pass
+            finally:
+                try:
+                    pynvml.nvmlShutdown()
+                except Exception:
+                    pass
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
 
     def start(self):
         try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.dev).uuid)
+            self._start_nvml()
+            return
+        except Exception:
+            self.thread = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "-i", self._uuid(), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
 
     def stop(self):
+        try:
+            return self._stop()
+        except Exception:
+            return None
+
+    def _stop(self):
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            sm = [x for x, _ in self.samples]
+            reasons = sorted({n for _, ns in self.samples for n in ns})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "samples": len(sm),
+                    "reasons": reasons, "source": "nvml, every 2 ms"}
         if self.proc is None:
             return None
         time.sleep(0.15)
@@ -114,7 +176,6 @@ class ClockSampler:
             self.proc.kill()
             out, _ = self.proc.communicate()
         sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in out.strip().splitlines():
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 7:
@@ -124,13 +185,13 @@ class ClockSampler:
                 mx.append(float(parts[1]))
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[3:7]):
+            for nm, v in zip(self.NAMES, parts[3:7]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "source": "nvidia-smi, every 100 ms"}
 
 
 # ---------------------------------------------------------------------------
