@@ -3,7 +3,9 @@
 Run in a container where the reference (beaglabs/murmurative-attention) is
 checked out; it is not needed anywhere else:
 
-    python tests/golden/make_golden.py [/path/to/reference/src]
+    python tests/golden/make_golden.py /path/to/reference/src
+
+(or with the path in MURM_REFERENCE_SRC).
 
 It imports the reference's own ``murmurative.reference`` module and composes
 its four functions (slot_select_reference, slot_attend_reference,
@@ -221,4 +223,7 @@ def make_surface(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MURM_REFERENCE_SRC")
+    if not src:
+        sys.exit("usage: make_golden.py /path/to/reference/src  (or set MURM_REFERENCE_SRC)")
+    main(src)
