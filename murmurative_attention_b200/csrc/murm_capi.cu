@@ -81,9 +81,7 @@ Geom make_geom(const murm_shape* s) {
   g.gamma = (float)s->gamma;
   g.scale = (float)(s->scale > 0 ? s->scale : 1.0 / std::sqrt((double)s->head_dim));
   const int tiles = (g.N + kTile - 1) / kTile;
-  g.fwd_chunks = tiles;
-  g.fwd_chunk_tokens = kTile;
-  // one wave: at most one chunk per SM (the tensor-core kernel holds a whole SM)
+  // CUDA-core path's reduction kernels: one wave, at most one chunk per SM
   int red = kSmCount / g.BH;
   red = red < 1 ? 1 : (red > tiles ? tiles : red);
   const int tiles_per = (tiles + red - 1) / red;

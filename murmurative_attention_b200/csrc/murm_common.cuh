@@ -84,8 +84,7 @@ struct Geom {
   int BH;
   float alpha, one_minus_alpha, gamma, scale;
   // token chunks: chunk c covers tokens [c*chunk_tokens, min(N, (c+1)*chunk_tokens))
-  int fwd_chunks, fwd_chunk_tokens;   // select/attend kernels (one tile per CTA)
-  int red_chunks, red_chunk_tokens;   // reduction kernels (many tiles per CTA)
+  int red_chunks, red_chunk_tokens;   // CUDA-core path's reduction kernels (many tiles per CTA)
   int bwd_chunks, bwd_chunk_tokens;   // tensor-core backward token kernel (64-token tiles)
   int ft_parts;                       // tensor-core forward: slot-sum partials per (b,h) (TileSplit)
 };
