@@ -21,10 +21,16 @@ murm_slot_murmurate_host_step) with pinned host buffers: every step copies q,
 slots and grad_out to the device and copies out, indices, weights and the
 three gradients back, pipelined over groups of (batch, head) pairs so the
 copies overlap the kernels. ``e2e_autograd`` is the same through
-slot_murmurate + autograd backward on device tensors copied in and out. ``roofline`` covers the kernel with the largest device time,
-timed with CUDA events recorded on its own launch stream.
+slot_murmurate + autograd backward on device tensors copied in and out.
+``roofline`` covers the kernel with the largest device time, timed with CUDA
+events recorded on its own launch stream. Two more BASELINE configurations run
+at the same N: ``strong`` is configs[2] (bf16 causal, 128 (batch, head) pairs)
+as one global problem split over the ranks (strong scaling, outputs gathered
+and checked against one GPU's run), ``layer`` is configs[3], the data-parallel
+layer training step with its NCCL gradient all-reduce inside the timed region.
 ``--impl reference`` times the reference's CPU path (the oracle port, which
-runs the reference.py operations) on the host cores.
+runs the reference.py operations) on the host cores, whole steps of the
+workload.
 """
 from __future__ import annotations
 
@@ -87,9 +93,11 @@ def load_peaks():
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """SM clock and clock-event reasons while the timed steps run. NVML is read every 2 ms from a
-    thread (reads only: the timed region is tens of milliseconds, shorter than nvidia-smi's
-    sampling period); without NVML, nvidia-smi every 100 ms. Any failure only drops the record."""
+    """SM clock and clock-event reasons while the timed steps run. NVML is read every 0.5 ms from a
+    thread (reads only: the timed region is a few milliseconds, far shorter than nvidia-smi's
+    sampling period); the interpreter's thread switch interval is cut to 0.1 ms meanwhile, so the
+    sampler is not held off by the timing loop for the default 5 ms. Without NVML, nvidia-smi every
+    100 ms. Any failure only drops the record."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -102,6 +110,7 @@ class ClockSampler:
         self.samples = []  # (sm MHz, reason names)
         self.max_mhz = None
         self.halt = threading.Event()
+        self.switch = None
 
     def _uuid(self):
         return "GPU-" + str(torch.cuda.get_device_properties(self.dev).uuid)
@@ -125,7 +134,7 @@ class ClockSampler:
                     sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
                     mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
                     self.samples.append((sm, tuple(n for b, n in bits if mask & b)))
-                    time.sleep(0.002)
+                    time.sleep(0.0005)
             except Exception:
                 pass
             finally:
@@ -138,6 +147,8 @@ class ClockSampler:
         self.thread.start()
 
     def start(self):
+        self.switch = sys.getswitchinterval()
+        sys.setswitchinterval(1e-4)
         try:
             self._start_nvml()
             return
@@ -151,6 +162,8 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.switch is not None:
+            sys.setswitchinterval(self.switch)
         try:
             return self._stop()
         except Exception:
@@ -165,7 +178,7 @@ class ClockSampler:
             sm = [x for x, _ in self.samples]
             reasons = sorted({n for _, ns in self.samples for n in ns})
             return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "samples": len(sm),
-                    "reasons": reasons, "source": "nvml, every 2 ms"}
+                    "reasons": reasons, "source": "nvml, every 0.5 ms"}
         if self.proc is None:
             return None
         time.sleep(0.15)
@@ -200,12 +213,12 @@ class ClockSampler:
 class AbiStep:
     """One fwd+bwd step through the C ABI with preallocated device buffers."""
 
-    def __init__(self, q, sk, sv, go):
+    def __init__(self, q, sk, sv, go, rounds=WL["R"], causal=WL["causal"]):
         from murmurative_attention_b200 import _lib, ops
         self._lib = _lib
         self.lib = _lib.load_library()
         B, H, N, D = q.shape
-        self.shape = ops._make_shape(q, sk.shape[2], WL["R"], 7, WL["causal"], 0.9, 0.15, None)
+        self.shape = ops._make_shape(q, sk.shape[2], rounds, 7, causal, 0.9, 0.15, None)
         saved_b, fws_b, bws_b = ops.slot_murmurate_sizes(self.shape)
         dev = q.device
         self.keep = dict(q=q, sk=sk, sv=sv, go=go)
@@ -241,6 +254,26 @@ def make_inputs(device, seed):
     sv = torch.zeros(B, H, M, D, device=device, dtype=DTYPE)
     go = torch.randn(B, H, N, D, generator=g, device=device).to(DTYPE)
     return q, sk, sv, go
+
+
+def graph_of(step):
+    """The step replayed from a CUDA graph (no host launch overhead in the timed region), or the
+    step itself when capture fails."""
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        g.replay()
+        torch.cuda.synchronize()
+        return g.replay, g
+    except Exception as e:  # noqa: BLE001
+        print(f"[bench] CUDA graph capture failed, timing eager launches: {e}", file=sys.stderr)
+        return step, None
 
 
 def time_steps(fn, steps, flush_buf):
@@ -302,25 +335,8 @@ def run_ours(args):
     launches_per_step = _lib.kernel_launches() - n0
 
     # replay the step from a CUDA graph (no host launch overhead in the timed region)
-    fn = step
-    graph_used = False
-    if not args.no_graph:
-        try:
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                step()
-            torch.cuda.current_stream().wait_stream(s)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                step()
-            g.replay()
-            torch.cuda.synchronize()
-            fn = g.replay
-            graph_used = True
-        except Exception as e:  # noqa: BLE001
-            print(f"[bench] CUDA graph capture failed, timing eager launches: {e}", file=sys.stderr)
-            fn = step
+    fn, graph = (step, None) if args.no_graph else graph_of(step)
+    graph_used = graph is not None
     for _ in range(args.warmup):
         fn()
     barrier(world)
@@ -348,6 +364,10 @@ def run_ours(args):
     e2e = run_e2e_host(q, sk, sv, go, min(args.steps, 20), args.warmup, flush, world)
     e2e_autograd = run_e2e(q, sk, sv, go, min(args.steps, 20), args.warmup, flush, slot_murmurate, world)
 
+    # the other BASELINE configurations at this N (every rank takes the same collective steps)
+    strong = None if args.skip_strong else strong_leg(args, world, rank, dev, flush)
+    layer = None if args.skip_layer else layer_leg(args, world, rank, dev, flush)
+
     if rank != 0:
         if world > 1:
             import torch.distributed as dist
@@ -369,6 +389,7 @@ def run_ours(args):
             "config": workload_config({"parallelism": f"(batch,head)-sharded weak scaling, {world} rank(s)",
                                        "timing": "CUDA graph replay" if graph_used else "eager launches"}),
             "roofline": roof, "step_roofline": step_roof, "e2e": e2e, "e2e_autograd": e2e_autograd,
+            "strong": strong, "layer": layer,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk,
             "kernels": {k: {"launches_per_step": v[0] / prof_steps, "ms_per_step": round(v[1] / prof_steps, 5)}
@@ -381,16 +402,132 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+CONFIG3 = dict(B=8, H=16, N=4096, D=64, M=256, R=3, causal=True)
+
+
+def strong_leg(args, world, rank, dev, flush):
+    """BASELINE configs[2] as ONE global problem split over the ranks by (batch, head) pair (strong
+    scaling): bf16 causal, q ~ N(0,1) [8,16,4096,64], slots_k ~ N(0,1)/8, slots_v ~ N(0,0.02),
+    grad_out ~ N(0,1), R=3, fwd+bwd. Every rank draws the same global inputs, runs its contiguous
+    share of the 128 pairs (distributed.local_pairs; pairs are independent, so no collective is
+    on the data path) and the step time is the slowest rank's. After timing, the indices and
+    outputs are gathered (distributed.gather_pairs, NCCL all-gather) and rank 0 compares them with
+    the whole problem run on its own GPU."""
+    from murmurative_attention_b200.distributed import gather_pairs, local_pairs
+    C = CONFIG3
+    g = torch.Generator(device=dev).manual_seed(6000)
+    tok = (C["B"], C["H"], C["N"], C["D"])
+    slot = (C["B"], C["H"], C["M"], C["D"])
+    q = torch.randn(*tok, generator=g, device=dev).to(torch.bfloat16)
+    sk = (torch.randn(*slot, generator=g, device=dev) / 8).to(torch.bfloat16)
+    sv = (torch.randn(*slot, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    go = torch.randn(*tok, generator=g, device=dev).to(torch.bfloat16)
+    loc = [local_pairs(t, world, rank).contiguous() for t in (q, sk, sv, go)]
+    step = AbiStep(*loc, rounds=C["R"], causal=C["causal"])
+    for _ in range(args.warmup):
+        step()
+    fn, graph = graph_of(step)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(fn, args.steps, flush)
+    barrier(world)
+    ms = max_over_ranks(sum(times), world) / args.steps
+    step()  # the outputs of one plain step, for the check
+    torch.cuda.synchronize()
+    check = {"ranks": world}
+    if world > 1:
+        idx_all = gather_pairs(step.idx, C["B"], C["H"])
+        out_all = gather_pairs(step.out, C["B"], C["H"])
+        if rank == 0:
+            whole = AbiStep(q, sk, sv, go, rounds=C["R"], causal=C["causal"])
+            whole()
+            torch.cuda.synchronize()
+            same = (idx_all == whole.idx).all(-1)
+            diff = (out_all.float() - whole.out.float()).abs()[same]
+            check.update({"rows_with_equal_indices": round(float(same.float().mean()), 6),
+                          "max_abs_out_diff_on_equal_rows": float(diff.max()) if diff.numel() else None,
+                          "against": "the whole 128-pair problem run on rank 0's GPU alone"})
+            del whole
+    else:
+        check["against"] = "one rank: the run is the whole problem"
+    tokens = C["B"] * C["N"]
+    return {"workload": "BASELINE configs[2]: bf16 causal [8,16,4096,64], sk~N(0,1)/8, sv~N(0,0.02), R=3, "
+                        "fwd+bwd, 128 (batch,head) pairs split contiguously over the ranks",
+            "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 5),
+            "scaling": "strong", "pairs_per_rank": int(loc[0].shape[1]),
+            "timing": "CUDA graph replay" if graph is not None else "eager launches", "check": check}
+
+
+def layer_leg(args, world, rank, dev, flush):
+    """the MurmurativeAttention layer training step, bf16, data parallel:
+    every rank trains on its own 2 sequences of 8192 tokens (16 sequences at 8 GPUs) and the
+    parameter gradients are averaged over NCCL while the backward runs (one all-reduce per
+    parameter, started by autograd hooks: q_proj and o_proj weights 2 MiB each, slot embeddings
+    0.5 MiB, bf16). One step = forward, mean-square loss, backward, gradient average, SGD update.
+    The collective's cost is also timed alone (the same three all-reduces back to back)."""
+    from murmurative_attention_b200 import MurmurativeAttention
+    from murmurative_attention_b200.training import GradientAverager, dp_train_step
+    L = LAYER
+    torch.manual_seed(0)  # the same initial parameters on every rank
+    layer = MurmurativeAttention(L["dim"], L["heads"], L["slots"], rounds=L["R"]).to(dev, torch.bfloat16)
+    with torch.no_grad():
+        layer.q_proj.weight.normal_(0.0, L["dim"] ** -0.5)
+        layer.o_proj.weight.normal_(0.0, L["dim"] ** -0.5)
+        layer.slot_embeddings.normal_(0.0, 1.0)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x = torch.randn(L["B"], L["N"], L["dim"], device=dev, dtype=torch.bfloat16, generator=g)
+    opt = torch.optim.SGD(layer.parameters(), lr=1e-3)
+    avg = GradientAverager(layer.parameters())
+    for _ in range(args.warmup):
+        dp_train_step(layer, x, opt, avg)
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(lambda: dp_train_step(layer, x, opt, avg), args.steps, flush)
+    barrier(world)
+    ms = max_over_ranks(sum(times), world) / args.steps
+    avg.remove()
+    grads = [p.grad for p in layer.parameters() if p.grad is not None]
+    coll = {"collective": "none (one rank)"}
+    if world > 1:
+        import torch.distributed as dist
+
+        def reduce_all():
+            for t in grads:
+                dist.all_reduce(t)
+        for _ in range(3):
+            reduce_all()
+        torch.cuda.synchronize()
+        barrier(world)
+        ar = time_steps(reduce_all, args.steps, flush)
+        ar_ms = max_over_ranks(sum(ar), world) / args.steps
+        nbytes = sum(t.numel() * t.element_size() for t in grads)
+        coll = {"collective": f"NCCL all_reduce (sum) of the {len(grads)} parameter gradients, "
+                              f"{nbytes / 2**20:.2f} MiB bf16 per step, overlapped with the backward",
+                "allreduce_ms_alone": round(ar_ms, 5), "share_of_step_if_not_overlapped": round(ar_ms / ms, 4)}
+    tokens = world * L["B"] * L["N"]
+    return {"workload": "layer (BASELINE configs[3]): dim 1024, heads 16 (d=64), M=256, R=3, k=7, "
+                        "x~N(0,1) [2 per rank,8192,1024], q_proj/o_proj ~N(0,1/1024), slot_embeddings ~N(0,1); SGD",
+            "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 5),
+            "scaling": "weak", "global_batch": world * L["B"], "seq_len": L["N"], "parallelism": f"dp{world}",
+            **coll}
+
+
 def roofline(prof, prof_steps, peaks):
     if not prof:
         return None
     name, (launches, total) = max(prof.items(), key=lambda kv: kv[1][1])
     avg_ms = total / launches
+    # DRAM bytes per launch cannot be read without a profiler: they come from the committed
+    # ncu capture of the same kernel (static, labelled as such), not from this run
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic_northstar.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get(name)
+    traffic_source = ("static: dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu capture "
+                      "recorded in profiles/traffic_northstar.json, not measured in this run")
     if name.startswith("select"):
         flops = select_flops_per_round()  # one round per launch
         achieved = flops / (avg_ms / 1e3) / 1e12
@@ -398,15 +535,12 @@ def roofline(prof, prof_steps, peaks):
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                 "peak_source": f"{peaks['source']} (burst dense bf16)",
                 "work_per_launch": f"select GEMM 2*M*d*tokens = {flops:.4g} FLOP",
-                "avg_launch_ms": round(avg_ms, 5), "launches": launches,
-                "limiter": "neither bound is reached: the CUDA-core top-7 selection between the MMAs limits it "
-                           "(ncu: ALU pipe ~50% of active cycles, issue ~37%, tensor pipe ~17%; "
-                           "profiles/k_fwd_tc_northstar.md)"}
+                "avg_launch_ms": round(avg_ms, 5), "launches": launches, "traffic_source": traffic_source}
     # memory-bound kernels: algorithmic bytes of the whole step spread over its launches
     per_launch = algorithmic_bytes() / (launches / prof_steps)
     achieved = per_launch / (avg_ms / 1e3) / 1e9
     return {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic, "traffic_source": traffic_source,
             "peak_source": f"{peaks['source']} copy bandwidth", "avg_launch_ms": round(avg_ms, 5),
             "launches": launches}
 
@@ -490,10 +624,14 @@ def cpu_sample_step(heads, seed=0):
     return step
 
 
-def cpu_baseline(seconds=12.0, heads=2):
+def cpu_baseline(seconds=12.0):
+    """The reference's CPU path (reference.py operations through the oracle port, torch.topk as
+    the reference calls it) on the whole workload — all (batch, head) pairs — per step, on every
+    host core: one warm-up step, then whole steps until ``seconds`` have passed (at least 2). The
+    same computation as ``--impl reference``, so the two legs report one number."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    step = cpu_sample_step(heads)
+    step = cpu_sample_step(WL["B"] * WL["H"])
     step()  # warm-up
     t0 = time.perf_counter()
     n = 0
@@ -503,10 +641,10 @@ def cpu_baseline(seconds=12.0, heads=2):
         if time.perf_counter() - t0 >= seconds and n >= 2:
             break
     dt = (time.perf_counter() - t0) / n
-    full = dt * (WL["B"] * WL["H"]) / heads  # (b,h) pairs are independent: time scales with their count
-    return {"value": round(WL["B"] * WL["N"] / full, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{heads} of {WL['B'] * WL['H']} (batch,head) pairs of the workload, fwd+bwd, fp32 CPU, "
-                      f"{n} timed steps of {dt * 1e3:.0f} ms, scaled by the pair count",
+    return {"value": round(WL["B"] * WL["N"] / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"the whole workload ({WL['B'] * WL['H']} of {WL['B'] * WL['H']} (batch,head) pairs) per "
+                      f"step, fwd+bwd, fp32 CPU (reference.py operations, torch.topk); {n} timed steps of "
+                      f"{dt * 1e3:.0f} ms after one warm-up step",
             "cpu": cpu_model()}
 
 
@@ -522,14 +660,18 @@ def cpu_model():
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle port of reference.py, with
+    torch.topk as the reference calls it) on all host cores, on the same workload as our arm:
+    every step is one forward + backward over all (batch, head) pairs. Under torchrun only rank 0
+    runs; the other ranks exit without work."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    heads = 1
-    step = cpu_sample_step(heads)
+    pairs = WL["B"] * WL["H"]
+    step = cpu_sample_step(pairs)
     for _ in range(args.warmup):
         step()
     times = []
@@ -538,12 +680,11 @@ def run_reference(args):
         step()
         times.append(time.perf_counter() - t0)
     dt = sum(times) / len(times)
-    full = dt * (WL["B"] * WL["H"]) / heads
-    value = round(WL["B"] * WL["N"] / full, 1)
-    sample = (f"{heads} of {WL['B'] * WL['H']} (batch,head) pairs per step, fwd+bwd, fp32 CPU (reference.py "
-              f"operations, torch.topk), scaled by the pair count")
+    value = round(WL["B"] * WL["N"] / dt, 1)
+    sample = (f"the whole workload ({pairs} of {pairs} (batch,head) pairs) per step, fwd+bwd, fp32 CPU "
+              f"(reference.py operations, torch.topk)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(full * 1e3, 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic", "config": workload_config({"parallelism": "host CPU, one process"}),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -556,49 +697,21 @@ LAYER = dict(B=2, N=8192, dim=1024, heads=16, slots=256, R=3)
 
 
 def run_layer(args):
-    """the MurmurativeAttention layer training step, bf16, data
-    parallel: every rank trains on its own 2 sequences of 8192 tokens (16 sequences at 8
-    GPUs) and the parameter gradients are averaged over NCCL while the backward runs.
-    One step = forward, mean-square loss, backward, gradient average, SGD update."""
+    """``--workload layer``: the layer training step alone (layer_leg) as the JSON line."""
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    from murmurative_attention_b200 import MurmurativeAttention
-    from murmurative_attention_b200.training import GradientAverager, dp_train_step
-
-    L = LAYER
-    torch.manual_seed(0)  # the same initial parameters on every rank
-    layer = MurmurativeAttention(L["dim"], L["heads"], L["slots"], rounds=L["R"]).to(dev, torch.bfloat16)
-    with torch.no_grad():
-        layer.q_proj.weight.normal_(0.0, L["dim"] ** -0.5)
-        layer.o_proj.weight.normal_(0.0, L["dim"] ** -0.5)
-        layer.slot_embeddings.normal_(0.0, 1.0)
-    g = torch.Generator(device=dev).manual_seed(2000 + rank)
-    x = torch.randn(L["B"], L["N"], L["dim"], device=dev, dtype=torch.bfloat16, generator=g)
-    opt = torch.optim.SGD(layer.parameters(), lr=1e-3)
-    avg = GradientAverager(layer.parameters())
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
-    for _ in range(args.warmup):
-        dp_train_step(layer, x, opt, avg)
-    torch.cuda.synchronize()
-    barrier(world)
-    times = time_steps(lambda: dp_train_step(layer, x, opt, avg), args.steps, flush)
-    barrier(world)
-    total_ms = max_over_ranks(sum(times), world)
-    tokens = world * L["B"] * L["N"] * args.steps
-    ms = total_ms / args.steps
+    res = layer_leg(args, world, rank, dev, flush)
     if rank == 0:
         line = {"metric": "MurmurativeAttention layer training step tokens/s (BASELINE configs[3])",
-                "value": round(tokens / (total_ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "layer: dim 1024, heads 16 (d=64), M=256, R=3, k=7, x~N(0,1) [2 per rank,8192,1024], "
-                                       "q_proj/o_proj ~N(0,1/1024), slot_embeddings ~N(0,1); SGD",
-                           "batch_per_rank": L["B"], "global_batch": world * L["B"], "seq_len": L["N"],
-                           "parallelism": f"dp{world}",
-                           "l2": "flushed by a 256 MiB write before every timed step"}}
+                "config": {"workload": res["workload"], "global_batch": res["global_batch"], "seq_len": res["seq_len"],
+                           "parallelism": res["parallelism"], "l2": "flushed by a 256 MiB write before every timed step"},
+                "collective": {k: v for k, v in res.items() if k.startswith(("collective", "allreduce", "share"))}}
         print(json.dumps(line), flush=True)
-    avg.remove()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -733,6 +846,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--skip-strong", action="store_true", help="omit the configs[2] strong-scaling leg")
+    ap.add_argument("--skip-layer", action="store_true", help="omit the configs[3] layer-step leg")
     ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode", "sp"), default="northstar",
                     help="layer: BASELINE configs[3], the data-parallel layer training step; "
                          "surface: the reference's 6-argument op through the per-phase kernels; "

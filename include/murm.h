@@ -125,21 +125,35 @@ MURM_API murm_status murm_slot_murmurate_fwd(const murm_fwd_args* args, void* st
  * autograd through ops.py:75-92 and 188-208. */
 MURM_API murm_status murm_slot_murmurate_bwd(const murm_bwd_args* args, void* stream);
 
+/* Forward from an fp32 slot state: identical to murm_slot_murmurate_fwd except
+ * that slots_k and slots_v are fp32 tables (strides in fp32 elements) whatever
+ * shape.dtype says for q, out and the arithmetic. The round loop keeps its slot
+ * state in fp32 between rounds (as the reference's fp32 update does,
+ * reference.py:86-115), so this call runs rounds r..R-1 of a longer loop from
+ * the state entering round r exactly as the full loop would: the state a
+ * reference run recorded (teacher-forced parity checks), or fp32 master slot
+ * tables kept by a caller whose tokens are 16-bit. No counterpart in the
+ * reference, whose op schemas take slots in the token dtype
+ * (torch_binding.cpp:7-10). Forward only; saved/workspace as for
+ * murm_slot_murmurate_fwd. */
+MURM_API murm_status murm_slot_murmurate_fwd_f32_slots(const murm_fwd_args* args, void* stream);
+
 /* Forward that needs no caller-provided scratch. No counterpart in the
  * reference. For callers that cannot allocate device memory: a serving plugin
  * that is handed only its input and output buffers under a memory budget fixed
- * at start-up, code running inside a global-mode CUDA stream capture (where
- * cudaMalloc is not permitted), or a foreign-language host with no binding to
- * the CUDA allocator. The round records and partial sums live in one
- * file-scope device array of MURM_NOSCRATCH_BYTES (64 MiB) that every GPU
- * loading this library holds until the process exits; this call allocates
- * nothing. `saved` and `workspace` in args must be NULL / 0; the caller still
- * passes q, slots and the outputs. A problem whose scratch exceeds the array
- * is rejected with MURM_ERR_WORKSPACE. The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture. All calls share the array: calls that overlap on
- * the GPU (different streams, or other host threads) race on it; serialise
- * them. Output only — there is no backward for this entry point. */
+ * at start-up, or a foreign-language host with no binding to the CUDA
+ * allocator. The round records and partial sums live in one file-scope device
+ * array of MURM_NOSCRATCH_BYTES (64 MiB) that every GPU loading this library
+ * holds until the process exits; this call allocates nothing. `saved` and
+ * `workspace` in args must be NULL / 0; the caller still passes q, slots and
+ * the outputs. A problem whose scratch exceeds the array is rejected with
+ * MURM_ERR_WORKSPACE. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and keeps it for the life of that device's
+ * primary context (after cudaDeviceReset the process must not call this entry
+ * again); make that first call before any stream capture. All calls share the
+ * array: calls that overlap on the GPU (different streams, or other host
+ * threads) race on it; serialise them. Output only — there is no backward for
+ * this entry point. */
 #define MURM_NOSCRATCH_BYTES (64u << 20)
 MURM_API murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* args, void* stream);
 
@@ -372,6 +386,17 @@ MURM_API murm_status murm_profile_end(murm_kernel_time* out, int32_t capacity, i
  * never completed) before they wind down cleanly. Returns MURM_ERR_DEVICE
  * when it was set. */
 MURM_API murm_status murm_device_status(void* stream);
+
+/* Failure-detection probe: launches one block that waits, bounded by limit_ns
+ * (at most 10 s), on an mbarrier of its own with the same bounded wait the
+ * tensor-core kernels use for their copies and MMAs. With `arrive` nonzero a
+ * thread arrives first and the wait completes; with 0 nothing arrives, the
+ * wait runs out, and the kernel sets the device error word (bit 16) and
+ * returns normally, so murm_device_status then reports MURM_ERR_DEVICE and the
+ * context stays usable. Lets a caller check its error handling without a
+ * fault. No counterpart in the reference (its launchers never check device
+ * errors, slot_select_attend.cu:474-490). */
+MURM_API murm_status murm_wait_probe(int32_t arrive, uint64_t limit_ns, void* stream);
 
 MURM_API const char* murm_status_string(murm_status status);
 MURM_API const char* murm_last_error_message(void);

@@ -207,10 +207,12 @@ EXPORTS = (
     "murm_slot_murmurate_fwd",
     "murm_slot_murmurate_bwd",
     "murm_slot_murmurate_fwd_noscratch",
+    "murm_slot_murmurate_fwd_f32_slots",
     "murm_status_string",
     "murm_last_error_message",
     "murm_abi_version",
     "murm_device_status",
+    "murm_wait_probe",
     "murm_kernel_launches",
     "murm_profile_begin",
     "murm_profile_end",
@@ -258,6 +260,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_slot_murmurate_bwd.restype = ctypes.c_int
         lib.murm_slot_murmurate_fwd_noscratch.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
         lib.murm_slot_murmurate_fwd_noscratch.restype = ctypes.c_int
+        lib.murm_slot_murmurate_fwd_f32_slots.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.murm_slot_murmurate_fwd_f32_slots.restype = ctypes.c_int
         lib.murm_status_string.argtypes = [ctypes.c_int]
         lib.murm_status_string.restype = ctypes.c_char_p
         lib.murm_last_error_message.argtypes = []
@@ -266,6 +270,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.murm_abi_version.restype = ctypes.c_int32
         lib.murm_device_status.argtypes = [ctypes.c_void_p]
         lib.murm_device_status.restype = ctypes.c_int
+        lib.murm_wait_probe.argtypes = [ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p]
+        lib.murm_wait_probe.restype = ctypes.c_int
         lib.murm_kernel_launches.argtypes = []
         lib.murm_kernel_launches.restype = ctypes.c_uint64
         lib.murm_profile_begin.argtypes = []

@@ -216,8 +216,15 @@ murm_status murm_device_status(void* stream) {
   if (e != cudaSuccess) return cuda_status(e, "murm_device_status");
   if (code)
     return fail(MURM_ERR_DEVICE, "a kernel gave up waiting (error bits 0x%x: 1 operand copy, 2 token tile copy, "
-                "4 tensor-core completion)", code);
+                "4 tensor-core completion, 8 backward copy or MMA, 16 wait probe)", code);
   return MURM_OK;
+}
+
+murm_status murm_wait_probe(int32_t arrive, uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(MURM_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 10 s], got %llu", (unsigned long long)limit_ns);
+  return cuda_status(launch_wait_probe(arrive ? 1 : 0, limit_ns, static_cast<cudaStream_t>(stream)),
+                     "wait probe launch");
 }
 
 murm_status murm_slot_murmurate_sizes(const murm_shape* shape, size_t* saved, size_t* fwd_ws, size_t* bwd_ws) {
@@ -229,7 +236,11 @@ murm_status murm_slot_murmurate_sizes(const murm_shape* shape, size_t* saved, si
   return MURM_OK;
 }
 
-murm_status murm_slot_murmurate_fwd(const murm_fwd_args* a, void* stream) {
+}  // extern "C"
+
+namespace murm {
+namespace {
+murm_status forward_entry(const murm_fwd_args* a, void* stream, int slots_f32) {
   if (!a) return fail(MURM_ERR_INVALID_ARGUMENT, "args is NULL");
   if (murm_status s = check_shape(&a->shape)) return s;
   const Geom g = make_geom(&a->shape);
@@ -252,12 +263,23 @@ murm_status murm_slot_murmurate_fwd(const murm_fwd_args* a, void* stream) {
   }
   p.indices = a->indices;
   p.weights = a->weights;
+  p.slots_f32 = slots_f32;
   const Saved sv = saved_views(z, a->saved);
   FwdScratch fs;
   fs.Spart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fS);
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fW);
   fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(a->workspace) + z.fImg);
   return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+}  // namespace murm
+
+extern "C" {
+
+murm_status murm_slot_murmurate_fwd(const murm_fwd_args* a, void* stream) { return forward_entry(a, stream, 0); }
+
+murm_status murm_slot_murmurate_fwd_f32_slots(const murm_fwd_args* a, void* stream) {
+  return forward_entry(a, stream, 1);
 }
 
 murm_status murm_slot_murmurate_bwd(const murm_bwd_args* a, void* stream) {
@@ -321,7 +343,7 @@ constexpr int kMaxDevices = 64;
 // The scratch of murm_slot_murmurate_fwd_noscratch: round records + partial
 // sums. In host code `g_noscratch` is only a host-side stand-in for the
 // symbol; kernels get the device address looked up below.
-__device__ __align__(256) unsigned char g_noscratch[kNoScratchBytes];
+static __device__ __align__(256) unsigned char g_noscratch[kNoScratchBytes];
 
 std::mutex g_noscratch_mu;
 void* g_noscratch_addr[kMaxDevices] = {};

@@ -25,6 +25,7 @@ struct FwdPtrs {
   void* out;      Strides3 os;
   int64_t* indices;
   float* weights;
+  int slots_f32 = 0;  // sk / sv are fp32 slot state (whatever the dtype of q and out)
 };
 
 struct BwdPtrs {
@@ -76,6 +77,15 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     ::murm::launch_end(stream);                                                      \
   } while (0)
 
+// Opts `kernel` into `bytes` of dynamic shared memory on the current device (murm_profile.cu).
+// The attribute belongs to one device's context, so it is tracked per (kernel, device) and only
+// raised when a launch needs more than was set before; safe to call from several host threads.
+cudaError_t smem_opt_in_raw(const void* kernel, int bytes);
+template <typename... A>
+inline cudaError_t smem_opt_in(void (*kernel)(A...), size_t bytes) {
+  return smem_opt_in_raw(reinterpret_cast<const void*>(kernel), static_cast<int>(bytes));
+}
+
 // Shared pieces of the round loop (murm_simt.cu).
 template <typename T>
 void launch_load_slots(const Geom& g, const FwdPtrs& p, const Saved& sv, cudaStream_t st);
@@ -94,6 +104,10 @@ template <typename T>
 cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdScratch& bs, cudaStream_t st);
 // Device error word written by bounded waits in tensor-core kernels.
 cudaError_t read_and_clear_device_error(int* code, cudaStream_t st);
+constexpr int kErrProbe = 16;  // the error bit of the wait probe (murm_tc.cu)
+// One block whose bounded wait on an mbarrier either completes (arrive != 0) or runs out after
+// limit_ns and sets kErrProbe (murm_tc.cu).
+cudaError_t launch_wait_probe(int arrive, uint64_t limit_ns, cudaStream_t st);
 
 // CUDA-core path (murm_simt.cu): every dtype, head_dim 16/32/64.
 template <typename T>

@@ -986,8 +986,8 @@ void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cuda
   int* offsets = reinterpret_cast<int*>(ws);
   int* entries = reinterpret_cast<int*>(ws + z.off_csr_entries);
   int* cnt = reinterpret_cast<int*>(ws + z.off_cnt);
-  cudaFuncSetAttribute(k_csr_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaFuncSetAttribute(k_csr_fill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  smem_opt_in(k_csr_count, smem);
+  smem_opt_in(k_csr_fill, smem);
   MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt);
   MURM_LAUNCH("phase_csr_scan", k_csr_scan, dim3(BH), 256, 0, st, ntiles, M, cnt, offsets);
   MURM_LAUNCH("phase_csr_fill", k_csr_fill, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt, offsets,
@@ -998,7 +998,7 @@ template <typename T>
 murm_status sa_fwd(const murm_select_attend_args& a, cudaStream_t st) {
   const int Mp = ((a.shape.slots + 31) / 32) * 32 + 1;
   const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
-  cudaFuncSetAttribute(k_sa_fwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  smem_opt_in(k_sa_fwd<T>, smem);
   const dim3 grid((a.shape.tokens + kWarps * kTokPerWarp - 1) / (kWarps * kTokPerWarp), a.shape.batch * a.shape.heads);
   const int64_t es = (int64_t)sizeof(T);
   int vec = (a.shape.head_dim * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.slot_keys) & 15) == 0;
@@ -1281,7 +1281,7 @@ MURM_API murm_status murm_decode_step(const murm_decode_args* a, void* stream) {
   for (int i = 0; i < 3; ++i) vec = vec && (a->sk_stride[i] * (int64_t)es) % 16 == 0 && (a->sv_stride[i] * (int64_t)es) % 16 == 0;
   const size_t smem_v = (size_t)a->slots * a->head_dim * es * 2 + (size_t)a->head_dim * 12 + (size_t)a->slots * 4 + 64;
   auto go = [&](auto kern, size_t bytes) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    smem_opt_in(kern, bytes);
     MURM_LAUNCH("decode_step", kern, dim3(a->batch * a->heads), 256, bytes, st, *a);
     return ph::launched("decode step");
   };

@@ -7,6 +7,7 @@
 // stream it runs on; results are aggregated by kernel name.
 #include <atomic>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -36,7 +37,21 @@ cudaEvent_t take_event() {
   cudaEventCreate(&e);
   return e;
 }
+std::mutex g_attr_mu;
+std::map<std::pair<const void*, int>, int> g_attr;  // (kernel, device) -> dynamic smem opted into
 }  // namespace
+
+cudaError_t smem_opt_in_raw(const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  int& have = g_attr[std::make_pair(kernel, dev)];
+  if (bytes <= have) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
 
 void launch_begin(const char* name, cudaStream_t st) {
   g_launches.fetch_add(1, std::memory_order_relaxed);

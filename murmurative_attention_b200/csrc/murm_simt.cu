@@ -597,16 +597,15 @@ static cudaError_t run_fwd_simt(const Geom& g, const FwdPtrs& p, const Saved& sv
   const int smem_sa = 2 * g.M * D * (int)sizeof(float);
   const int smem_up = (g.M * D + g.M + kTile * D + kTile * 8) * 4 + g.M * 16 + (kMaxSlots + 4 + 8) * 4 +
                       kTile * 8 + 2 * kTile * kTopK;
-  static int attr_smem = 0;  // dynamic-smem opt-in once per instantiation (largest size seen)
-  if (smem_sa > attr_smem || smem_up > attr_smem) {
-    cudaFuncSetAttribute(k_select_attend<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sa);
-    cudaFuncSetAttribute(k_update_partial<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
-    attr_smem = smem_sa > smem_up ? smem_sa : smem_up;
-  }
+  if (cudaError_t e = smem_opt_in(k_select_attend<T, D>, smem_sa)) return e;
+  if (cudaError_t e = smem_opt_in(k_update_partial<T, D>, smem_up)) return e;
   const T* q = static_cast<const T*>(p.q);
-  if (g.R > 0)  // with zero rounds the saved block is empty and nothing reads the slots
+  if (g.R > 0 && p.slots_f32)  // with zero rounds the saved block is empty and nothing reads the slots
+    MURM_LAUNCH("load_slots", k_load_slots<float>, dim3(g.BH, 4), 256, 0, st, g, static_cast<const float*>(p.sk),
+                p.sks, static_cast<const float*>(p.sv), p.svs, sv.K, sv.V);
+  else if (g.R > 0)
     MURM_LAUNCH("load_slots", k_load_slots<T>, dim3(g.BH, 4), 256, 0, st, g, static_cast<const T*>(p.sk), p.sks,
-                                                    static_cast<const T*>(p.sv), p.svs, sv.K, sv.V);
+                static_cast<const T*>(p.sv), p.svs, sv.K, sv.V);
   for (int r = 0; r < g.R; ++r) {
     MURM_LAUNCH("select_attend_simt", (k_select_attend<T, D>), dim3((g.N + kSimtTPB - 1) / kSimtTPB, g.BH), kSimtTPB,
                 smem_sa, st, 
@@ -631,12 +630,8 @@ static cudaError_t run_bwd_simt(const Geom& g, const BwdPtrs& p, const Saved& sv
   const int smem_tok = (3 * g.M * D + g.M) * (int)sizeof(float);
   const int smem_sc = (2 * g.M * D + 2 * kTile * D + 2 * kTile * 8) * 4 + g.M * 16 + (kMaxSlots + 4 + 8) * 4 +
                       kTile * 8 + 2 * kTile * kTopK;
-  static int attr_smem = 0;
-  if (smem_tok > attr_smem || smem_sc > attr_smem) {
-    cudaFuncSetAttribute(k_bwd_tokens<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_tok);
-    cudaFuncSetAttribute(k_bwd_scatter<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_sc);
-    attr_smem = smem_tok > smem_sc ? smem_tok : smem_sc;
-  }
+  if (cudaError_t e = smem_opt_in(k_bwd_tokens<T, D>, smem_tok)) return e;
+  if (cudaError_t e = smem_opt_in(k_bwd_scatter<T, D>, smem_sc)) return e;
   const T* q = static_cast<const T*>(p.q);
   const T* go = static_cast<const T*>(p.go);
   if (g.R == 0) {

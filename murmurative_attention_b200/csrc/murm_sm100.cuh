@@ -32,10 +32,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity: about one second on %globaltimer, read only
-// once the first poll has failed (the read costs ~0.1 us). Returns false on expiry (the caller
+// Plain arrival (count 1) on the barrier's current phase.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // one second
+// Bounded wait for the phase with the given parity: `limit_ns` (one second) on %globaltimer, read
+// only once the first poll has failed (the read costs ~0.1 us). Returns false on expiry (the caller
 // records an error and winds down).
-__device__ __forceinline__ bool mbar_timed_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_timed_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -45,7 +50,7 @@ __device__ __forceinline__ bool mbar_timed_wait(uint64_t* bar, uint32_t parity) 
       if (mbar_try_wait(bar, parity)) return true;
     uint64_t t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > 1000000000ull) return false;
+    if (t1 - t0 > limit_ns) return false;
   }
 }
 // Bounded wait: returns false when the phase did not complete within

@@ -258,10 +258,11 @@ __device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k
 }
 }  // namespace tc
 
-// Round-0 state: slot tables (dtype, strided; batch stride 0 broadcasts) -> fp32 state + images.
-// grid (BH, 256/16): block y covers 16 slot rows, 16 threads each (rows >= M write zero images).
-template <typename T>
-__global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const T* sk, Strides3 sks, const T* svv,
+// Round-0 state: slot tables (element type S: the dtype of q, or fp32 slot state; strided, batch
+// stride 0 broadcasts) -> fp32 state + images. grid (BH, 256/16): block y covers 16 slot rows,
+// 16 threads each (rows >= M write zero images).
+template <typename T, typename S>
+__global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const S* sk, Strides3 sks, const S* svv,
                                                                         Strides3 svs, Saved sv, uint8_t* images) {
   pdl_wait();  // the previous step's kernels may still read the state and images
   pdl_trigger();
@@ -270,10 +271,10 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, c
   const int m = blockIdx.y * kSlotRows + (threadIdx.x >> 4);
   float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
   if (m < g.M) {
-    const T* pk = row_ptr(sk, sks, b, h, m) + 4 * l;
-    const T* pv = row_ptr(svv, svs, b, h, m) + 4 * l;
-    k = make_float4(Elem<T>::load(pk), Elem<T>::load(pk + 1), Elem<T>::load(pk + 2), Elem<T>::load(pk + 3));
-    v = make_float4(Elem<T>::load(pv), Elem<T>::load(pv + 1), Elem<T>::load(pv + 2), Elem<T>::load(pv + 3));
+    const S* pk = row_ptr(sk, sks, b, h, m) + 4 * l;
+    const S* pv = row_ptr(svv, svs, b, h, m) + 4 * l;
+    k = make_float4(Elem<S>::load(pk), Elem<S>::load(pk + 1), Elem<S>::load(pk + 2), Elem<S>::load(pk + 3));
+    v = make_float4(Elem<S>::load(pv), Elem<S>::load(pv + 1), Elem<S>::load(pv + 2), Elem<S>::load(pv + 3));
     const size_t e = (size_t)bh * g.M * tc::kD + (size_t)m * tc::kD + 4 * l;
     tc::st4(sv.K + e, k);
     tc::st4(sv.V + e, v);
@@ -998,6 +999,28 @@ bool tc_forward_supported(const Geom& g, int dtype, const FwdPtrs& p) {
   return !(force && force[0] == '1');
 }
 
+// Failure-detection probe: one warp waits, bounded by `limit_ns`, on an mbarrier of its own. With
+// `arrive` set a thread arrives first and the wait ends at once; without it nothing arrives, the
+// wait runs out and the kernel records kErrProbe in the device error word, as the round kernels do
+// when a copy or an MMA never completes, then returns normally (no trap, no fault).
+__global__ void k_wait_probe(int arrive, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (arrive) mbar_arrive(&bar);
+    if (!mbar_timed_wait(&bar, 0, limit_ns)) atomicOr(&g_device_error, kErrProbe);
+  }
+}
+
+cudaError_t launch_wait_probe(int arrive, uint64_t limit_ns, cudaStream_t st) {
+  MURM_LAUNCH("wait_probe", k_wait_probe, 1, 32, 0, st, arrive, limit_ns);
+  return cudaGetLastError();
+}
+
 cudaError_t read_and_clear_device_error(int* code, cudaStream_t st) {
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return e;
@@ -1028,13 +1051,13 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Layout<T>::kSmem);
-    attr = true;
-  }
-  MURM_LAUNCH_PDL("tc_load", k_tc_load<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g, static_cast<const T*>(p.sk), p.sks,
-              static_cast<const T*>(p.sv), p.svs, sv, images);
+  if (cudaError_t e = smem_opt_in(k_fwd_tc<T>, tc::Layout<T>::kSmem)) return e;
+  if (p.slots_f32)
+    MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, float>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
+                    static_cast<const float*>(p.sk), p.sks, static_cast<const float*>(p.sv), p.svs, sv, images);
+  else
+    MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, T>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
+                    static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, sv, images);
   TileSplit split;  // the plan the workspace was sized for (make_geom)
   plan_split(g.BH, g.N, kTile, kMaxSplitCtas, &split);
   for (int r = 0; r < g.R; ++r) {

@@ -797,11 +797,7 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
   CUtensorMap qmap, gmap;
   if (!make_rows_map<T>(&qmap, g, p.q, p.qs) || !make_rows_map<T>(&gmap, g, p.go, p.gos))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_bwd_tokens_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcb::kSmem);
-    attr = true;
-  }
+  if (cudaError_t e = smem_opt_in(k_bwd_tokens_tc<T>, tcb::kSmem)) return e;
   uint8_t* tables = bs.tables;
   float* dWpad = reinterpret_cast<float*>(tables + (size_t)g.BH * tcb::kTables);
   const int slot_blocks = (g.M + kSlotRows - 1) / kSlotRows;

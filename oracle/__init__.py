@@ -18,6 +18,7 @@ from .murmurate import (  # noqa: F401
     slot_update,
     slot_diffusion,
     slot_murmurate,
+    slot_murmurate_forced,
     slot_murmurate_trace,
     slot_murmurate_backward_explicit,
     slot_murmurate_layer_reference,

@@ -214,6 +214,45 @@ def slot_murmurate_full(x, q_proj, k_proj, v_proj, slot_k_emb, slot_v_emb, num_h
     return x_h.permute(0, 2, 1, 3).contiguous().view(B, N, D)              # :191
 
 
+def slot_murmurate_forced(q, slots_k, slots_v, forced, causal: bool = False, alpha: float = 0.9,
+                          gamma: float = 0.15, scale: Optional[float] = None):
+    """The round loop of ``slot_murmurate`` with each round's selection given.
+
+    ``forced[r]`` (int64 [B,H,N,7]) replaces round r's top-7 (reference.py:185): the attend,
+    the update and the diffusion of that round use those indices, exactly as
+    reference.py:186-189 would use its own. This lets the oracle follow the discrete choices of
+    an implementation under test, so that every row's output, weights and gradients can be
+    compared even where a near tie made the two pick different slots. The oracle's own choice
+    is still computed on its state every round and returned for the index check.
+
+    Returns ``(out, weights_of_last_round, info)``; differentiable with respect to q, slots_k
+    and slots_v. ``info["own_idx"][r]`` is the oracle's own top-7 (lowest-index tie rule) on the
+    state entering round r, ``info["top8"][r]`` the 8 largest masked scores of each row.
+    """
+    qf = q.float()
+    B, H = q.shape[:2]
+    sk = slots_k.float().expand(B, H, -1, -1)
+    sv = slots_v.float().expand(B, H, -1, -1)
+    M = sk.shape[2]
+    out = torch.zeros_like(qf)
+    info: Dict[str, List[torch.Tensor]] = {"own_idx": [], "top8": []}
+    w = None
+    for idx in forced:
+        with torch.no_grad():
+            scores = slot_scores(qf.detach(), sk.detach(), causal=causal)             # :14-36
+            srt = torch.sort(scores, dim=-1, descending=True, stable=True).values
+            info["top8"].append(srt[..., :min(8, M)])
+            info["own_idx"].append(topk_indices(scores))                              # :38
+            del scores, srt
+        o, w = slot_attend(qf, sk, sv, idx.to(torch.int64), scale)                    # :186
+        out = out + o                                                                 # :187
+        sk, sv = slot_update(qf, qf, sk, sv, idx.to(torch.int64), w, alpha)          # :188
+        sk, sv = slot_diffusion(sk, sv, gamma)                                        # :189
+    if w is None:
+        w = torch.zeros(B, H, q.shape[2], TOP_K, dtype=torch.float32)
+    return out, w, info
+
+
 @torch.no_grad()
 def slot_murmurate_trace(q, slots_k, slots_v, rounds: int = 3, causal: bool = False,
                          alpha: float = 0.9, gamma: float = 0.15,

@@ -1,5 +1,7 @@
 """Multi-process host logic on CPU ranks (gloo, world size 2): (batch, head)
-sharding round trips and the data-parallel gradient all-reduce."""
+sharding round trips, the data-parallel gradient all-reduce, and a rank that
+leaves between data-parallel steps (the survivor's next collective must end
+with an error within the process group's timeout)."""
 import os
 import socket
 
@@ -122,3 +124,50 @@ def test_gloo_two_ranks_dp_train_step_matches_single_process():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert dict(results) == {0: True, 1: True}
+
+
+def _leaver_worker(rank, world, port, results):
+    """Both ranks take one data-parallel step; then rank 1 leaves (between steps, with no
+    collective in flight) and rank 0's next step must end with an error from its gradient
+    all-reduce within the process group's short timeout, not hang."""
+    import datetime
+    import time
+    from murmurative_attention_b200.training import GradientAverager, dp_train_step
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    model = _Toy()
+    opt = torch.optim.SGD(model.parameters(), lr=0.1)
+    avg = GradientAverager(model.parameters())
+    x = torch.randn(3, 6, generator=torch.Generator().manual_seed(rank))
+    dp_train_step(model, x, opt, avg)
+    dist.barrier()
+    if rank == 1:
+        results[rank] = "left"
+        os._exit(0)  # leaves without a goodbye
+    time.sleep(0.5)
+    t0 = time.monotonic()
+    try:
+        dp_train_step(model, x, opt, avg)
+        results[rank] = ("completed", time.monotonic() - t0)
+    except Exception as e:  # noqa: BLE001 — the collective's error, whatever its class
+        results[rank] = ("error", time.monotonic() - t0, type(e).__name__)
+    os._exit(0)  # the group cannot be torn down cleanly without its peer
+
+
+def test_gloo_rank_leaving_between_steps_ends_survivors_next_step_with_an_error():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results[1] == "left"
+    kind, seconds = results[0][0], results[0][1]
+    assert kind == "error", results[0]
+    assert seconds < 30, results[0]

@@ -131,3 +131,23 @@ def test_oracle_full_surface_matches_reference():
     (out * f["grad_out"]).sum().backward()
     for n, t in zip(names, leaves):
         torch.testing.assert_close(t.grad, f["grad_" + n], atol=1e-5, rtol=1e-4, msg=n)
+
+
+def test_forced_oracle_with_its_own_picks_is_the_oracle():
+    """oracle.slot_murmurate_forced given the oracle's own per-round picks reproduces
+    oracle.slot_murmurate exactly (outputs, weights, gradients) on a reference fixture's inputs,
+    and reports those picks as its own top-7."""
+    f = load("causal_small")
+    rounds, causal = int(f["meta_rounds"]), bool(int(f["meta_causal"]))
+    q, sk, sv, go = (f[k].float() for k in ("q", "slots_k", "slots_v", "grad_out"))
+    tr = om.slot_murmurate_trace(q, sk, sv, rounds, causal)
+    a = [t.clone().requires_grad_(True) for t in (q, sk, sv)]
+    b = [t.clone().requires_grad_(True) for t in (q, sk, sv)]
+    o1, i1, w1 = om.slot_murmurate(*a, rounds=rounds, causal=causal)
+    o2, w2, info = om.slot_murmurate_forced(*b, tr["idx"], causal=causal)
+    assert torch.equal(o1, o2) and torch.equal(w1, w2)
+    assert all(torch.equal(x, y) for x, y in zip(info["own_idx"], tr["idx"]))
+    (o1 * go).sum().backward()
+    (o2 * go).sum().backward()
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)

@@ -1,9 +1,8 @@
 """The forward entry point that allocates nothing (murm_slot_murmurate_fwd_noscratch).
 
 Some callers cannot allocate device memory — a serving plugin handed only its
-input and output buffers under a fixed memory budget, code inside a
-global-mode CUDA stream capture, a foreign-language host without a binding to
-the CUDA allocator. For them the library keeps its forward scratch in one
+input and output buffers under a fixed memory budget, or a foreign-language
+host without a binding to the CUDA allocator. For them the library keeps its forward scratch in one
 built-in 64 MiB device array. These tests call that entry point through the C
 ABI and check it against the regular entry point (caller-provided scratch) on
 two calls in a row with different inputs, so contents the shared array keeps
