@@ -123,94 +123,134 @@ class _SelectAttend(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out, grad_weights, _grad_indices):
-        lib = _lib.load_library()
         q, sk, sv, indices, weights = ctx.saved_tensors
-        B, H, N, D = q.shape
-        M = sk.shape[2]
-        dt = q.dtype
-        shape = _shape(B, H, N, M, D, _DT[dt])
-        _, ws_bytes = _sizes(shape)
-        ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
-        go = _rows(grad_out if grad_out is not None else torch.zeros_like(q), dt)
-        gw = grad_weights.float().contiguous() if grad_weights is not None else None
-        gq = torch.empty(B, H, N, D, device=q.device, dtype=dt)
-        gsk = torch.empty(B, H, M, D, device=q.device, dtype=dt)
-        gsv = torch.empty(B, H, M, D, device=q.device, dtype=dt)
-        a = _lib.SelectAttendBwdArgs(
-            shape=shape, scale=float(ctx.scale) if ctx.scale is not None else 0.0,
-            q=_ptr(q), q_stride=_s3(q), slot_keys=_ptr(sk), sk_stride=_s3(sk), slot_values=_ptr(sv),
-            sv_stride=_s3(sv), indices=_ptr(indices), weights=_ptr(weights), grad_out=_ptr(go),
-            go_stride=_s3(go), grad_weights=_ptr(gw), grad_q=_ptr(gq), gq_stride=_s3(gq),
-            grad_slot_keys=_ptr(gsk), gsk_stride=_s3(gsk), grad_slot_values=_ptr(gsv), gsv_stride=_s3(gsv),
-            workspace=_ptr(ws), workspace_bytes=ws_bytes)
-        _lib.check(lib.murm_select_attend_bwd(ctypes.byref(a), _stream()))
+        gq, gsk, gsv = select_attend_backward(grad_out, grad_weights, q, sk, sv, indices, weights, ctx.scale)
         dq_t, dk_t, dv_t = ctx.in_dtypes
         return gq.to(dq_t), gsk.to(dk_t), gsv.to(dv_t), None, None, None, None, None, None
+
+
+def select_attend_backward(grad_out: Optional[torch.Tensor], grad_weights: Optional[torch.Tensor],
+                           query: torch.Tensor, slot_keys: torch.Tensor, slot_values: torch.Tensor,
+                           indices: torch.Tensor, weights: torch.Tensor,
+                           scale: Optional[float]) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients of slot_select_attend's output and weights with respect to query, slot_keys
+    and slot_values (in query's dtype), given the forward's indices and weights: the
+    reference's slot_select_attend_backward (torch_binding.cpp:11-14)."""
+    lib = _lib.load_library()
+    dt = query.dtype
+    q = _rows(query, dt)
+    sk = _rows(slot_keys, dt)
+    sv = _rows(slot_values, dt)
+    B, H, N, D = q.shape
+    M = sk.shape[2]
+    shape = _shape(B, H, N, M, D, _dtype_code(q, "query"))
+    _, ws_bytes = _sizes(shape)
+    ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
+    go = _rows(grad_out if grad_out is not None else torch.zeros_like(q), dt)
+    gw = grad_weights.float().contiguous() if grad_weights is not None else None
+    idx = indices.to(device=q.device, dtype=torch.int64).contiguous()
+    w = weights.to(device=q.device, dtype=torch.float32).contiguous()
+    gq = torch.empty(B, H, N, D, device=q.device, dtype=dt)
+    gsk = torch.empty(B, H, M, D, device=q.device, dtype=dt)
+    gsv = torch.empty(B, H, M, D, device=q.device, dtype=dt)
+    a = _lib.SelectAttendBwdArgs(
+        shape=shape, scale=float(scale) if scale is not None else 0.0,
+        q=_ptr(q), q_stride=_s3(q), slot_keys=_ptr(sk), sk_stride=_s3(sk), slot_values=_ptr(sv),
+        sv_stride=_s3(sv), indices=_ptr(idx), weights=_ptr(w), grad_out=_ptr(go),
+        go_stride=_s3(go), grad_weights=_ptr(gw), grad_q=_ptr(gq), gq_stride=_s3(gq),
+        grad_slot_keys=_ptr(gsk), gsk_stride=_s3(gsk), grad_slot_values=_ptr(gsv), gsv_stride=_s3(gsv),
+        workspace=_ptr(ws), workspace_bytes=ws_bytes)
+    _lib.check(lib.murm_select_attend_bwd(ctypes.byref(a), _stream()))
+    return gq, gsk, gsv
+
+
+def _update_forward(token_keys, token_values, slot_keys, slot_values, indices, weights, alpha):
+    """murm_slot_update_fwd: new slot tables (slot_keys' dtype) and the saved block (per-slot
+    means and weight sums, which depend on the tokens, indices and weights only)."""
+    lib = _lib.load_library()
+    code = _dtype_code(slot_keys, "slot_keys")
+    dt = slot_keys.dtype
+    tk = _rows(token_keys, dt)
+    tv = _rows(token_values, dt)
+    sk = _rows(slot_keys, dt)
+    sv = _rows(slot_values, dt)
+    B, H, N, D = tk.shape
+    M = sk.shape[2]
+    shape = _shape(B, H, N, M, D, code)
+    saved_bytes, ws_bytes = _sizes(shape)
+    dev = tk.device
+    saved = torch.empty(saved_bytes, device=dev, dtype=torch.uint8)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    idx = indices.to(device=dev, dtype=torch.int64).contiguous()
+    w = weights.to(device=dev, dtype=torch.float32).contiguous()
+    nk = torch.empty(B, H, M, D, device=dev, dtype=dt)
+    nv = torch.empty(B, H, M, D, device=dev, dtype=dt)
+    a = _lib.SlotUpdateArgs(
+        shape=shape, alpha=float(alpha), token_keys=_ptr(tk), tk_stride=_s3(tk), token_values=_ptr(tv),
+        tv_stride=_s3(tv), slot_keys=_ptr(sk), sk_stride=_s3(sk), slot_values=_ptr(sv), sv_stride=_s3(sv),
+        indices=_ptr(idx), weights=_ptr(w), new_slot_keys=_ptr(nk), nsk_stride=_s3(nk),
+        new_slot_values=_ptr(nv), nsv_stride=_s3(nv), saved=_ptr(saved), saved_bytes=saved_bytes,
+        workspace=_ptr(ws), workspace_bytes=ws_bytes)
+    _lib.check(lib.murm_slot_update_fwd(ctypes.byref(a), _stream()))
+    return nk, nv, saved, (tk, tv, idx, w)
+
+
+def slot_update_backward(grad_new_keys: Optional[torch.Tensor], grad_new_values: Optional[torch.Tensor],
+                         token_keys: torch.Tensor, token_values: torch.Tensor, indices: torch.Tensor,
+                         weights: torch.Tensor, alpha: float, slots: int, saved: Optional[torch.Tensor] = None):
+    """Gradients of slot_update: (grad_token_keys, grad_token_values, grad_old_slot_keys,
+    grad_old_slot_values, grad_weights), the reference's slot_update_backward
+    (torch_binding.cpp:19-21). ``saved`` is the forward's block; without it the per-slot means
+    and weight sums are recomputed from the tokens, indices and weights."""
+    lib = _lib.load_library()
+    dt = token_keys.dtype
+    tk = _rows(token_keys, dt)
+    tv = _rows(token_values, dt)
+    B, H, N, D = tk.shape
+    M = int(slots)
+    dev = tk.device
+    gnk = _rows(grad_new_keys if grad_new_keys is not None else torch.zeros(B, H, M, D, device=dev, dtype=dt), dt)
+    gnv = _rows(grad_new_values if grad_new_values is not None else torch.zeros(B, H, M, D, device=dev, dtype=dt), dt)
+    idx = indices.to(device=dev, dtype=torch.int64).contiguous()
+    w = weights.to(device=dev, dtype=torch.float32).contiguous()
+    if saved is None:  # the means and weight sums do not depend on the old slot tables
+        _, _, saved, _ = _update_forward(tk, tv, gnk, gnv, idx, w, alpha)
+    shape = _shape(B, H, N, M, D, _DT[dt])
+    _, ws_bytes = _sizes(shape)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    gtk = torch.empty(B, H, N, D, device=dev, dtype=dt)
+    gtv = torch.empty(B, H, N, D, device=dev, dtype=dt)
+    gsk = torch.empty(B, H, M, D, device=dev, dtype=dt)
+    gsv = torch.empty(B, H, M, D, device=dev, dtype=dt)
+    gw = torch.empty(B, H, N, 7, device=dev, dtype=torch.float32)
+    a = _lib.SlotUpdateBwdArgs(
+        shape=shape, alpha=float(alpha), token_keys=_ptr(tk), tk_stride=_s3(tk), token_values=_ptr(tv),
+        tv_stride=_s3(tv), indices=_ptr(idx), weights=_ptr(w), saved=_ptr(saved), saved_bytes=saved.numel(),
+        grad_new_keys=_ptr(gnk), gnk_stride=_s3(gnk), grad_new_values=_ptr(gnv), gnv_stride=_s3(gnv),
+        grad_token_keys=_ptr(gtk), gtk_stride=_s3(gtk), grad_token_values=_ptr(gtv), gtv_stride=_s3(gtv),
+        grad_slot_keys=_ptr(gsk), gsk_stride=_s3(gsk), grad_slot_values=_ptr(gsv), gsv_stride=_s3(gsv),
+        grad_weights=_ptr(gw), workspace=_ptr(ws), workspace_bytes=ws_bytes)
+    _lib.check(lib.murm_slot_update_bwd(ctypes.byref(a), _stream()))
+    return gtk, gtv, gsk, gsv, gw
 
 
 class _SlotUpdate(torch.autograd.Function):
     @staticmethod
     def forward(ctx, token_keys, token_values, slot_keys, slot_values, indices, weights, alpha):
-        lib = _lib.load_library()
-        code = _dtype_code(slot_keys, "slot_keys")
-        dt = slot_keys.dtype
-        tk = _rows(token_keys, dt)
-        tv = _rows(token_values, dt)
-        sk = _rows(slot_keys, dt)
-        sv = _rows(slot_values, dt)
-        B, H, N, D = tk.shape
-        M = sk.shape[2]
-        shape = _shape(B, H, N, M, D, code)
-        saved_bytes, ws_bytes = _sizes(shape)
-        dev = tk.device
-        saved = torch.empty(saved_bytes, device=dev, dtype=torch.uint8)
-        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
-        idx = indices.to(device=dev, dtype=torch.int64).contiguous()
-        w = weights.to(device=dev, dtype=torch.float32).contiguous()
-        nk = torch.empty(B, H, M, D, device=dev, dtype=dt)
-        nv = torch.empty(B, H, M, D, device=dev, dtype=dt)
-        a = _lib.SlotUpdateArgs(
-            shape=shape, alpha=float(alpha), token_keys=_ptr(tk), tk_stride=_s3(tk), token_values=_ptr(tv),
-            tv_stride=_s3(tv), slot_keys=_ptr(sk), sk_stride=_s3(sk), slot_values=_ptr(sv), sv_stride=_s3(sv),
-            indices=_ptr(idx), weights=_ptr(w), new_slot_keys=_ptr(nk), nsk_stride=_s3(nk),
-            new_slot_values=_ptr(nv), nsv_stride=_s3(nv), saved=_ptr(saved), saved_bytes=saved_bytes,
-            workspace=_ptr(ws), workspace_bytes=ws_bytes)
-        _lib.check(lib.murm_slot_update_fwd(ctypes.byref(a), _stream()))
+        nk, nv, saved, (tk, tv, idx, w) = _update_forward(token_keys, token_values, slot_keys, slot_values,
+                                                           indices, weights, alpha)
         ctx.save_for_backward(tk, tv, idx, w, saved)
         ctx.alpha = float(alpha)
-        ctx.M = M
+        ctx.M = slot_keys.shape[2]
         ctx.in_dtypes = (token_keys.dtype, token_values.dtype, slot_keys.dtype, slot_values.dtype)
         return nk, nv
 
     @staticmethod
     def backward(ctx, grad_nk, grad_nv):
-        lib = _lib.load_library()
         tk, tv, idx, w, saved = ctx.saved_tensors
-        B, H, N, D = tk.shape
-        M = ctx.M
-        dt = tk.dtype
-        shape = _shape(B, H, N, M, D, _DT[dt])
-        _, ws_bytes = _sizes(shape)
-        dev = tk.device
-        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
-        gnk = _rows(grad_nk if grad_nk is not None else torch.zeros(B, H, M, D, device=dev, dtype=dt), dt)
-        gnv = _rows(grad_nv if grad_nv is not None else torch.zeros(B, H, M, D, device=dev, dtype=dt), dt)
-        gtk = torch.empty_like(tk, memory_format=torch.contiguous_format)
-        gtv = torch.empty_like(tv, memory_format=torch.contiguous_format)
-        gsk = torch.empty(B, H, M, D, device=dev, dtype=dt)
-        gsv = torch.empty(B, H, M, D, device=dev, dtype=dt)
-        gw = torch.empty(B, H, N, 7, device=dev, dtype=torch.float32)
-        a = _lib.SlotUpdateBwdArgs(
-            shape=shape, alpha=ctx.alpha, token_keys=_ptr(tk), tk_stride=_s3(tk), token_values=_ptr(tv),
-            tv_stride=_s3(tv), indices=_ptr(idx), weights=_ptr(w), saved=_ptr(saved), saved_bytes=saved.numel(),
-            grad_new_keys=_ptr(gnk), gnk_stride=_s3(gnk), grad_new_values=_ptr(gnv), gnv_stride=_s3(gnv),
-            grad_token_keys=_ptr(gtk), gtk_stride=_s3(gtk), grad_token_values=_ptr(gtv), gtv_stride=_s3(gtv),
-            grad_slot_keys=_ptr(gsk), gsk_stride=_s3(gsk), grad_slot_values=_ptr(gsv), gsv_stride=_s3(gsv),
-            grad_weights=_ptr(gw), workspace=_ptr(ws), workspace_bytes=ws_bytes)
-        _lib.check(lib.murm_slot_update_bwd(ctypes.byref(a), _stream()))
+        gtk, gtv, gsk, gsv, gw = slot_update_backward(grad_nk, grad_nv, tk, tv, idx, w, ctx.alpha, ctx.M, saved)
         a_t, b_t, c_t, d_t = ctx.in_dtypes
         return gtk.to(a_t), gtv.to(b_t), gsk.to(c_t), gsv.to(d_t), None, gw, None
-
 
 
 class _SlotSums(torch.autograd.Function):
@@ -264,6 +304,13 @@ class _SlotSums(torch.autograd.Function):
         _lib.check(lib.murm_slot_sums_bwd(ctypes.byref(a), _stream()))
         a_t, b_t = ctx.in_dtypes
         return gtk.to(a_t), gtv.to(b_t), None, gw, None
+
+
+def slot_diffusion_backward(grad_new_keys: torch.Tensor, grad_new_values: torch.Tensor,
+                            gamma: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The transposed stencil applied to the output gradients: the reference's
+    slot_diffusion_backward (torch_binding.cpp:26-28)."""
+    return _SlotDiffusion._run(_lib.load_library().murm_slot_diffusion_bwd, grad_new_keys, grad_new_values, gamma)
 
 
 class _SlotDiffusion(torch.autograd.Function):

@@ -12,6 +12,7 @@ import torch
 import torch.nn as nn
 
 from .ops import slot_murmurate
+from .torch_ops import slot_murmurate as slot_murmurate_op
 
 
 class MurmurativeAttention(nn.Module):
@@ -33,7 +34,9 @@ class MurmurativeAttention(nn.Module):
         q = self.q_proj(x).view(B, N, self.heads, self.head_dim).transpose(1, 2)
         slots_k = self.slot_embeddings.unsqueeze(0).expand(B, -1, -1, -1)
         slots_v = torch.zeros_like(slots_k)
-        attn_out, _, _ = slot_murmurate(q, slots_k, slots_v, rounds=self.rounds, top_k=self.top_k,
-                                        causal=self.causal)
+        # under torch.compile the registered operator (traceable, same kernels); eagerly the
+        # autograd Function, which skips the dispatcher's Python round trip
+        op = slot_murmurate_op if torch.compiler.is_compiling() else slot_murmurate
+        attn_out, _, _ = op(q, slots_k, slots_v, rounds=self.rounds, top_k=self.top_k, causal=self.causal)
         attn_out = attn_out.transpose(1, 2).reshape(B, N, D)
         return self.o_proj(attn_out)

@@ -87,7 +87,7 @@ def _check_inputs(q, slots_k, slots_v):
         raise RuntimeError("q, slots_k and slots_v must be on the same device")
 
 
-def _forward(q, slots_k, slots_v, rounds, top_k, causal, alpha, gamma, scale):
+def _forward(q, slots_k, slots_v, rounds, top_k, causal, alpha, gamma, scale, out=None):
     lib = _lib.load_library()
     _check_inputs(q, slots_k, slots_v)
     if not torch.cuda.is_available():
@@ -99,7 +99,8 @@ def _forward(q, slots_k, slots_v, rounds, top_k, causal, alpha, gamma, scale):
     shape = _make_shape(q, sk.shape[2], rounds, top_k, causal, alpha, gamma, scale)
     saved_b, fws_b, _ = slot_murmurate_sizes(shape)
     dev = q.device
-    out = torch.empty_like(q)  # keeps q's layout, e.g. [B,N,H,d] memory for a transposed view
+    if out is None or not _rows_ok(out, False):
+        out = torch.empty_like(q)  # keeps q's layout, e.g. [B,N,H,d] memory for a transposed view
     if not _rows_ok(out, False):
         out = torch.empty(q.shape, dtype=q.dtype, device=dev)
     idx = torch.empty(B, H, N, _lib.TOP_K, dtype=torch.int64, device=dev)
@@ -115,14 +116,15 @@ def _forward(q, slots_k, slots_v, rounds, top_k, causal, alpha, gamma, scale):
     return out, idx, w, saved, shape
 
 
-def _backward(q, grad_out, grad_w, saved, shape, slots_shape):
+def _backward(q, grad_out, grad_w, saved, shape, slots_shape, gq=None):
     lib = _lib.load_library()
     q = _rows(q)
     go = _rows(grad_out.to(q.dtype))
     gw = grad_w.float().contiguous() if grad_w is not None else None
     _, _, bws_b = slot_murmurate_sizes(shape)
     dev = q.device
-    gq = torch.empty_like(q)
+    if gq is None or not _rows_ok(gq, False):
+        gq = torch.empty_like(q)
     if not _rows_ok(gq, False):
         gq = torch.empty(q.shape, dtype=q.dtype, device=dev)
     gsk = torch.empty(slots_shape, dtype=q.dtype, device=dev)

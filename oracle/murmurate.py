@@ -84,11 +84,14 @@ def slot_select(query, slot_keys, mask=None, causal=False, position_bias=None,
                                     effective_M), tie_rule)
 
 
-def slot_attend(query, slot_keys, slot_values, indices, scale: Optional[float] = None):
+def slot_attend(query, slot_keys, slot_values, indices, scale: Optional[float] = None,
+                logits_out: Optional[list] = None):
     """reference.py:42-68 (``slot_attend_reference``).
 
     Gathers the selected keys, recomputes their scores *without* any mask
     (reference.py:61-63), softmaxes them and averages the selected values.
+    ``logits_out`` (checker instrumentation): the scaled logits are appended to it, with
+    their gradient retained when they require one.
     """
     B, H, N, D = query.shape
     M = slot_keys.shape[2]
@@ -98,6 +101,10 @@ def slot_attend(query, slot_keys, slot_values, indices, scale: Optional[float] =
     flat = indices.clamp(0, M - 1).reshape(B, H, N * K, 1).expand(-1, -1, -1, D)  # :56-58
     keys = torch.gather(slot_keys, 2, flat).reshape(B, H, N, K, D)        # :59
     logits = torch.einsum("bhnd,bhnkd->bhnk", query, keys) * scale        # :61
+    if logits_out is not None:
+        if logits.requires_grad:
+            logits.retain_grad()
+        logits_out.append(logits)
     w = F.softmax(logits, dim=-1)                                         # :63
     vals = torch.gather(slot_values, 2, flat).reshape(B, H, N, K, D)      # :65
     out = torch.einsum("bhnk,bhnkd->bhnd", w, vals)                       # :66
@@ -227,7 +234,9 @@ def slot_murmurate_forced(q, slots_k, slots_v, forced, causal: bool = False, alp
 
     Returns ``(out, weights_of_last_round, info)``; differentiable with respect to q, slots_k
     and slots_v. ``info["own_idx"][r]`` is the oracle's own top-7 (lowest-index tie rule) on the
-    state entering round r, ``info["top8"][r]`` the 8 largest masked scores of each row.
+    state entering round r, ``info["top8"][r]`` the 8 largest masked scores of each row,
+    ``info["w"][r]`` round r's softmax weights and ``info["logits"][r]`` its scaled logits (whose
+    ``.grad`` after a backward pass is the softmax adjoint of that round).
     """
     qf = q.float()
     B, H = q.shape[:2]
@@ -235,7 +244,7 @@ def slot_murmurate_forced(q, slots_k, slots_v, forced, causal: bool = False, alp
     sv = slots_v.float().expand(B, H, -1, -1)
     M = sk.shape[2]
     out = torch.zeros_like(qf)
-    info: Dict[str, List[torch.Tensor]] = {"own_idx": [], "top8": []}
+    info: Dict[str, List[torch.Tensor]] = {"own_idx": [], "top8": [], "w": [], "logits": []}
     w = None
     for idx in forced:
         with torch.no_grad():
@@ -244,7 +253,8 @@ def slot_murmurate_forced(q, slots_k, slots_v, forced, causal: bool = False, alp
             info["top8"].append(srt[..., :min(8, M)])
             info["own_idx"].append(topk_indices(scores))                              # :38
             del scores, srt
-        o, w = slot_attend(qf, sk, sv, idx.to(torch.int64), scale)                    # :186
+        o, w = slot_attend(qf, sk, sv, idx.to(torch.int64), scale, info["logits"])    # :186
+        info["w"].append(w)
         out = out + o                                                                 # :187
         sk, sv = slot_update(qf, qf, sk, sv, idx.to(torch.int64), w, alpha)          # :188
         sk, sv = slot_diffusion(sk, sv, gamma)                                        # :189
