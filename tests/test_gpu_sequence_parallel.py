@@ -3,9 +3,9 @@ phase it is built on.
 
 The two-rank test runs two processes on one GPU over gloo (CUDA tensors; the kernels of
 the two processes never wait on each other), each with half the tokens, and compares the
-ranks' outputs, indices, weights and gradients with one process over all tokens. Slot
-gradients are per-rank partial sums (like data-parallel gradients); their sum over the
-ranks must equal the single-process gradient.
+ranks' outputs, indices, weights and gradients with one process over all tokens and with the
+oracle. Slot gradients are per-rank partial sums (like data-parallel gradients); their sum
+over the ranks must equal the single-process gradient.
 """
 import os
 import socket
@@ -110,3 +110,17 @@ def test_two_ranks_match_one(causal):
     torch.testing.assert_close(cat("gq"), full["gq"], atol=1e-4, rtol=1e-4)
     torch.testing.assert_close(r0["gsk"] + r1["gsk"], full["gsk"], atol=1e-4, rtol=1e-4)
     torch.testing.assert_close(r0["gsv"] + r1["gsv"], full["gsv"], atol=1e-4, rtol=1e-4)
+    # and the two-rank composition against the oracle (reference.py:177-189, with the slot sums
+    # of reference.py:87-103 all-reduced over the token shards): fp32, every row unambiguous here
+    q, sk, sv, go = _inputs(causal)
+    qf, skf, svf = (t.clone().requires_grad_(True) for t in (q, sk, sv))
+    ro, ri, rw = om.slot_murmurate(qf, skf, svf, rounds=3, causal=causal)
+    (ro * go).sum().backward()
+    ok = om.row_gap_ok(om.slot_murmurate_trace(q, sk, sv, 3, causal)["top8"][-1])
+    assert bool(ok.all()), "these seeded inputs have no near-tie rows"
+    assert torch.equal(cat("idx"), ri)
+    torch.testing.assert_close(cat("out"), ro.detach(), atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(cat("w"), rw.detach(), atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(cat("gq"), qf.grad, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(r0["gsk"] + r1["gsk"], skf.grad, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(r0["gsv"] + r1["gsv"], svf.grad, atol=1e-4, rtol=1e-4)
