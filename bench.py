@@ -27,7 +27,10 @@ events recorded on its own launch stream. Two more BASELINE configurations run
 at the same N: ``strong`` is configs[2] (bf16 causal, 128 (batch, head) pairs)
 as one global problem split over the ranks (strong scaling, outputs gathered
 and checked against one GPU's run), ``layer`` is configs[3], the data-parallel
-layer training step with its NCCL gradient all-reduce inside the timed region.
+layer training step with its NCCL gradient all-reduce inside the timed region. The rows past the
+hot path are measured in the same run: ``sp`` (sequence parallelism over the ranks, one NCCL
+all-reduce of the slot sums per round), ``surface`` (the reference's 6-argument op with mask and
+position bias) and ``decode`` (the streaming decode step).
 ``--impl reference`` times the reference's CPU path (the oracle port, which
 runs the reference.py operations) on the host cores, whole steps of the
 workload.
@@ -367,6 +370,11 @@ def run_ours(args):
     # the other BASELINE configurations at this N (every rank takes the same collective steps)
     strong = None if args.skip_strong else strong_leg(args, world, rank, dev, flush)
     layer = None if args.skip_layer else layer_leg(args, world, rank, dev, flush)
+    sp = surface = decode = None
+    if not args.skip_widening:  # the rows past the hot path, measured in the same run
+        sp = sp_leg(args, world, rank, dev, flush)
+        surface = surface_leg(args, dev, flush)
+        decode = decode_leg(args, dev, flush)
 
     if rank != 0:
         if world > 1:
@@ -389,7 +397,7 @@ def run_ours(args):
             "config": workload_config({"parallelism": f"(batch,head)-sharded weak scaling, {world} rank(s)",
                                        "timing": "CUDA graph replay" if graph_used else "eager launches"}),
             "roofline": roof, "step_roofline": step_roof, "e2e": e2e, "e2e_autograd": e2e_autograd,
-            "strong": strong, "layer": layer,
+            "strong": strong, "layer": layer, "sp": sp, "surface": surface, "decode": decode,
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk,
             "kernels": {k: {"launches_per_step": v[0] / prof_steps, "ms_per_step": round(v[1] / prof_steps, 5)}
@@ -717,13 +725,11 @@ def run_layer(args):
         dist.destroy_process_group()
 
 
-def run_surface(args):
+def surface_leg(args, dev, flush):
     """The reference's full op (ops.slot_murmurate, 6 arguments) on the north-star sizes:
     B=1, N=8192, 16 heads of d=64 (D=1024), M=256, R=3, fp16, separate q/k/v projections,
     residual x, a selection mask and a position bias; forward + backward through the
-    per-phase CUDA-core kernels (murm_ops.cu). One rank."""
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    per-phase CUDA-core kernels (murm_ops.cu)."""
     from murmurative_attention_b200 import functional as F
     B, N, H, Dh, M = 1, 8192, 16, 64, 256
     g = torch.Generator(device=dev).manual_seed(3000)
@@ -738,27 +744,21 @@ def run_surface(args):
     def step():
         out = F.slot_murmurate(x, qp, kp, vp, ske, sve, num_heads=H, rounds=3, mask=mask, position_bias_fn=bias_fn)
         out.backward(go)
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    times = time_steps(step, args.steps, flush)
-    ms = sum(times) / args.steps
-    line = {"metric": "ops.slot_murmurate (6-argument op surface) fwd+bwd tokens/s", "value": round(B * N / (ms / 1e3), 1),
-            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "op surface: x, q/k/v projections [1,8192,1024], slot embeddings [16,256,64], "
-                                   "mask [8192,256] (90% kept), position bias from x, dynamic M, R=3",
-                       "path": "per-phase CUDA-core kernels (murm_ops.cu)"}}
-    print(json.dumps(line), flush=True)
+    ms = sum(time_steps(step, args.steps, flush)) / args.steps
+    return {"metric": "ops.slot_murmurate (6-argument op surface) fwd+bwd tokens/s", "value": round(B * N / (ms / 1e3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 5), "dtype": "fp16",
+            "workload": "op surface: x, q/k/v projections [1,8192,1024], slot embeddings [16,256,64], "
+                        "mask [8192,256] (90% kept), position bias from x, dynamic M, R=3",
+            "path": "per-phase CUDA-core kernels (murm_ops.cu)"}
 
 
-def run_decode(args):
+def decode_leg(args, dev, flush):
     """Streaming decode (the reference's decode plan): 16 sequences x 16 heads of d=64,
     M=256 resident slots, fp16, one token per sequence per step through murm_decode_step,
     the step replayed from a CUDA graph. tokens/s = sequences / step time."""
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     from murmurative_attention_b200.decode import SlotPool
     B, H, M, D = 16, 16, 256, 64
     g = torch.Generator(device=dev).manual_seed(4000)
@@ -770,44 +770,28 @@ def run_decode(args):
     for _ in range(args.warmup):
         pool.step(q, k, v, x, causal=True)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        pool.step(q, k, v, x, causal=True)
-    graph.replay()
-    torch.cuda.synchronize()
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
-    times = time_steps(graph.replay, args.steps, flush)
-    ms = sum(times) / args.steps
-    line = {"metric": "streaming decode tokens/s (one token per sequence per step)", "value": round(B / (ms / 1e3), 1),
-            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "decode: 16 sequences x 16 heads, d=64, M=256 resident slots, causal, one launch per step",
-                       "pool_bytes_per_step": 2 * 2 * B * H * M * D * 2,
-                       "l2": "flushed by a 256 MiB write before every timed step"}}
-    print(json.dumps(line), flush=True)
+    fn, graph = graph_of(lambda: pool.step(q, k, v, x, causal=True))
+    ms = sum(time_steps(fn, args.steps, flush)) / args.steps
+    return {"metric": "streaming decode tokens/s (one token per sequence per step)", "value": round(B / (ms / 1e3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 5), "dtype": "fp16",
+            "workload": "decode: 16 sequences x 16 heads, d=64, M=256 resident slots, causal, one launch per step",
+            "pool_bytes_per_step": 2 * 2 * B * H * M * D * 2, "timing": "CUDA graph replay" if graph else "eager"}
 
 
-def run_sp(args):
-    """Sequence parallelism (sequence_parallel.slot_murmurate_sp) for a long context with
-    few (batch, head) pairs: B=1, H=2, N=65536, d=64, M=256, R=3, fp16, causal; the
-    tokens are split over the ranks (strong scaling), one NCCL all-reduce of the slot sums
-    per round. Forward + backward (+ the slot-gradient all-reduce)."""
-    world, rank, local = dist_setup()
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    from murmurative_attention_b200.sequence_parallel import slot_murmurate_sp
+def sp_leg(args, world, rank, dev, flush):
+    """Sequence parallelism (sequence_parallel.slot_murmurate_sp) for a long context with few
+    (batch, head) pairs: B=1, H=2, N=65536, d=64, M=256, R=3, fp16, causal; the tokens are split
+    over the ranks (strong scaling), one NCCL all-reduce of the slot sums per round, and the
+    slot gradients all-reduced after the backward. Forward + backward."""
     import torch.distributed as dist
-    if world == 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29533")
-        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    from murmurative_attention_b200.sequence_parallel import slot_murmurate_sp
     B, H, N, D, M = 1, 2, 65536, 64, 256
     n = N // world
     g = torch.Generator(device=dev).manual_seed(5000)
     q = torch.randn(B, H, N, D, device=dev, generator=g).half()[:, :, rank * n:(rank + 1) * n].contiguous()
     sk = torch.randn(B, H, M, D, device=dev, generator=g).half()
     sv = torch.zeros(B, H, M, D, device=dev, dtype=torch.float16)
-    go = torch.randn(B, H, n, D, device=dev, generator=g).half()
+    go = torch.randn(B, H, N, D, device=dev, generator=g).half()[:, :, rank * n:(rank + 1) * n].contiguous()
     qd, skd, svd = (t.clone().requires_grad_(True) for t in (q, sk, sv))
 
     def step():
@@ -816,25 +800,40 @@ def run_sp(args):
         if world > 1:
             dist.all_reduce(skd.grad)
             dist.all_reduce(svd.grad)
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+        qd.grad = skd.grad = svd.grad = None
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier(world)
     times = time_steps(step, args.steps, flush)
     barrier(world)
-    total_ms = max_over_ranks(sum(times), world)
-    ms = total_ms / args.steps
+    ms = max_over_ranks(sum(times), world) / args.steps
+    return {"metric": "sequence-parallel slot_murmurate fwd+bwd (b,h)-tokens/s (long context, few (b,h))",
+            "value": round(B * H * N / (ms / 1e3), 1), "unit": "(b,h)-tokens/s", "ms_per_step": round(ms, 5),
+            "scaling": "strong", "dtype": "fp16",
+            "workload": "sp: B=1, H=2, N=65536 split over the ranks, d=64, M=256, R=3, causal",
+            "path": "per-phase kernels + one NCCL all-reduce of the slot sums per round", "parallelism": f"sp{world}"}
+
+
+def _single(args, leg_name):
+    """``--workload surface|decode|sp``: one leg alone as the JSON line."""
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    if leg_name == "sp":
+        res = sp_leg(args, world, rank, dev, flush)
+    else:
+        res = (surface_leg if leg_name == "surface" else decode_leg)(args, dev, flush)
     if rank == 0:
-        line = {"metric": "sequence-parallel slot_murmurate fwd+bwd tokens/s (long context, few (b,h))",
-                "value": round(B * H * N / (ms / 1e3), 1), "unit": "(b,h)-tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-                "config": {"workload": "sp: B=1, H=2, N=65536 split over the ranks, d=64, M=256, R=3, causal",
-                           "path": "per-phase kernels + one NCCL all-reduce of the slot sums per round",
-                           "parallelism": f"sp{world}"}}
+        line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit"), "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res.pop("ms_per_step"),
+                "higher_is_better": True, "scaling": res.pop("scaling", "weak"), "vs_baseline": None,
+                "dtype": res.pop("dtype"), "data": "synthetic", "config": res}
         print(json.dumps(line), flush=True)
-    dist.destroy_process_group()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 def main():
@@ -848,6 +847,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-strong", action="store_true", help="omit the configs[2] strong-scaling leg")
     ap.add_argument("--skip-layer", action="store_true", help="omit the configs[3] layer-step leg")
+    ap.add_argument("--skip-widening", action="store_true",
+                    help="omit the sequence-parallel, op-surface and decode legs")
     ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode", "sp"), default="northstar",
                     help="layer: BASELINE configs[3], the data-parallel layer training step; "
                          "surface: the reference's 6-argument op through the per-phase kernels; "
@@ -859,7 +860,10 @@ def main():
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference arm here"}))
             return
-        {"layer": run_layer, "surface": run_surface, "decode": run_decode, "sp": run_sp}[args.workload](args)
+        if args.workload == "layer":
+            run_layer(args)
+        else:
+            _single(args, args.workload)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -12,7 +12,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmurm_b200.so")
+# the in-tree build; MURM_B200_LIB names another build of the same library
+LIB_PATH = os.environ.get("MURM_B200_LIB") or os.path.join(HERE, "libmurm_b200.so")
 
 MURM_F32, MURM_F16, MURM_BF16 = 0, 1, 2
 TOP_K = 7

@@ -28,8 +28,10 @@ def slot_murmurate_sp(q: torch.Tensor, slots_k: torch.Tensor, slots_v: torch.Ten
     """The north-star op (token keys = token values = q, zero residual) over this rank's
     token shard ``q`` [B, H, n, d]; returns (out, indices, weights) for the shard, equal
     to the corresponding rows of the single-process result."""
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
+    if dist.is_available() and dist.is_initialized():
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+    else:  # no process group: one rank holding every token
+        world, rank = 1, 0
     B, H, n, D = q.shape
     M = slots_k.shape[2]
     mask = None
