@@ -125,6 +125,23 @@ template <typename T>
 __device__ __forceinline__ float from_bits(uint16_t b) {
   return Elem<T>::load(reinterpret_cast<const T*>(&b));
 }
+// Two floats <-> two packed 16-bit values (round to nearest), one conversion instruction per pair.
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t u);
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
 
 // Descending sort of 8 floats (19 compare-exchanges).
 __device__ __forceinline__ void sort8_desc(float (&a)[8]) {
@@ -531,9 +548,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
     }
   };
-  auto p_entry = [&](int m) -> uint16_t* {
-    return reinterpret_cast<uint16_t*>(sm + L::OFF_P + (m >> 6) * 16384 + sw128_offset(row, m & 63));
+  auto p_off = [&](int m) -> uint32_t {  // byte offset of this row's entry for slot m in P
+    return L::OFF_P + (m >> 6) * 16384 + sw128_offset(row, m & 63);
   };
+  auto p_at = [&](uint32_t off) -> uint16_t* { return reinterpret_cast<uint16_t*>(sm + off); };
 
   // fp16 (three Q buffers) runs SELECT(i+1) ahead of MMA_A(i): the row warps rank tile i+1
   // while MMA_A(i) runs, then finish tile i (second weight term, output). bf16 has one Q
@@ -633,13 +651,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     // A tile's state kept for its completion (second weight term, records, output)
     int pick[kTopK];
     float wgt[kTopK];
+    uint32_t poff[kTopK];         // P offsets of the picks of the tile being completed
     bool done_valid = false;      // the tile being completed has a valid row here
-    int old_pick[kTopK];          // picks whose P entries are set
+    uint32_t old_off[kTopK];      // P offsets of the entries that are set (0: none)
     uint4 prev[4];                // this thread's 32 output columns from earlier rounds
     T* orow = out;
 #pragma unroll
     for (int j = 0; j < kTopK; ++j) {
-      old_pick[j] = -1;
+      old_off[j] = 0u;
+      poff[j] = 0u;
       pick[j] = 0;
       wgt[j] = 0.f;
     }
@@ -656,13 +676,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < kTopK; ++j) {
             const uint16_t hb = tc::to_bits<T>(wgt[j]);
-            *p_entry(pick[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
+            *p_at(poff[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
           }
         }
         fence_proxy_async_smem();
       }
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) old_pick[j] = done_valid ? pick[j] : -1;
+      for (int j = 0; j < kTopK; ++j) old_off[j] = done_valid ? poff[j] : 0u;
       tc_fence_before();
       tc::rows_arrive<tc::kBarPlo>();  // MMA_B may start
       // ---- output: out (+)= O, 32 columns per thread ----
@@ -673,12 +693,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         if (done_valid) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            uint4 pk;
-            uint16_t* ph = reinterpret_cast<uint16_t*>(&pk);
-            const T* pv = reinterpret_cast<const T*>(&prev[i]);
+            uint32_t pk[4];
+            const uint32_t* pv = reinterpret_cast<const uint32_t*>(&prev[i]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ph[e] = tc::to_bits<T>((r ? Elem<T>::load(pv + e) : 0.f) + o[8 * i + e]);
-            reinterpret_cast<uint4*>(orow)[i] = pk;
+            for (int e = 0; e < 4; ++e) {
+              const float2 a = r ? tc::unpack2<T>(pv[e]) : make_float2(0.f, 0.f);
+              pk[e] = tc::pack2<T>(a.x + o[8 * i + 2 * e], a.y + o[8 * i + 2 * e + 1]);
+            }
+            reinterpret_cast<uint4*>(orow)[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
       }
@@ -842,7 +864,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         tc::rows_arrive<tc::kBarSfree>();  // SELECT(i+1) may overwrite the scores
       }
       if (!aborting) {
-        float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
           npick[j] = valid ? tslot[j] : 0;
@@ -854,17 +875,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             for (int k2 = 0; k2 < kTopK; ++k2) sc = (npick[j] == lim + k2) ? mraw[k2] : sc;
           }
           nwgt[j] = sc * g.scale;
-          mx = fmaxf(mx, nwgt[j]);
         }
+        const float mx = fmaxf(fmaxf(fmaxf(nwgt[0], nwgt[1]), fmaxf(nwgt[2], nwgt[3])),
+                               fmaxf(fmaxf(nwgt[4], nwgt[5]), nwgt[6]));
         // softmax with the hardware exponential and one reciprocal: the weights enter P as
         // 16-bit terms and the update sums, where a relative error of ~1e-6 is far below
         // the rounding of those terms and the parity tolerance
-        float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) {
-          nwgt[j] = __expf(nwgt[j] - mx);
-          sum += nwgt[j];
-        }
+        for (int j = 0; j < kTopK; ++j) nwgt[j] = __expf(nwgt[j] - mx);
+        const float sum = ((nwgt[0] + nwgt[1]) + (nwgt[2] + nwgt[3])) + ((nwgt[4] + nwgt[5]) + nwgt[6]);
         const float inv = __frcp_rn(sum);
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) nwgt[j] *= inv;
@@ -876,21 +895,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
       }
 
+      uint32_t npoff[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) npoff[j] = p_off(npick[j]);
       // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
       if (tile > 0) wait_live(bar_b, ph_b);
       if (!aborting && part == 0) {
 #pragma unroll
         for (int j = 0; j < kTopK; ++j)
-          if (old_pick[j] >= 0) *p_entry(old_pick[j]) = 0;
+          if (old_off[j]) *p_at(old_off[j]) = 0;
         if (valid) {
 #pragma unroll
-          for (int j = 0; j < kTopK; ++j) *p_entry(npick[j]) = tc::to_bits<T>(nwgt[j]);
+          for (int j = 0; j < kTopK; ++j) *p_at(npoff[j]) = tc::to_bits<T>(nwgt[j]);
         }
         fence_proxy_async_smem();
       }
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        old_pick[j] = (valid && !aborting) ? npick[j] : -1;
+        old_off[j] = (valid && !aborting) ? npoff[j] : 0u;
+        poff[j] = npoff[j];
         pick[j] = npick[j];
         wgt[j] = nwgt[j];
       }
