@@ -497,13 +497,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tc_fence_after();
   };
   auto q_slot = [&](int tile_idx) { return tile_idx % C::kQBufs; };
-  const uint64_t l2_keep = l2_policy_evict_last();
   auto issue_q = [&](int tile_idx) {  // issuer
     const int bs = q_slot(tile_idx);
     mbar_arrive_expect_tx(&bar_q[bs], tc::kQBytes);
-    // q is read again by the later rounds and the backward: keep it in L2
-    tma_load_4d_hint(sm + L::OFF_Q + bs * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bs],
-                     l2_keep);
+    tma_load_4d(sm + L::OFF_Q + bs * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bs]);
     q_pending[bs] = true;
   };
   auto wait_q = [&](int tile_idx) -> bool {  // issuer

@@ -423,19 +423,16 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   // the issuer's bookkeeping of asynchronous copies: the last tile issued / waited for
   int q_issued = -1, g_issued = -1, w_issued = -1, q_done = -1, g_done = -1, w_done = -1;
   bool tab_pending = false;
-  // q and grad_out tiles are read again by the earlier rounds' launches: keep them in L2 until
-  // the last backward launch (round 0), whose reads are the step's last
-  const uint64_t l2_pol = r > 0 ? l2_policy_evict_last() : l2_policy_evict_first();
   auto load_q = [&](int j) {  // issuer
     const int s = j % 3;
     mbar_arrive_expect_tx(&bar_q[s], tcb::kTileBytes);
-    tma_load_4d_hint(sm + tcb::OFF_Q + s * tcb::kTileBytes, &qmap, 0, t_beg + j * kBT, h, b, &bar_q[s], l2_pol);
+    tma_load_4d(sm + tcb::OFF_Q + s * tcb::kTileBytes, &qmap, 0, t_beg + j * kBT, h, b, &bar_q[s]);
     q_issued = j;
   };
   auto load_g = [&](int j) {  // issuer
     const int s = j % 3;
     mbar_arrive_expect_tx(&bar_g[s], tcb::kTileBytes);
-    tma_load_4d_hint(sm + tcb::OFF_G + s * tcb::kTileBytes, &gmap, 0, t_beg + j * kBT, h, b, &bar_g[s], l2_pol);
+    tma_load_4d(sm + tcb::OFF_G + s * tcb::kTileBytes, &gmap, 0, t_beg + j * kBT, h, b, &bar_g[s]);
     g_issued = j;
   };
   auto load_w = [&](int j) {  // issuer: the tile's softmax weights, 32 bytes per token
