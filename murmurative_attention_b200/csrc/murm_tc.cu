@@ -44,15 +44,22 @@ __device__ int g_device_error;  // set by a bounded wait that expired; read by m
 namespace tc {
 constexpr int kD = 64;
 constexpr int kSlotsPad = 256;
-constexpr int kRowThreads = 256;               // 2 warps per TMEM lane quadrant
-constexpr int kIssuerWarp = kRowThreads / 32;   // one more warp: its lane 0 issues MMAs and copies
-constexpr int kThreads = kRowThreads + 32;
+constexpr int kRowThreads = 256;                // 8 row warps: 2 per TMEM lane quadrant
+constexpr int kEpiWarp = kRowThreads / 32;       // 4 epilogue warps (8..11), one per lane quadrant
+constexpr int kEpiThreads = 128;
+constexpr int kIssuerWarp = kEpiWarp + 4;        // a fourth warpgroup: warp 12's lane 0 issues MMAs and
+constexpr int kThreads = kRowThreads + kEpiThreads + 128;  // copies, warps 13-15 only give up registers
+// Registers per thread: launched at 128 (512 threads, the whole register file); the row warpgroups
+// raise theirs to kRowRegs, the fourth warpgroup lowers its to kIdleRegs, the epilogue keeps 128.
+constexpr int kRowRegs = 152, kIdleRegs = 80;
+static_assert(2 * 128 * kRowRegs + 128 * 128 + 128 * kIdleRegs == 65536, "register split must sum to the launch's");
 constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: scores | slot sums S and weight sums W (2 halves of 80: 64 S columns, then 16
-// columns that each hold W) | exchange | attend output O
-constexpr uint32_t COL_S = 0, COL_U = 256, COL_X = 416, COL_O = 448;
+// columns that each hold W) | group-maxima exchange of a row's two threads | the row's picks and
+// scores handed from the row warps to the epilogue warps | attend output O
+constexpr uint32_t COL_S = 0, COL_U = 256, COL_X = 416, COL_H = 432, COL_O = 448;
 constexpr uint32_t kUW = 80;  // columns per half of the slot-sum accumulator
 constexpr uint32_t kQBytes = 128 * 128;
 
@@ -62,17 +69,18 @@ enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
 __device__ __forceinline__ void quadrant_sync(int quadrant) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(32 * kParts) : "memory");
 }
-// Named barriers over the whole CTA that the issuer warp waits on and the row
-// warps only arrive at: the tile's first (5) and second (6) weight terms are in P;
-// the row warps are done reading the tile's scores (7).
+// Named barriers that the issuer warp waits on and the others only arrive at: the tile's first (5)
+// and second (6) weight terms are in P (the epilogue warps arrive); the row warps are done reading
+// the tile's scores (7).
 constexpr int kBarPhi = 5, kBarPlo = 6, kBarSfree = 7;
-template <int kId>
+constexpr int kCountP = kEpiThreads + 32, kCountS = kRowThreads + 32;
+template <int kId, int kCount>
 __device__ __forceinline__ void issuer_wait() {
-  asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kThreads) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kCount) : "memory");
 }
-template <int kId>
-__device__ __forceinline__ void rows_arrive() {
-  asm volatile("bar.arrive %0, %1;" ::"n"(kId), "n"(kThreads) : "memory");
+template <int kId, int kCount>
+__device__ __forceinline__ void group_arrive() {
+  asm volatile("bar.arrive %0, %1;" ::"n"(kId), "n"(kCount) : "memory");
 }
 
 // Shared-memory matrix descriptor kept as two 32-bit words. The low word holds the
@@ -109,7 +117,7 @@ template <typename T> struct Layout {
   static constexpr uint32_t OFF_ONES = OFF_Q + Cfg<T>::kQBufs * kQBytes;
   static constexpr uint32_t OFF_XCH = OFF_ONES + 2048;  // [7][kRowThreads] packed ranks: per-thread top-7 lists
   static constexpr uint32_t OFF_MISC = OFF_XCH + kTopK * kRowThreads * 8;
-  static constexpr uint32_t kSmem = OFF_MISC + 128 + 1024;  // + alignment slack
+  static constexpr uint32_t kSmem = OFF_MISC + 192 + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
@@ -416,11 +424,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint64_t* bar_s = bar_img + 4;  // SELECT done
   uint64_t* bar_a = bar_img + 5;  // MMA_A done
   uint64_t* bar_b = bar_img + 6;  // MMA_B done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 64);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 68);
+  uint64_t* hand_ready = bar_img + 7;  // [4] per lane quadrant: the row warps' picks of a tile are in TMEM
+  uint64_t* hand_free = bar_img + 11;  // [4] per lane quadrant: the epilogue warp has read them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 128);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 132);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool issuer_warp = warp == tc::kIssuerWarp;
+  const bool row_warp = warp < tc::kEpiWarp;
+  const bool epi_warp = warp >= tc::kEpiWarp && warp < tc::kIssuerWarp;
   const int row = tid & (kTile - 1);  // token row within the tile == TMEM lane
   const int part = (tid >> 7) & 1;    // which 128 of the 256 slot columns this thread scans
   const int quadrant = warp & 3;
@@ -454,6 +466,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_b, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&hand_ready[i], 32);  // the quadrant's first row warp (its 32 threads)
+      mbar_init(&hand_free[i], 32);   // the quadrant's epilogue warp
+    }
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -475,6 +491,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // kernel, whose outputs (the round's state and operand images) are read from here on
   pdl_wait();
   pdl_trigger();
+  // the register split between the warpgroups; it sums to the launch's allocation, so the row
+  // warpgroups' increase is met once the fourth warpgroup has given its registers back
+  if (warp >= tc::kIssuerWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(tc::kIdleRegs));
+  } else if (warp < tc::kEpiWarp) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(tc::kRowRegs));
+  }
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * quadrant) << 16;
   const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
@@ -567,7 +590,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       return ok;
     };
     auto mma_b = [&](int tile_idx) {  // ---- MMA_B(tile_idx) ----
-      tc::issuer_wait<tc::kBarPlo>();
+      tc::issuer_wait<tc::kBarPlo, tc::kCountP>();
       if (lane == 0 && !*s_abort) {
         tc_fence_after();
         issue_update(tile_idx, false);
@@ -614,7 +637,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     for (int tile = 0; tile < ntiles; ++tile) {
       if (kEarlySelect) {
         if (tile > 0) mma_b(tile - 1);
-        tc::issuer_wait<tc::kBarSfree>();  // the scores of tile i are read: SELECT(i+1)
+        tc::issuer_wait<tc::kBarSfree, tc::kCountS>();  // the scores of tile i are read: SELECT(i+1)
         if (lane == 0 && !*s_abort && tile + 1 < ntiles) {
           tc_fence_after();
           if (wait_q(tile + 1)) {
@@ -624,7 +647,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
         __syncwarp();
       }
-      tc::issuer_wait<tc::kBarPhi>();
+      tc::issuer_wait<tc::kBarPhi, tc::kCountP>();
       if (lane == 0 && !*s_abort) {
         tc_fence_after();
         // ---- MMA_A(i) ----
@@ -643,67 +666,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     if (kEarlySelect && ntiles > 0) mma_b(ntiles - 1);
     }  // segments
     if (lane == 0) drain();
-  } else {
+  } else if (row_warp) {
     // ================= row warps =================
-    // A tile's state kept for its completion (second weight term, records, output)
-    int pick[kTopK];
-    float wgt[kTopK];
-    uint32_t poff[kTopK];         // P offsets of the picks of the tile being completed
-    bool done_valid = false;      // the tile being completed has a valid row here
-    uint32_t old_off[kTopK];      // P offsets of the entries that are set (0: none)
-    uint4 prev[4];                // this thread's 32 output columns from earlier rounds
-    T* orow = out;
-#pragma unroll
-    for (int j = 0; j < kTopK; ++j) {
-      old_off[j] = 0u;
-      poff[j] = 0u;
-      pick[j] = 0;
-      wgt[j] = 0.f;
-    }
-    // wait on an mbarrier unless the kernel is already giving up
+    // Per tile: the scores' group maxima, the threshold, the ranking of each half-row, the merge of a
+    // row's two lists; the first row warp of each quadrant hands the row's picks and their scores
+    // to the quadrant's epilogue warp through TMEM, and the row warps go on to the next tile.
+    uint32_t hcount = 0;  // tiles handed over (all segments)
     auto wait_live = [&](uint64_t* bar, uint32_t& ph) {
       if (!*s_abort) wait_bar(bar, ph);
     };
-    // second weight term and output of the tile whose P_hi MMA_A has consumed
-    auto complete = [&]() {
-      wait_live(bar_a, ph_a);
-      const bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
-      if (ok && part == 0) {
-        if (done_valid) {
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) {
-            const uint16_t hb = tc::to_bits<T>(wgt[j]);
-            *p_at(poff[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
-          }
-        }
-        fence_proxy_async_smem();
-      }
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) old_off[j] = done_valid ? poff[j] : 0u;
-      tc_fence_before();
-      tc::rows_arrive<tc::kBarPlo>();  // MMA_B may start
-      // ---- output: out (+)= O, 32 columns per thread ----
-      if (ok) {
-        float o[32];
-        tmem_ld32(tmem + lane_base + tc::COL_O + 32 * part, o);
-        tmem_wait_ld();
-        if (done_valid) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t pk[4];
-            const uint32_t* pv = reinterpret_cast<const uint32_t*>(&prev[i]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 a = r ? tc::unpack2<T>(pv[e]) : make_float2(0.f, 0.f);
-              pk[e] = tc::pack2<T>(a.x + o[8 * i + 2 * e], a.y + o[8 * i + 2 * e + 1]);
-            }
-            reinterpret_cast<uint4*>(orow)[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
-        }
-      }
-      tc_fence_before();  // the output's TMEM reads come before the next MMA_A
-    };
-
     for (int u = split.start[cta]; u < u_end; u = next_segment()) {
     set_segment(u);
     for (int tile = 0; tile < ntiles; ++tile) {
@@ -800,20 +771,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
       };
-      if (!aborting) rank_chunks(0);
-      // the previous tile: second weight term and output (its MMA_A is done by now; MMA_B then
-      // runs under the rest of the ranking)
-      if (kEarlySelect && tile > 0) complete();
       if (!aborting) {
+        rank_chunks(0);
         rank_chunks(2);
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) xch[j * tc::kRowThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
       }
       tc::quadrant_sync(quadrant);
 
-      // pass 3 (both threads of a row, redundantly): merge the two lists, softmax
-      int npick[kTopK];
-      float nwgt[kTopK];
+      // pass 3 (both threads of a row, redundantly): merge the two lists
       float mraw[kTopK];  // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
@@ -858,73 +824,113 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
       if (kEarlySelect) {
         tc_fence_before();
-        tc::rows_arrive<tc::kBarSfree>();  // SELECT(i+1) may overwrite the scores
+        tc::group_arrive<tc::kBarSfree, tc::kCountS>();  // SELECT(i+1) may overwrite the scores
       }
-      if (!aborting) {
+      if (part == 0) {  // warp-uniform: the quadrant's first row warp hands the row over
+        uint32_t hv[16];
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
-          npick[j] = valid ? tslot[j] : 0;
+          const int pk = (valid && !aborting) ? tslot[j] : 0;
           // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
           const uint32_t kk = tkey[j];
           float sc = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
-          if (npick[j] >= lim) {
+          if (pk >= lim) {
 #pragma unroll
-            for (int k2 = 0; k2 < kTopK; ++k2) sc = (npick[j] == lim + k2) ? mraw[k2] : sc;
+            for (int k2 = 0; k2 < kTopK; ++k2) sc = (pk == lim + k2) ? mraw[k2] : sc;
           }
-          nwgt[j] = sc * g.scale;
+          hv[j] = (uint32_t)pk;
+          hv[kTopK + j] = __float_as_uint(sc);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(nwgt[0], nwgt[1]), fmaxf(nwgt[2], nwgt[3])),
-                               fmaxf(fmaxf(nwgt[4], nwgt[5]), nwgt[6]));
+        hv[14] = hv[15] = 0u;
+        // the epilogue warp has read the previous tile's hand-over
+        if (hcount > 0 && !*s_abort && !tc::timed_wait(&hand_free[quadrant], (hcount - 1) & 1)) fail(tc::kErrMmaWait);
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + tc::COL_H, hv);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&hand_ready[quadrant]);
+      }
+      ++hcount;
+    }
+    }  // segments
+  } else if (epi_warp) {
+    // ================= epilogue warps =================
+    // One thread per token row (TMEM lane) of its quadrant: the softmax of the row's picks, the
+    // weight tile P (both 16-bit terms), the round records and the output, while the row warps
+    // rank the next tile; at a segment's end, its slot-sum partials.
+    uint32_t hcount = 0;
+    uint32_t old_off[kTopK];  // P offsets of the previous tile's entries (0: none)
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) old_off[j] = 0u;
+    auto wait_live = [&](uint64_t* bar, uint32_t& ph) {
+      if (!*s_abort) wait_bar(bar, ph);
+    };
+    for (int u = split.start[cta]; u < u_end; u = next_segment()) {
+    set_segment(u);
+    for (int tile = 0; tile < ntiles; ++tile) {
+      const int n0 = t_beg + tile * kTile;
+      const int n = n0 + row;
+      const bool valid = n < t_end;
+      T* orow = row_ptr(out, os, b, h, valid ? n : n0);
+      uint4 prev[8];  // this row's output of the earlier rounds, added to this round's
+      if (r && valid) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) prev[i] = reinterpret_cast<const uint4*>(orow)[i];
+      }
+      // the row warps' picks of this tile
+      if (!*s_abort && !tc::timed_wait(&hand_ready[quadrant], hcount & 1)) fail(tc::kErrMmaWait);
+      ++hcount;
+      tc_fence_after();
+      float hf[16];
+      tmem_ld16(tmem + lane_base + tc::COL_H, hf);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&hand_free[quadrant]);
+      const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
+      int pick[kTopK];
+      float wgt[kTopK];
+      uint32_t poff[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        pick[j] = (int)__float_as_uint(hf[j]);
+        wgt[j] = hf[kTopK + j] * g.scale;
+      }
+      {
         // softmax with the hardware exponential and one reciprocal: the weights enter P as
         // 16-bit terms and the update sums, where a relative error of ~1e-6 is far below
         // the rounding of those terms and the parity tolerance
+        const float mx = fmaxf(fmaxf(fmaxf(wgt[0], wgt[1]), fmaxf(wgt[2], wgt[3])),
+                               fmaxf(fmaxf(wgt[4], wgt[5]), wgt[6]));
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) nwgt[j] = __expf(nwgt[j] - mx);
-        const float sum = ((nwgt[0] + nwgt[1]) + (nwgt[2] + nwgt[3])) + ((nwgt[4] + nwgt[5]) + nwgt[6]);
+        for (int j = 0; j < kTopK; ++j) wgt[j] = __expf(wgt[j] - mx);
+        const float sum = ((wgt[0] + wgt[1]) + (wgt[2] + wgt[3])) + ((wgt[4] + wgt[5]) + wgt[6]);
         const float inv = __frcp_rn(sum);
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) nwgt[j] *= inv;
-      } else {
-#pragma unroll
         for (int j = 0; j < kTopK; ++j) {
-          npick[j] = 0;
-          nwgt[j] = 0.f;
+          wgt[j] *= inv;
+          poff[j] = p_off(pick[j]);
         }
       }
-
-      uint32_t npoff[kTopK];
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) npoff[j] = p_off(npick[j]);
       // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
       if (tile > 0) wait_live(bar_b, ph_b);
-      if (!aborting && part == 0) {
+      const bool live = valid && !aborting;
+      if (!aborting) {
 #pragma unroll
         for (int j = 0; j < kTopK; ++j)
           if (old_off[j]) *p_at(old_off[j]) = 0;
         if (valid) {
 #pragma unroll
-          for (int j = 0; j < kTopK; ++j) *p_at(npoff[j]) = tc::to_bits<T>(nwgt[j]);
+          for (int j = 0; j < kTopK; ++j) *p_at(poff[j]) = tc::to_bits<T>(wgt[j]);
         }
         fence_proxy_async_smem();
       }
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        old_off[j] = (valid && !aborting) ? npoff[j] : 0u;
-        poff[j] = npoff[j];
-        pick[j] = npick[j];
-        wgt[j] = nwgt[j];
-      }
-      done_valid = valid && !aborting;
-      orow = row_ptr(out, os, b, h, valid ? n : n0) + 32 * part;
-      if (r && done_valid) {  // read early; added in the output
-#pragma unroll
-        for (int i = 0; i < 4; ++i) prev[i] = reinterpret_cast<const uint4*>(orow)[i];
-      }
+      for (int j = 0; j < kTopK; ++j) old_off[j] = live ? poff[j] : 0u;
       tc_fence_before();
-      tc::rows_arrive<tc::kBarPhi>();  // MMA_A(i) may start; this tile's score reads are done
+      tc::group_arrive<tc::kBarPhi, tc::kCountP>();  // MMA_A(i) may start
 
-      // round records, by the row's second thread (off the tensor-core path)
-      if (done_valid && part == 1) {
+      // round records (off the tensor-core path)
+      if (live) {
         const size_t trow = ((size_t)r * g.BH + bh) * g.N + n;
         uint32_t lo = 0, hi = 0;
 #pragma unroll
@@ -947,9 +953,46 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
       }
-      if (!kEarlySelect) complete();
+
+      // MMA_A(i) has consumed P_hi and left the attend output in TMEM
+      wait_live(bar_a, ph_a);
+      const bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
+      if (ok) {
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            const uint16_t hb = tc::to_bits<T>(wgt[j]);
+            *p_at(poff[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      tc::group_arrive<tc::kBarPlo, tc::kCountP>();  // MMA_B(i) may start
+      // ---- output: out (+)= O, 64 columns ----
+      if (ok) {
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          float o[32];
+          tmem_ld32(tmem + lane_base + tc::COL_O + 32 * hc, o);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t pk[4];
+              const uint32_t* pv = reinterpret_cast<const uint32_t*>(&prev[4 * hc + i]);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 a = r ? tc::unpack2<T>(pv[e]) : make_float2(0.f, 0.f);
+                pk[e] = tc::pack2<T>(a.x + o[8 * i + 2 * e], a.y + o[8 * i + 2 * e + 1]);
+              }
+              reinterpret_cast<uint4*>(orow)[4 * hc + i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+        }
+      }
+      tc_fence_before();  // the output's TMEM reads come before the next MMA_A
     }
-    if (kEarlySelect && ntiles > 0) complete();
     if (ntiles > 0) wait_live(bar_b, ph_b);
 
     // ---- the segment's partials: TMEM lanes are slots here ----
@@ -958,18 +1001,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int m = 128 * hh + row;
-        float s32[32], wv[16];
-        tmem_ld32(tmem + lane_base + tc::COL_U + tc::kUW * hh + 32 * part, s32);
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          float s32[32];
+          tmem_ld32(tmem + lane_base + tc::COL_U + tc::kUW * hh + 32 * hc, s32);
+          tmem_wait_ld();
+          if (m < g.M) {
+            float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * hc);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
+          }
+        }
+        float wv[16];
         tmem_ld16(tmem + lane_base + tc::COL_U + tc::kUW * hh + 64, wv);
         tmem_wait_ld();
-        if (m < g.M) {
-          float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * part);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
-          if (part == 0) fs.Wpart[po * g.M + m] = wv[0];
-        }
+        if (m < g.M) fs.Wpart[po * g.M + m] = wv[0];
       }
     }
+    tc_fence_before();  // the partials' TMEM reads come before the next segment's MMAs
     }  // segments
   }
   // ---- wind down: wait (bounded) for copies still in flight, free TMEM ----
