@@ -636,7 +636,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     __syncwarp();
     for (int tile = 0; tile < ntiles; ++tile) {
       if (kEarlySelect) {
-        if (tile > 0) mma_b(tile - 1);
+        // the row warps free tile i's scores before the epilogue warps finish tile i-1's weights,
+        // so SELECT(i+1) goes first
         tc::issuer_wait<tc::kBarSfree, tc::kCountS>();  // the scores of tile i are read: SELECT(i+1)
         if (lane == 0 && !*s_abort && tile + 1 < ntiles) {
           tc_fence_after();
@@ -646,6 +647,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
         __syncwarp();
+        if (tile > 0) mma_b(tile - 1);
       }
       tc::issuer_wait<tc::kBarPhi, tc::kCountP>();
       if (lane == 0 && !*s_abort) {
@@ -756,9 +758,19 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         exact_scan = valid && !(thr > -INFINITY);
         scan = valid && !exact_scan;
       }
+      // The second chunk load below is the last read of this tile's scores: a warp with no
+      // exact-scan row frees them for SELECT(i+1) there, so the next tile's scores are computed
+      // while the row warps finish ranking; the others free them after the scan.
+      const bool scan_warp = __any_sync(0xffffffffu, exact_scan);
+      bool s_freed = false;  // warp-uniform
       auto rank_chunks = [&](int c) {  // columns 32c .. 32c+63 of this thread's half
         float x[2][32];
         load2(c, x[0], x[1]);
+        if (kEarlySelect && c == 2 && !scan_warp) {
+          tc_fence_before();
+          tc::group_arrive<tc::kBarSfree, tc::kCountS>();  // SELECT(i+1) may overwrite the scores
+          s_freed = true;
+        }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           uint32_t msk = scan ? tc::ge_mask32(x[k], thr) : 0u;
@@ -799,7 +811,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             tslot[j] = tc::rank_slot(top[j]);
           }
         }
-        if (__any_sync(0xffffffffu, exact_scan)) {
+        if (scan_warp) {
           // Rows with fewer than 7 finite group maxima have fewer than 7 finite scores: causal
           // rows n < 6, lim = n + 1 <= 6 (every column below 7 is in a group of its own). Their
           // picks are all lim finite columns and then the first masked ones in slot order (equal
@@ -822,7 +834,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
       }
-      if (kEarlySelect) {
+      if (kEarlySelect && !s_freed) {
         tc_fence_before();
         tc::group_arrive<tc::kBarSfree, tc::kCountS>();  // SELECT(i+1) may overwrite the scores
       }
