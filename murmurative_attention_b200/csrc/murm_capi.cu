@@ -104,7 +104,7 @@ struct Sizes {
   size_t saved, fwd_ws, bwd_ws;
   // offsets inside each block
   size_t sK, sV, sU, sW, sIdx, sw;
-  size_t fS, fW, fImg;
+  size_t fS, fW, fImg, fCnt;
   size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq, btab;
 };
 
@@ -127,6 +127,7 @@ Sizes make_sizes(const Geom& g) {
   z.fW = take(BH * fparts * M * 4);
   // operand images of the tensor-core path (16-bit dtypes, head_dim 64)
   z.fImg = take(tc_images_bytes(g));
+  z.fCnt = take(2 * BH * sizeof(int));  // the multi-round tensor-core launch's counters per pair
   z.fwd_ws = o;
   o = 0;
   z.bdK0 = take(slot); z.bdK1 = take(slot); z.bdV0 = take(slot); z.bdV1 = take(slot);
@@ -216,7 +217,7 @@ murm_status murm_device_status(void* stream) {
   if (e != cudaSuccess) return cuda_status(e, "murm_device_status");
   if (code)
     return fail(MURM_ERR_DEVICE, "a kernel gave up waiting (error bits 0x%x: 1 operand copy, 2 token tile copy, "
-                "4 tensor-core completion, 8 backward copy or MMA, 16 wait probe)", code);
+                "4 tensor-core completion, 8 backward copy or MMA, 16 wait probe, 32 another CTA's round)", code);
   return MURM_OK;
 }
 
@@ -269,6 +270,7 @@ murm_status forward_entry(const murm_fwd_args* a, void* stream, int slots_f32) {
   fs.Spart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fS);
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fW);
   fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(a->workspace) + z.fImg);
+  fs.counters = reinterpret_cast<int*>(static_cast<char*>(a->workspace) + z.fCnt);
   return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }
 }  // namespace
@@ -403,5 +405,6 @@ extern "C" murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* a,
   fs.Spart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fS);
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fW);
   fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(base) + z.saved + z.fImg);
+  fs.counters = reinterpret_cast<int*>(static_cast<char*>(base) + z.saved + z.fCnt);
   return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }

@@ -169,9 +169,11 @@ struct Saved {
   float* w;      // [R][BH][N][8] softmax weights (7 used)
 };
 struct FwdScratch {
-  float* Spart;     // [BH][parts][M][D] (parts: red_chunks, or ft_parts on the tensor-core path)
+  float* Spart;     // CUDA-core path: [BH][red_chunks][M][D]; tensor-core path: [BH][ft_parts][D/4][M][4]
+                    // (4-column chunks, slot rows contiguous: coalesced stores from the TMEM lanes)
   float* Wpart;     // [BH][parts][M]
   uint8_t* images;  // [BH][3][256][64] 16-bit operand images (tensor-core path)
+  int* counters;    // [2][BH] partials written / finalize shares done (multi-round tensor-core launch)
 };
 struct BwdScratch {
   float* dK[2];  // [BH][M][D] ping-pong slot-key gradients

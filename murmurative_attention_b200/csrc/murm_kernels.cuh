@@ -77,6 +77,35 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     ::murm::launch_end(stream);                                                      \
   } while (0)
 
+// A cooperative launch (every block resident at once, so blocks may wait on each other),
+// also a programmatic dependent of the previous kernel on the stream.
+template <typename... KArgs, typename... Args>
+inline void launch_coop_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+#define MURM_LAUNCH_COOP_PDL(name, kernel, grid, block, smem, stream, ...)                \
+  do {                                                                                    \
+    ::murm::launch_begin(name, stream);                                                   \
+    ::murm::launch_coop_pdl(kernel, dim3(grid), dim3(block), smem, stream, __VA_ARGS__);  \
+    ::murm::launch_end(stream);                                                           \
+  } while (0)
+// True when `blocks` blocks of `kernel` can all be resident on the current device at once and
+// the device supports cooperative launches (murm_profile.cu; cached per kernel and device).
+bool coop_fits(const void* kernel, int threads, int smem, int blocks);
+
 // Opts `kernel` into `bytes` of dynamic shared memory on the current device (murm_profile.cu).
 // The attribute belongs to one device's context, so it is tracked per (kernel, device) and only
 // raised when a launch needs more than was set before; safe to call from several host threads.

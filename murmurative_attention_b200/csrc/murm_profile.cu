@@ -10,6 +10,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "murm_kernels.cuh"
@@ -51,6 +52,25 @@ cudaError_t smem_opt_in_raw(const void* kernel, int bytes) {
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) have = bytes;
   return e;
+}
+
+bool coop_fits(const void* kernel, int threads, int smem, int blocks) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int, int>, int> resident;  // -> blocks resident at once
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(kernel, dev, threads, smem);
+  auto it = resident.find(key);
+  if (it == resident.end()) {
+    int coop = 0, sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess)
+      coop = 0;
+    it = resident.emplace(key, coop ? sms * per_sm : 0).first;
+  }
+  return blocks <= it->second;
 }
 
 void launch_begin(const char* name, cudaStream_t st) {

@@ -69,6 +69,41 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Generic-proxy global-memory writes (another CTA's, seen through an acquire) -> visible to
+// this thread's later async-proxy reads (bulk copies).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// counters in global memory shared by the CTAs of one (co-resident) grid
+// ---------------------------------------------------------------------------
+// Adds `v` with release semantics at GPU scope: the writes this thread made, or saw through a
+// CTA barrier before the call, are visible to a thread that acquires the new value.
+__device__ __forceinline__ void counter_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int counter_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *p >= target (%globaltimer, read once the first poll has failed). Returns
+// false on expiry (the caller records an error and winds down).
+__device__ __forceinline__ bool counter_wait_ge(const int* p, int target, uint64_t limit_ns = kWaitLimitNs) {
+  if (counter_acquire(p) >= target) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (counter_acquire(p) >= target) return true;
+    uint64_t t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > limit_ns) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // programmatic dependent launch
 // ---------------------------------------------------------------------------

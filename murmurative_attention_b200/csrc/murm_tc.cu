@@ -1,4 +1,4 @@
-// murm_tc.cu — tensor-core (tcgen05/TMEM/TMA) forward round for fp16/bf16, head_dim 64.
+// murm_tc.cu — tensor-core (tcgen05/TMEM/TMA) forward rounds for fp16/bf16, head_dim 64.
 //
 // One CTA per SM; the (batch, head) x 128-token tile list is split over them by
 // TileSplit (murm_common.cuh), so a CTA takes a run of tiles that may finish one
@@ -22,8 +22,12 @@
 //      accumulates the slot update sums S += P^T . Q and W += P^T . 1
 //      (reference.py:93-103) over both terms in TMEM across all tiles of the
 //      segment — fp32-level sums, deterministic, no atomics.
-// A segment's S/W partials go to global memory; k_tc_finalize combines the partials
-// of a (batch, head) in token order, applies the EMA and the diffusion.
+// A segment's S/W partials go to global memory. All R rounds run in one cooperative launch:
+// between rounds the CTAs whose runs end in a (batch, head) combine its partials in token
+// order, apply the EMA and the diffusion and write the next round's state and operand images,
+// and the pair's next round starts once its own finalize is done (two counters per pair, no
+// grid-wide barrier); no slot update follows the last round. Without a cooperative launch,
+// one launch per round with k_tc_finalize between them does the same arithmetic.
 //
 // Shared memory (from a 1024-byte aligned base; operand tiles use the 128-byte
 // swizzle, rows of 64 16-bit elements):
@@ -63,7 +67,7 @@ constexpr uint32_t COL_S = 0, COL_U = 256, COL_X = 416, COL_H = 432, COL_O = 448
 constexpr uint32_t kUW = 80;  // columns per half of the slot-sum accumulator
 constexpr uint32_t kQBytes = 128 * 128;
 
-enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4 };
+enum : int { kErrImgWait = 1, kErrQWait = 2, kErrMmaWait = 4, kErrPeerWait = 32 };
 
 // Barrier over the warps that share one TMEM lane quadrant.
 __device__ __forceinline__ void quadrant_sync(int quadrant) {
@@ -73,6 +77,7 @@ __device__ __forceinline__ void quadrant_sync(int quadrant) {
 // and second (6) weight terms are in P (the epilogue warps arrive); the row warps are done reading
 // the tile's scores (7).
 constexpr int kBarPhi = 5, kBarPlo = 6, kBarSfree = 7;
+constexpr int kBarRows = 8, kBarEpi = 9;  // all row warps; all epilogue warps
 constexpr int kCountP = kEpiThreads + 32, kCountS = kRowThreads + 32;
 template <int kId, int kCount>
 __device__ __forceinline__ void issuer_wait() {
@@ -285,13 +290,19 @@ __device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k
 
 // Round-0 state: slot tables (element type S: the dtype of q, or fp32 slot state; strided, batch
 // stride 0 broadcasts) -> fp32 state + images. grid (BH, 256/16): block y covers 16 slot rows,
-// 16 threads each (rows >= M write zero images).
+// 16 threads each (rows >= M write zero images). Also zeroes the pair's two counters of the
+// multi-round forward launch that follows.
 template <typename T, typename S>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const S* sk, Strides3 sks, const S* svv,
-                                                                        Strides3 svs, Saved sv, uint8_t* images) {
-  pdl_wait();  // the previous step's kernels may still read the state and images
+                                                                        Strides3 svs, Saved sv, uint8_t* images,
+                                                                        int* counters) {
+  pdl_wait();  // the previous step's kernels may still read the state, images and counters
   pdl_trigger();
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, l = threadIdx.x & 15;
+  if (blockIdx.y == 0 && threadIdx.x == 0) {
+    counters[bh] = 0;
+    counters[g.BH + bh] = 0;
+  }
   uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
   const int m = blockIdx.y * kSlotRows + (threadIdx.x >> 4);
   float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
@@ -352,7 +363,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
 #pragma unroll
         for (int u = 0; u < kW; ++u) {
           const size_t po = (size_t)bh * g.ft_parts + min(ch + u, nparts - 1);
-          a[u] = tc::ld4(fs.Spart + (po * g.M + m) * tc::kD + 4 * l);
+          a[u] = reinterpret_cast<const float4*>(fs.Spart)[(po * 16 + l) * g.M + m];
           wv[u] = fs.Wpart[po * g.M + m];
         }
 #pragma unroll
@@ -401,19 +412,20 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
 }
 
 // ---------------------------------------------------------------------------
-// The forward round kernel: 8 row warps (thread = token row x half of the slots)
-// and one issuer warp whose lane 0 issues every MMA and copy, so the row warps
-// never stall behind the tensor-core queue.
+// The forward round kernel, rounds [r0, r1): 8 row warps (thread = token row x half of the
+// slots) rank the tiles, 4 epilogue warps (thread = token row) write the weights, the round
+// records and the output, and the issuer warp's lane 0 issues every MMA and copy, so neither
+// stalls behind the tensor-core queue; 3 more warps only give their registers to the row warps.
 //
-// Tensor-core order per tile i:  MMA_A(i) = {O = P_hi.V, S += P_hi^T.Q, W += P_hi^T.1},
-// then SELECT(i+1) (scores of the next tile), then MMA_B(i) = {S += P_lo^T.Q,
-// W += P_lo^T.1}. SELECT(i+1) runs while the row warps write the second weight
-// term and the output of tile i; MMA_B(i) runs while they rank tile i+1.
+// Tensor-core order per tile i (fp16): SELECT(i+1) (scores of the next tile, once the row warps
+// have read tile i's), MMA_B(i-1) = {S += P_lo^T.Q, W += P_lo^T.1}, MMA_A(i) = {O = P_hi.V,
+// S += P_hi^T.Q, W += P_hi^T.1}. The row warps rank tile i+1 while the epilogue warps finish
+// tile i. After the last round no update is issued (no P_lo, no partials).
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(tc::kThreads, 1)
-    k_fwd_tc(Geom g, int r, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
-             float* weights, Saved sv, FwdScratch fs, const uint8_t* images, const __grid_constant__ TileSplit split) {
+    k_fwd_tc(Geom g, int r0, int r1, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
+             float* weights, Saved sv, FwdScratch fs, const __grid_constant__ TileSplit split) {
   using C = tc::Cfg<T>;
   using L = tc::Layout<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -441,6 +453,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // this CTA's run of the flat (b,h) x tile list, one segment per (b,h) it meets
   const int cta = blockIdx.x;
   const int u_end = split.start[cta + 1];
+  int r = r0;               // the round being run; each role steps through [r0, r1)
+  bool last_round = false;  // no slot update follows the last round: no second weight term, no partials
+  // Several rounds in one launch (all CTAs resident: a cooperative launch): between rounds the
+  // CTAs of each pair combine its slot-sum partials themselves, through two counters per pair.
+  const bool multi = r1 - r0 > 1;
+  int* cnt_part = fs.counters;         // [BH] segment partials written, over the launch
+  int* cnt_fin = fs.counters + g.BH;   // [BH] finalize shares done, over the launch
   int bh = 0, b = 0, h = 0, part_idx = 0, t_beg = 0, t_end = 0, ntiles = 0;
   auto set_segment = [&](int u) {  // the segment that starts at unit u
     bh = u / split.tpb;
@@ -501,7 +520,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * quadrant) << 16;
   const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;
-  const bool last_round = (r == g.R - 1);
 
   // mbarrier phases of the row threads (each waits every phase once)
   uint32_t ph_s = 0, ph_a = 0, ph_b = 0;
@@ -573,6 +591,149 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   };
   auto p_at = [&](uint32_t off) -> uint16_t* { return reinterpret_cast<uint16_t*>(sm + off); };
 
+  // ---- between two rounds of one launch: the finalize of a pair, by the row warps ----
+  // The CTAs whose runs end in pair p each take a share of its 256 padded slot rows (a CTA whose
+  // run goes on into the next pair leaves p to the others); a pair whose only CTA runs on
+  // beyond it is finalized by that CTA alone.
+  auto fin_range = [&](int p, int& first, int& count) {
+    first = split.first_cta(p);
+    const int last = split.cta_of(p * split.tpb + split.tpb - 1);
+    count = last - first + (split.start[last + 1] <= (p + 1) * split.tpb ? 1 : 0);
+    if (count == 0) {
+      first = last;
+      count = 1;
+    }
+  };
+  auto rows_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"n"(tc::kBarRows), "n"(tc::kRowThreads) : "memory"); };
+  // Share k of `count` of pair p after round r: once every CTA of p has written its partial,
+  // combine the partials in token order, EMA (reference.py:105-113), diffusion
+  // (reference.py:128-133); write U_r, W_r, the state entering round r+1 and its operand images.
+  // Warp w takes columns 8w..8w+7 of 32 consecutive slot rows, a row per lane (the partials'
+  // loads coalesce); rows base-1 and base+30 (lanes 0 and 31) are recomputed halos, so each pass
+  // gives 30 rows and the diffusion's neighbours are the adjacent lanes.
+  auto fin_share = [&](int p, int k, int count) {
+    const int nparts = split.parts(p);
+    const int done = r - r0;  // rounds of this launch finished before round r
+    if (tid == 0 && !*s_abort) {
+      if (!counter_wait_ge(&cnt_part[p], nparts * (done + 1)) || !counter_wait_ge(&cnt_fin[p], count * done))
+        fail(tc::kErrPeerWait);
+    }
+    rows_sync();
+    if (!*s_abort) {
+      const size_t MD = (size_t)g.M * tc::kD;
+      const size_t cur = ((size_t)r * g.BH + p) * MD, nxt = cur + (size_t)g.BH * MD;
+      uint8_t* img = fs.images + (size_t)p * L::kImages;
+      const int lo = k * tc::kSlotsPad / count, hi = (k + 1) * tc::kSlotsPad / count;
+      const int c8 = warp * 8;  // this warp's first column
+      for (int base = lo; base < hi; base += 30) {
+        const int m = base - 1 + lane;
+        const bool own = lane >= 1 && lane <= 30 && m < hi;
+        float kx[8], vx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kx[i] = vx[i] = 0.f;
+        if (m >= 0 && m < g.M) {
+          const float4* ko = reinterpret_cast<const float4*>(sv.K + cur + (size_t)m * tc::kD + c8);
+          const float4* vo = reinterpret_cast<const float4*>(sv.V + cur + (size_t)m * tc::kD + c8);
+          const float4 k0 = ko[0], k1 = ko[1], v0 = vo[0], v1 = vo[1];
+          float S[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) S[i] = 0.f;
+          float W = 0.f;
+          constexpr int kB = 6;  // partial loads in flight per batch
+          for (int q0 = 0; q0 < nparts; q0 += kB) {  // added in token order
+            float4 a0[kB], a1[kB];
+            float wv[kB];
+#pragma unroll
+            for (int u = 0; u < kB; ++u) {
+              const size_t po = (size_t)p * g.ft_parts + min(q0 + u, nparts - 1);
+              const float4* sp = reinterpret_cast<const float4*>(fs.Spart) + (po * 16 + 2 * warp) * g.M + m;
+              a0[u] = sp[0];
+              a1[u] = sp[g.M];
+              wv[u] = fs.Wpart[po * g.M + m];
+            }
+#pragma unroll
+            for (int u = 0; u < kB; ++u) {
+              if (q0 + u < nparts) {
+                const float a[8] = {a0[u].x, a0[u].y, a0[u].z, a0[u].w, a1[u].x, a1[u].y, a1[u].z, a1[u].w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) S[i] = __fadd_rn(S[i], a[i]);
+                W = __fadd_rn(W, wv[u]);
+              }
+            }
+          }
+          const float den = __fadd_rn(W, kEmaEps);
+          float U[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) U[i] = __fdiv_rn(S[i], den);
+          if (own) {
+            float4* u = reinterpret_cast<float4*>(sv.U + cur + (size_t)m * tc::kD + c8);
+            u[0] = make_float4(U[0], U[1], U[2], U[3]);
+            u[1] = make_float4(U[4], U[5], U[6], U[7]);
+            if (warp == 0) sv.W[((size_t)r * g.BH + p) * g.M + m] = W;
+          }
+          const float ko8[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+          const float vo8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+          const bool hit = W > 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kx[i] = hit ? __fadd_rn(__fmul_rn(g.alpha, ko8[i]), __fmul_rn(g.one_minus_alpha, U[i])) : ko8[i];
+            vx[i] = hit ? __fadd_rn(__fmul_rn(g.alpha, vo8[i]), __fmul_rn(g.one_minus_alpha, U[i])) : vo8[i];
+          }
+        }
+        float kl[8], kr[8], vl[8], vr[8];  // rows m-1 and m+1 (used by lanes 1..30 only)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          kl[i] = __shfl_up_sync(0xffffffffu, kx[i], 1);
+          vl[i] = __shfl_up_sync(0xffffffffu, vx[i], 1);
+          kr[i] = __shfl_down_sync(0xffffffffu, kx[i], 1);
+          vr[i] = __shfl_down_sync(0xffffffffu, vx[i], 1);
+        }
+        if (own) {
+          float kn[8], vn[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) kn[i] = vn[i] = 0.f;  // rows >= M: zero images
+          if (m < g.M) {
+            const bool inner = m > 0 && m < g.M - 1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              kn[i] = inner ? diffuse1(kx[i], kl[i], kr[i], g.gamma) : kx[i];
+              vn[i] = inner ? diffuse1(vx[i], vl[i], vr[i], g.gamma) : vx[i];
+            }
+            float4* kd = reinterpret_cast<float4*>(sv.K + nxt + (size_t)m * tc::kD + c8);
+            float4* vd = reinterpret_cast<float4*>(sv.V + nxt + (size_t)m * tc::kD + c8);
+            kd[0] = make_float4(kn[0], kn[1], kn[2], kn[3]);
+            kd[1] = make_float4(kn[4], kn[5], kn[6], kn[7]);
+            vd[0] = make_float4(vn[0], vn[1], vn[2], vn[3]);
+            vd[1] = make_float4(vn[4], vn[5], vn[6], vn[7]);
+          }
+          // the 8 columns are one 16-byte chunk of each 16-bit image (128-byte swizzle)
+          const uint32_t off = (uint32_t)m * 128 + (((uint32_t)warp ^ ((uint32_t)m & 7)) << 4);
+#pragma unroll
+          for (int sp = 0; sp < C::kSplits; ++sp) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t a = tc::to_bits<T>(kn[2 * i]), b2 = tc::to_bits<T>(kn[2 * i + 1]);
+              kn[2 * i] -= tc::from_bits<T>((uint16_t)a);  // exact in fp32: the next term carries the residual
+              kn[2 * i + 1] -= tc::from_bits<T>((uint16_t)b2);
+              w4[i] = a | (b2 << 16);
+            }
+            *reinterpret_cast<uint4*>(img + sp * tc::kImg + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+          uint32_t w4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) w4[i] = tc::to_bits<T>(vn[2 * i]) | (tc::to_bits<T>(vn[2 * i + 1]) << 16);
+          *reinterpret_cast<uint4*>(img + L::OFF_V + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+    rows_sync();
+    if (tid == 0) {  // even after a failure, so that the pair's other CTAs do not wait out their limit
+      __threadfence();
+      counter_release_add(&cnt_fin[p], 1);
+    }
+  };
+
   // fp16 (three Q buffers) runs SELECT(i+1) ahead of MMA_A(i): the row warps rank tile i+1
   // while MMA_A(i) runs, then finish tile i (second weight term, output). bf16 has one Q
   // buffer, so SELECT(i+1) waits for MMA_B(i) and the row warps finish tile i first.
@@ -611,16 +772,38 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
       __syncwarp();
     };
+    // last round, one Q buffer: no update reads it, so SELECT(i+1) follows MMA_A(i) (the rows
+    // had tile i's scores, so SELECT(i) is complete)
+    auto select_next = [&](int tile_idx) {
+      if (lane == 0 && !*s_abort && tile_idx + 1 < ntiles) {
+        issue_q(tile_idx + 1);
+        if (wait_q(tile_idx + 1)) {
+          issue_select(tile_idx + 1);
+          ++n_s;
+        }
+      }
+      __syncwarp();
+    };
+    for (r = r0; r < r1; ++r) {
+    last_round = r == g.R - 1;
     for (int u = split.start[cta]; u < u_end; u = next_segment()) {
     set_segment(u);
     if (lane == 0 && !*s_abort) {  // segment prologue: operand images, first token tiles, first SELECT
       if (!drain()) {
         fail(tc::kErrMmaWait);
       } else {
-        mbar_arrive_expect_tx(bar_img, L::kImages);
-        bulk_g2s(sm, images + (size_t)bh * L::kImages, L::kImages, bar_img);
-        img_pending = true;
         for (int i = 0; i < C::kQBufs && i < ntiles; ++i) issue_q(i);
+        if (multi && r > r0) {  // the pair's finalize after the previous round is done
+          int first, count;
+          fin_range(bh, first, count);
+          if (!counter_wait_ge(&cnt_fin[bh], count * (r - r0))) fail(tc::kErrPeerWait);
+          fence_proxy_async_global();  // images written by other CTAs, read by the bulk copy below
+        }
+      }
+      if (!*s_abort) {
+        mbar_arrive_expect_tx(bar_img, L::kImages);
+        bulk_g2s(sm, fs.images + (size_t)bh * L::kImages, L::kImages, bar_img);
+        img_pending = true;
         if (!tc::timed_wait(bar_img, img_phase)) {
           fail(tc::kErrImgWait);
         } else {
@@ -647,7 +830,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           }
         }
         __syncwarp();
-        if (tile > 0) mma_b(tile - 1);
+        if (tile > 0 && !last_round) mma_b(tile - 1);
       }
       tc::issuer_wait<tc::kBarPhi, tc::kCountP>();
       if (lane == 0 && !*s_abort) {
@@ -656,17 +839,22 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk)
           mma_f16(tmem + tc::COL_O, d_pk.at((kk >> 2) * 16384 + (kk & 3) * 32), d_v.at(kk * 2048), ID_ATT, kk != 0);
-        issue_update(tile, tile == 0);
+        if (!last_round) issue_update(tile, tile == 0);
         mma_commit(bar_a);
         ++n_a;
-        // the row warps saw MMA_B(i-1) complete before writing P: its Q buffer is free
+        // the epilogue warps saw MMA_B(i-1) complete before writing P (in the last round no update
+        // reads the Q tiles): its Q buffer is free
         if (C::kQBufs > 1 && tile >= 1 && tile - 1 + C::kQBufs < ntiles) issue_q(tile - 1 + C::kQBufs);
       }
       __syncwarp();
-      if (!kEarlySelect) mma_b(tile);
+      if (!kEarlySelect) {
+        if (!last_round) mma_b(tile);
+        else select_next(tile);
+      }
     }
-    if (kEarlySelect && ntiles > 0) mma_b(ntiles - 1);
+    if (kEarlySelect && ntiles > 0 && !last_round) mma_b(ntiles - 1);
     }  // segments
+    }  // rounds
     if (lane == 0) drain();
   } else if (row_warp) {
     // ================= row warps =================
@@ -677,6 +865,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     auto wait_live = [&](uint64_t* bar, uint32_t& ph) {
       if (!*s_abort) wait_bar(bar, ph);
     };
+    for (r = r0; r < r1; ++r) {
+    last_round = r == g.R - 1;
     for (int u = split.start[cta]; u < u_end; u = next_segment()) {
     set_segment(u);
     for (int tile = 0; tile < ntiles; ++tile) {
@@ -865,6 +1055,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       ++hcount;
     }
     }  // segments
+    if (multi && !last_round) {  // this CTA's finalize shares of round r
+      const int p_first = split.start[cta] / split.tpb, p_last = (u_end - 1) / split.tpb;
+      for (int p = p_first; p <= p_last; ++p) {
+        int first, count;
+        fin_range(p, first, count);
+        if (cta >= first && cta < first + count) fin_share(p, cta - first, count);
+      }
+    }
+    }  // rounds
   } else if (epi_warp) {
     // ================= epilogue warps =================
     // One thread per token row (TMEM lane) of its quadrant: the softmax of the row's picks, the
@@ -877,6 +1076,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     auto wait_live = [&](uint64_t* bar, uint32_t& ph) {
       if (!*s_abort) wait_bar(bar, ph);
     };
+    for (r = r0; r < r1; ++r) {
+    last_round = r == g.R - 1;
     for (int u = split.start[cta]; u < u_end; u = next_segment()) {
     set_segment(u);
     for (int tile = 0; tile < ntiles; ++tile) {
@@ -923,8 +1124,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           poff[j] = p_off(pick[j]);
         }
       }
-      // MMA_B(i-1) still reads the previous tile's P entries and Q buffer
-      if (tile > 0) wait_live(bar_b, ph_b);
+      // MMA_B(i-1) still reads the previous tile's P entries and Q buffer (none after the last round)
+      if (tile > 0 && !last_round) wait_live(bar_b, ph_b);
       const bool live = valid && !aborting;
       if (!aborting) {
 #pragma unroll
@@ -969,7 +1170,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       // MMA_A(i) has consumed P_hi and left the attend output in TMEM
       wait_live(bar_a, ph_a);
       const bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
-      if (ok) {
+      if (ok && !last_round) {
         if (valid) {
 #pragma unroll
           for (int j = 0; j < kTopK; ++j) {
@@ -980,7 +1181,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         fence_proxy_async_smem();
       }
       tc_fence_before();
-      tc::group_arrive<tc::kBarPlo, tc::kCountP>();  // MMA_B(i) may start
+      if (!last_round) tc::group_arrive<tc::kBarPlo, tc::kCountP>();  // MMA_B(i) may start
       // ---- output: out (+)= O, 64 columns ----
       if (ok) {
 #pragma unroll
@@ -1005,6 +1206,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
       tc_fence_before();  // the output's TMEM reads come before the next MMA_A
     }
+    if (last_round) continue;  // no slot update follows
     if (ntiles > 0) wait_live(bar_b, ph_b);
 
     // ---- the segment's partials: TMEM lanes are slots here ----
@@ -1018,11 +1220,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           float s32[32];
           tmem_ld32(tmem + lane_base + tc::COL_U + tc::kUW * hh + 32 * hc, s32);
           tmem_wait_ld();
-          if (m < g.M) {
-            float4* dst = reinterpret_cast<float4*>(fs.Spart + (po * g.M + m) * tc::kD + 32 * hc);
+          if (m < g.M) {  // chunk-major: a warp's store of one 4-column chunk covers 32 consecutive rows
+            float4* dst = reinterpret_cast<float4*>(fs.Spart) + (po * 16 + 8 * hc) * g.M + m;
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
+              dst[(size_t)i * g.M] = make_float4(s32[4 * i], s32[4 * i + 1], s32[4 * i + 2], s32[4 * i + 3]);
           }
         }
         float wv[16];
@@ -1032,7 +1234,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       }
     }
     tc_fence_before();  // the partials' TMEM reads come before the next segment's MMAs
+    if (multi) {  // the partial is written: count it for the pair's finalize (even after a failure)
+      asm volatile("bar.sync %0, %1;" ::"n"(tc::kBarEpi), "n"(tc::kEpiThreads) : "memory");
+      if (tid == tc::kRowThreads) {
+        __threadfence();
+        counter_release_add(&cnt_part[bh], 1);
+      }
+    }
     }  // segments
+    }  // rounds
   }
   // ---- wind down: wait (bounded) for copies still in flight, free TMEM ----
   if (issuer_warp && lane == 0) {
@@ -1139,15 +1349,26 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
   if (cudaError_t e = smem_opt_in(k_fwd_tc<T>, tc::Layout<T>::kSmem)) return e;
   if (p.slots_f32)
     MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, float>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
-                    static_cast<const float*>(p.sk), p.sks, static_cast<const float*>(p.sv), p.svs, sv, images);
+                    static_cast<const float*>(p.sk), p.sks, static_cast<const float*>(p.sv), p.svs, sv, images,
+                    fs.counters);
   else
     MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, T>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
-                    static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, sv, images);
+                    static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, sv, images, fs.counters);
   TileSplit split;  // the plan the workspace was sized for (make_geom)
   plan_split(g.BH, g.N, kTile, kMaxSplitCtas, &split);
+  // All rounds in one launch when every CTA can be resident at once (a cooperative launch): the
+  // CTAs wait on each other between rounds. Otherwise one launch per round, with k_tc_finalize
+  // between them. MURM_FWD_LAUNCH_PER_ROUND=1 forces the latter.
+  const char* per_round = getenv("MURM_FWD_LAUNCH_PER_ROUND");
+  if (g.R > 1 && !(per_round && per_round[0] == '1') &&
+      coop_fits(reinterpret_cast<const void*>(k_fwd_tc<T>), tc::kThreads, tc::Layout<T>::kSmem, split.G)) {
+    MURM_LAUNCH_COOP_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st,
+                         g, 0, g.R, qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, split);
+    return cudaGetLastError();
+  }
   for (int r = 0; r < g.R; ++r) {
     MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
-                qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, images, split);
+                r + 1, qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, split);
     if (r + 1 < g.R)
       MURM_LAUNCH_PDL("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs,
                       split);
