@@ -182,7 +182,7 @@ struct BwdScratch {
   float* dW;     // [BH][M]    gradient w.r.t. the weight sum
   float* dKdir;  // [BH][M][D] direct (EMA-kept) part of dK
   float* dVdir;
-  float* dKpart; // [BH][chunks][M][D] (red_chunks, or bwd_chunks on the tensor-core path)
+  float* dKpart; // CUDA-core path: [BH][red_chunks][M][D]; tensor-core path: [BH][bwd_chunks][D/4][M][4]
   float* dVpart;
   float* coef;   // [BH][N][8] scale * dlogit per pick
   float* dq;     // [BH][N][D] running dL/dq over rounds

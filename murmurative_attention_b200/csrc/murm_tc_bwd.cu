@@ -232,11 +232,16 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
   const int rr = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int m = blockIdx.y * kSlotRows - 1 + rr;
   const size_t MD = (size_t)g.M * g.D;
-  // 1. dK_r, dV_r for the block and its halo, every chunk load of a row in flight at once
+  // 1. dK_r, dV_r for the block and its halo, every chunk load of a row in flight at once. Here a
+  // thread takes row m0-1+t%18, columns 4*(t/18).. (consecutive threads, consecutive rows of one
+  // column chunk: the chunk-major partials load coalesced); the rest of the kernel reads the rows
+  // back from shared memory with 16 threads per row.
   {
+    const int rr2 = threadIdx.x % kSlotHalo, l2 = threadIdx.x / kSlotHalo;
+    const int m2 = blockIdx.y * kSlotRows - 1 + rr2;
     float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
-    if (m >= 0 && m < g.M) {
-      const size_t e = bh * MD + (size_t)m * g.D + 4 * l;
+    if (m2 >= 0 && m2 < g.M) {
+      const size_t e = bh * MD + (size_t)m2 * g.D + 4 * l2;
       if (has_dir) {
         k = tcb::ld4(dir_k + e);
         v = tcb::ld4(dir_v + e);
@@ -246,9 +251,10 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
           float4 a[8], c[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const size_t po = ((size_t)bh * g.bwd_chunks + min(ch + u, g.bwd_chunks - 1)) * MD + (size_t)m * g.D + 4 * l;
-            a[u] = tcb::ld4(bs.dKpart + po);
-            c[u] = tcb::ld4(bs.dVpart + po);
+            // chunk partials are chunk-major: [BH][chunks][16 column chunks][M][4]
+            const size_t po = (((size_t)bh * g.bwd_chunks + min(ch + u, g.bwd_chunks - 1)) * 16 + l2) * g.M + m2;
+            a[u] = reinterpret_cast<const float4*>(bs.dKpart)[po];
+            c[u] = reinterpret_cast<const float4*>(bs.dVpart)[po];
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -260,8 +266,8 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
         }
       }
     }
-    skk[rr][l] = k;
-    svv[rr][l] = v;
+    skk[rr2][l2] = k;
+    svv[rr2][l2] = v;
   }
   __syncthreads();
   if (rr < 1 || rr > kSlotRows || m >= g.M) return;  // uniform per half warp
@@ -731,12 +737,14 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       tmem_ld32(tmem + lb + col, a);
       tmem_ld32(tmem + lb + col + 32, c2);
       tmem_wait_ld();
-      if (m < g.M) {
-        float4* dst = reinterpret_cast<float4*>(dst_base + (po * g.M + m) * g.D);
+      if (m < g.M) {  // chunk-major: a warp's store of one 4-column chunk covers 32 consecutive rows
+        float4* dst = reinterpret_cast<float4*>(dst_base) + po * 16 * g.M + m;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+        for (int i = 0; i < 8; ++i)
+          dst[(size_t)i * g.M] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[8 + i] = make_float4(c2[4 * i], c2[4 * i + 1], c2[4 * i + 2], c2[4 * i + 3]);
+        for (int i = 0; i < 8; ++i)
+          dst[(size_t)(8 + i) * g.M] = make_float4(c2[4 * i], c2[4 * i + 1], c2[4 * i + 2], c2[4 * i + 3]);
       }
     }
   }
