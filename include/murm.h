@@ -383,8 +383,9 @@ MURM_API murm_status murm_profile_end(murm_kernel_time* out, int32_t capacity, i
 
 /* Synchronises `stream`, then reads and clears this device's error word, which
  * tensor-core kernels set when a bounded wait gives up (a copy or an MMA that
- * never completed) before they wind down cleanly. Returns MURM_ERR_DEVICE
- * when it was set. */
+ * never completed, or, bit 32, another CTA of the forward's one-launch round
+ * loop that never finished its part of a round) before they wind down cleanly.
+ * Returns MURM_ERR_DEVICE when it was set. */
 MURM_API murm_status murm_device_status(void* stream);
 
 /* Failure-detection probe: launches one block that waits, bounded by limit_ns

@@ -486,7 +486,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     mbar_init(bar_a, 1);
     mbar_init(bar_b, 1);
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&hand_ready[i], 32);  // the quadrant's first row warp (its 32 threads)
+      mbar_init(&hand_ready[i], 64);  // the quadrant's two row warps
       mbar_init(&hand_free[i], 32);   // the quadrant's epilogue warp
     }
     *s_abort = 0;
@@ -976,50 +976,31 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       if (!aborting) {
         rank_chunks(0);
         rank_chunks(2);
-#pragma unroll
-        for (int j = 0; j < kTopK; ++j) xch[j * tc::kRowThreads + tid] = tc::pack_rank(tkey[j], tslot[j]);
       }
-      tc::quadrant_sync(quadrant);
 
-      // pass 3 (both threads of a row, redundantly): merge the two lists
+      // pass 3 (the row's first thread): rows with fewer than 7 finite group maxima
       float mraw[kTopK];  // raw scores of the first masked columns lim..lim+6 (picked by causal rows n < 6)
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) mraw[j] = 0.f;
-      if (!aborting) {
-        if (!exact_scan) {
-          uint64_t other[8], mine[8], top[8];
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) {
-            other[j] = xch[j * tc::kRowThreads + (tid ^ kTile)];
-            mine[j] = tc::pack_rank(tkey[j], tslot[j]);
-          }
-          other[7] = mine[7] = 0;
-          tc::merge8_rank(mine, other, top);
-#pragma unroll
-          for (int j = 0; j < kTopK; ++j) {
-            tkey[j] = tc::rank_score_key(top[j]);
-            tslot[j] = tc::rank_slot(top[j]);
-          }
-        }
-        if (scan_warp) {
-          // Rows with fewer than 7 finite group maxima have fewer than 7 finite scores: causal
-          // rows n < 6, lim = n + 1 <= 6 (every column below 7 is in a group of its own). Their
-          // picks are all lim finite columns and then the first masked ones in slot order (equal
-          // -inf keys, lower slot first), so only columns below lim + 7 <= 13 need a look.
-          float w32[32];
-          tmem_ld32(tmem + lane_base + tc::COL_S, w32);
-          tmem_wait_ld();
-          if (exact_scan) {  // rare path: kept compact (not unrolled)
-            const int mend = min(g.M, lim + kTopK);
+      if (!aborting && part == 0 && scan_warp) {  // warp-uniform
+        // Rows with fewer than 7 finite group maxima have fewer than 7 finite scores: causal
+        // rows n < 6, lim = n + 1 <= 6 (every column below 7 is in a group of its own). Their
+        // picks are all lim finite columns and then the first masked ones in slot order (equal
+        // -inf keys, lower slot first), so only columns below lim + 7 <= 13 (the first thread's
+        // half) need a look.
+        float w32[32];
+        tmem_ld32(tmem + lane_base + tc::COL_S, w32);
+        tmem_wait_ld();
+        if (exact_scan) {  // rare path: kept compact (not unrolled)
+          const int mend = min(g.M, lim + kTopK);
 #pragma unroll 1
-            for (int m = 0; m < mend; ++m) {
-              if (m < lim) {
-                tc::offer7_asc(tkey, tslot, rank_key(w32[m]), m);
-              } else {
+          for (int m = 0; m < mend; ++m) {
+            if (m < lim) {
+              tc::offer7_asc(tkey, tslot, rank_key(w32[m]), m);
+            } else {
 #pragma unroll
-                for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[m] : mraw[j];
-                tc::offer7_asc(tkey, tslot, kNegInfKey, m);
-              }
+              for (int j = 0; j < kTopK; ++j) mraw[j] = (m == lim + j) ? w32[m] : mraw[j];
+              tc::offer7_asc(tkey, tslot, kNegInfKey, m);
             }
           }
         }
@@ -1028,30 +1009,46 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         tc_fence_before();
         tc::group_arrive<tc::kBarSfree, tc::kCountS>();  // SELECT(i+1) may overwrite the scores
       }
-      if (part == 0) {  // warp-uniform: the quadrant's first row warp hands the row over
+      // hand-over to the quadrant's epilogue warp, which merges the row's two lists: the first
+      // thread's through TMEM (keys, packed slots; an exact-scan row's final picks and scores,
+      // flagged), the second thread's through shared memory; the epilogue warp has read the
+      // previous tile's
+      if (hcount > 0 && !*s_abort && !tc::timed_wait(&hand_free[quadrant], (hcount - 1) & 1)) fail(tc::kErrMmaWait);
+      if (part == 0) {  // warp-uniform
         uint32_t hv[16];
+        uint32_t s0 = 0, s1 = 0;
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) {
-          const int pk = (valid && !aborting) ? tslot[j] : 0;
-          // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
+          const uint32_t pk = (valid && !aborting) ? (uint32_t)tslot[j] : 0u;
+          if (j < 4) s0 |= pk << (8 * j);
+          else s1 |= pk << (8 * (j - 4));
           const uint32_t kk = tkey[j];
-          float sc = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
-          if (pk >= lim) {
+          if (exact_scan) {  // masked picks (causal rows n < 6) attend with their real score (reference.py:61)
+            float sc = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk);
+            if ((int)pk >= lim) {
 #pragma unroll
-            for (int k2 = 0; k2 < kTopK; ++k2) sc = (pk == lim + k2) ? mraw[k2] : sc;
+              for (int k2 = 0; k2 < kTopK; ++k2) sc = ((int)pk == lim + k2) ? mraw[k2] : sc;
+            }
+            hv[j] = __float_as_uint(sc);
+          } else {
+            hv[j] = kk;
           }
-          hv[j] = (uint32_t)pk;
-          hv[kTopK + j] = __float_as_uint(sc);
+          if (!valid || aborting) hv[j] = 0u;  // score 0 (the row is not written)
         }
-        hv[14] = hv[15] = 0u;
-        // the epilogue warp has read the previous tile's hand-over
-        if (hcount > 0 && !*s_abort && !tc::timed_wait(&hand_free[quadrant], (hcount - 1) & 1)) fail(tc::kErrMmaWait);
+        hv[7] = s0;
+        hv[8] = s1;
+        hv[9] = (exact_scan || !valid || aborting) ? 1u : 0u;  // 1: the list is final (no merge)
+#pragma unroll
+        for (int j = 10; j < 16; ++j) hv[j] = 0u;
         tc_fence_after();
         tmem_st16(tmem + lane_base + tc::COL_H, hv);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&hand_ready[quadrant]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) xch[j * kTile + row] = tc::pack_rank(tkey[j], tslot[j]);
       }
+      mbar_arrive(&hand_ready[quadrant]);
       ++hcount;
     }
     }  // segments
@@ -1097,16 +1094,36 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       float hf[16];
       tmem_ld16(tmem + lane_base + tc::COL_H, hf);
       tmem_wait_ld();
+      uint64_t other[8];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) other[j] = xch[j * kTile + row];
       tc_fence_before();
       mbar_arrive(&hand_free[quadrant]);
       const bool aborting = __any_sync(0xffffffffu, *s_abort != 0);  // warp-uniform
       int pick[kTopK];
       float wgt[kTopK];
       uint32_t poff[kTopK];
+      {
+        const uint32_t s0 = __float_as_uint(hf[7]), s1 = __float_as_uint(hf[8]);
+        uint64_t mine[8], top[8];
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        pick[j] = (int)__float_as_uint(hf[j]);
-        wgt[j] = hf[kTopK + j] * g.scale;
+        for (int j = 0; j < kTopK; ++j) {
+          pick[j] = (int)(((j < 4 ? s0 : s1) >> (8 * (j & 3))) & 0xffu);
+          mine[j] = tc::pack_rank(__float_as_uint(hf[j]), pick[j]);
+        }
+        if (__float_as_uint(hf[9]) != 0u) {  // final list: an exact-scan row's picks and scores
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) wgt[j] = hf[j] * g.scale;
+        } else {  // merge the two threads' lists: the row's top 7, ties to the lower slot
+          other[7] = mine[7] = 0;
+          tc::merge8_rank(mine, other, top);
+#pragma unroll
+          for (int j = 0; j < kTopK; ++j) {
+            const uint32_t kk = tc::rank_score_key(top[j]);
+            pick[j] = tc::rank_slot(top[j]);
+            wgt[j] = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk) * g.scale;
+          }
+        }
       }
       {
         // softmax with the hardware exponential and one reciprocal: the weights enter P as
