@@ -55,12 +55,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "slot_murmurate fwd+bwd tokens/s at N=8192, 1/2/4/8 B200; % of roofline"
 WL = dict(B=1, H=16, N=8192, D=64, M=256, R=3, causal=False)
-DTYPE = torch.float16
+DTYPE = torch.float16  # --dtype bf16 switches the north-star workload to bfloat16 inputs
+DTYPE_NAME = "fp16"
 ESIZE = 2
 
 
 def workload_config(extra=None):
-    cfg = {"workload": "northstar: BASELINE configs[1] inputs (fp16 q~N(0,1) [1,16,8192,64], slots_k~N(0,1) "
+    cfg = {"workload": f"northstar: BASELINE configs[1] inputs ({DTYPE_NAME} q~N(0,1) [1,16,8192,64], slots_k~N(0,1) "
                        "[1,16,256,64], slots_v=0) with backward (grad_out~N(0,1)); R=3, k=7, non-causal",
            "batch_per_rank": WL["B"], "heads": WL["H"], "tokens": WL["N"], "head_dim": WL["D"], "slots": WL["M"],
            "rounds": WL["R"], "top_k": 7, "causal": WL["causal"],
@@ -401,7 +402,7 @@ def run_ours(args):
                  "note": "T_roof = max(bytes/HBM, select FLOPs/tensor peak) per rank, measured peaks"}
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME, "data": "synthetic",
             "config": workload_config({"parallelism": f"(batch,head)-sharded weak scaling, {world} rank(s)",
                                        "timing": "CUDA graph replay" if graph_used else "eager launches"}),
             "roofline": roof, "step_roofline": step_roof, "e2e": e2e, "e2e_autograd": e2e_autograd,
@@ -539,18 +540,21 @@ def roofline(prof, prof_steps, peaks):
     # ncu capture of the same kernel (static, labelled as such), not from this run
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic_northstar.json")
-    if os.path.exists(tpath):
+    if os.path.exists(tpath) and DTYPE_NAME == "fp16":
         with open(tpath) as f:
             traffic = json.load(f).get(name)
     traffic_source = ("static: dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu capture "
-                      "recorded in profiles/traffic_northstar.json, not measured in this run")
+                      "recorded in profiles/traffic_northstar.json, not measured in this run"
+                      if DTYPE_NAME == "fp16" else "no ncu capture of the bf16 kernels recorded")
     if name.startswith("select"):
-        flops = select_flops_per_round()  # one round per launch
+        # the forward runs all R rounds in one launch (one launch per round on the fallback path)
+        rounds_per_launch = WL["R"] * prof_steps / launches
+        flops = select_flops_per_round() * rounds_per_launch
         achieved = flops / (avg_ms / 1e3) / 1e12
         return {"kernel": name, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                 "peak_source": f"{peaks['source']} (burst dense bf16)",
-                "work_per_launch": f"select GEMM 2*M*d*tokens = {flops:.4g} FLOP",
+                "work_per_launch": f"select GEMM 2*M*d*tokens per round x {rounds_per_launch:g} rounds = {flops:.4g} FLOP",
                 "avg_launch_ms": round(avg_ms, 5), "launches": launches, "traffic_source": traffic_source}
     # memory-bound kernels: algorithmic bytes of the whole step spread over its launches
     per_launch = algorithmic_bytes() / (launches / prof_steps)
@@ -857,6 +861,8 @@ def main():
     ap.add_argument("--skip-layer", action="store_true", help="omit the configs[3] layer-step leg")
     ap.add_argument("--skip-widening", action="store_true",
                     help="omit the sequence-parallel, op-surface and decode legs")
+    ap.add_argument("--dtype", choices=("fp16", "bf16"), default="fp16",
+                    help="input dtype of the north-star workload (BASELINE configs[1] is fp16)")
     ap.add_argument("--workload", choices=("northstar", "layer", "surface", "decode", "sp"), default="northstar",
                     help="layer: BASELINE configs[3], the data-parallel layer training step; "
                          "surface: the reference's 6-argument op through the per-phase kernels; "
@@ -864,6 +870,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    global DTYPE, DTYPE_NAME
+    DTYPE, DTYPE_NAME = (torch.bfloat16, "bf16") if args.dtype == "bf16" else (torch.float16, "fp16")
     if args.workload != "northstar":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference arm here"}))
