@@ -105,7 +105,7 @@ struct Sizes {
   // offsets inside each block
   size_t sK, sV, sU, sW, sIdx, sw;
   size_t fS, fW, fImg, fCnt;
-  size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq, btab;
+  size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq, btab, bamax;
 };
 
 Sizes make_sizes(const Geom& g) {
@@ -138,6 +138,7 @@ Sizes make_sizes(const Geom& g) {
   z.bcoef = take(BH * N * 8 * 4);
   z.bdq = take(BH * N * D * 4);
   z.btab = take(tc_bwd_tables_bytes(g));
+  z.bamax = take(BH * 64 * sizeof(float));
   z.bwd_ws = o;
   return z;
 }
@@ -318,6 +319,7 @@ murm_status murm_slot_murmurate_bwd(const murm_bwd_args* a, void* stream) {
   bs.dKpart = reinterpret_cast<float*>(w + z.bdKpart); bs.dVpart = reinterpret_cast<float*>(w + z.bdVpart);
   bs.coef = reinterpret_cast<float*>(w + z.bcoef); bs.dq = reinterpret_cast<float*>(w + z.bdq);
   bs.tables = reinterpret_cast<uint8_t*>(w + z.btab);
+  bs.amax = reinterpret_cast<float*>(w + z.bamax);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   const bool tc = tc_backward_supported(g, g.dtype, p);

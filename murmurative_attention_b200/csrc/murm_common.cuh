@@ -187,6 +187,7 @@ struct BwdScratch {
   float* coef;   // [BH][N][8] scale * dlogit per pick
   float* dq;     // [BH][N][D] running dL/dq over rounds
   uint8_t* tables;  // [BH][3][256][64] 16-bit K, V, dS of a round + [BH][256] fp32 dW (tensor-core path)
+  float* amax;      // [BH][64] bf16 tensor-core path: block maxima of |q| (0..31) and |grad_out| (32..63)
 };
 
 }  // namespace murm

@@ -92,9 +92,9 @@ __device__ __forceinline__ float dot8<__nv_bfloat16>(const uint4& a, const uint4
 }
 #undef MURM_DOT8
 
-// acc[i] += x * row_i over eight 16-bit values. fp16: x is rounded to fp16 and each
-// product taken by an fp32 fma on the 16-bit operands (the precision the fp16 scatter
-// MMAs use for the same weights); bf16: the row is converted and x kept in fp32.
+// acc[i] += x * row_i over eight 16-bit values, each product an fp32 fma on 16-bit operands.
+// fp16: x rounded to fp16 (the precision the fp16 scatter MMAs use for the same weights); bf16:
+// x as two bf16 terms, which keeps x's rounding well below the bf16 rows' own.
 template <typename T>
 __device__ __forceinline__ void axpy8(float x, const uint4& row, float (&acc)[8]);
 template <>
@@ -111,9 +111,51 @@ __device__ __forceinline__ void axpy8<__half>(float x, const uint4& row, float (
 }
 template <>
 __device__ __forceinline__ void axpy8<__nv_bfloat16>(float x, const uint4& row, float (&acc)[8]) {
-  const __nv_bfloat16* t = reinterpret_cast<const __nv_bfloat16*>(&row);
+  // x as two bf16 terms (16 significant bits), each product an fp32 fma on the 16-bit operands
+  const __nv_bfloat16 xh = __float2bfloat16_rn(x);
+  const uint16_t h0 = __bfloat16_as_ushort(xh), h1 = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(xh)));
+  asm("{\n .reg .b16 r0, r1;\n"
+      " mov.b32 {r0, r1}, %10;\n fma.rn.f32.bf16 %0, %8, r0, %0;\n fma.rn.f32.bf16 %1, %8, r1, %1;\n"
+      " fma.rn.f32.bf16 %0, %9, r0, %0;\n fma.rn.f32.bf16 %1, %9, r1, %1;\n"
+      " mov.b32 {r0, r1}, %11;\n fma.rn.f32.bf16 %2, %8, r0, %2;\n fma.rn.f32.bf16 %3, %8, r1, %3;\n"
+      " fma.rn.f32.bf16 %2, %9, r0, %2;\n fma.rn.f32.bf16 %3, %9, r1, %3;\n"
+      " mov.b32 {r0, r1}, %12;\n fma.rn.f32.bf16 %4, %8, r0, %4;\n fma.rn.f32.bf16 %5, %8, r1, %5;\n"
+      " fma.rn.f32.bf16 %4, %9, r0, %4;\n fma.rn.f32.bf16 %5, %9, r1, %5;\n"
+      " mov.b32 {r0, r1}, %13;\n fma.rn.f32.bf16 %6, %8, r0, %6;\n fma.rn.f32.bf16 %7, %8, r1, %7;\n"
+      " fma.rn.f32.bf16 %6, %9, r0, %6;\n fma.rn.f32.bf16 %7, %9, r1, %7;\n}"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+        "+f"(acc[7])
+      : "h"(h0), "h"(h1), "r"(row.x), "r"(row.y), "r"(row.z), "r"(row.w));
+}
+
+// bf16 operands of the scatter MMAs as fp16 under a per-(b,h) power-of-two scale s: the largest
+// |x| of the pair maps into [2^14, 2^15), so every bf16 value of the pair (8 significant bits)
+// converts exactly unless it lies below 2^-39 of the largest (an fp16 subnormal, rounded).
+__device__ __forceinline__ float absmax8_bf16(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = fmaf(x, __bfloat162float(t[i]), acc[i]);
+  for (int i = 0; i < 4; ++i)
+    m = fmaxf(m, fmaxf(__uint_as_float((w[i] & 0x7FFFu) << 16), __uint_as_float(w[i] & 0x7FFF0000u)));
+  return m;
+}
+__device__ __forceinline__ uint4 bf16_to_f16_scaled(const uint4& u, float s) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(w[i] << 16) * s, hi = __uint_as_float(w[i] & 0xFFFF0000u) * s;
+    o[i] = (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+// 2^e for e in [-126, 126] (exact)
+__device__ __forceinline__ float pow2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+// the scale exponent for a pair whose largest |x| is m: m * 2^e in [2^14, 2^15)
+__device__ __forceinline__ int scale_exp(float m) {
+  if (!(m > 0.f)) return 0;
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
+  return max(-126, min(126, 14 - ex));
 }
 
 template <typename T> struct Fmt;
@@ -331,12 +373,42 @@ __global__ void __launch_bounds__(tcb::kRowLanes * kSlotHalo, 2)
   *reinterpret_cast<uint2*>(tab + tcb::OFF_DS + off) = tcb::pack4<T>(dS);
 }
 
-// Tables of the last round (no slot gradient flows into it): K, V; dS = 0, dW = 0.
+// Tables of the last round (no slot gradient flows into it): K, V; dS = 0, dW = 0. For bf16 also
+// the maxima of |q| and |grad_out| over block y's 1/32 of the pair's tokens (the token kernel's
+// operand scales).
 template <typename T>
-__global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8_t* tables, float* dWpad) {
+__global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8_t* tables, float* dWpad, const T* q,
+                                                         Strides3 qs, const T* go, Strides3 gos, float* amax) {
   pdl_wait();
   pdl_trigger();
   const int bh = blockIdx.x;
+  if constexpr (tcb::Fmt<T>::v == 1) {
+    __shared__ float red[2][8];
+    const int b = bh / g.H, h = bh - b * g.H;
+    const int n0 = (int)((int64_t)g.N * blockIdx.y / gridDim.y), n1 = (int)((int64_t)g.N * (blockIdx.y + 1) / gridDim.y);
+    float mq = 0.f, mg = 0.f;
+    for (int e = threadIdx.x; e < (n1 - n0) * 8; e += blockDim.x) {
+      const int n = n0 + (e >> 3), c = (e & 7) * 8;
+      mq = fmaxf(mq, tcb::absmax8_bf16(*reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n) + c)));
+      mg = fmaxf(mg, tcb::absmax8_bf16(*reinterpret_cast<const uint4*>(row_ptr(go, gos, b, h, n) + c)));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+      mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+      red[0][threadIdx.x >> 5] = mq;
+      red[1][threadIdx.x >> 5] = mg;
+    }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, red[threadIdx.x][i]);
+      amax[(size_t)bh * 64 + 32 * threadIdx.x + blockIdx.y] = m;
+    }
+  }
   const size_t st = ((size_t)(g.R - 1) * g.BH + bh) * g.M * g.D;
   uint8_t* tab = tables + (size_t)bh * tcb::kTables;
   for (int e = blockIdx.y * blockDim.x + threadIdx.x; e < tcb::kSlotsPad * 32; e += gridDim.y * blockDim.x) {
@@ -395,7 +467,6 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   const bool math_thread = tid < tcb::kIssuer;
   const int grp = lane >> 3, c8 = lane & 7;
   const int tok = 4 * warp + grp;  // the token of this lane group within a tile (math warps)
-  constexpr uint32_t ID_UPD = idesc_f16(tcb::Fmt<T>::v, 128, 64, 1, 1);
 
   if (tid == tcb::kIssuer) {
     mbar_init(bar_tab, 1);
@@ -426,6 +497,36 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   uint32_t ph_mma = 0;
+  // Scatter operands. fp16: as they are. bf16: as fp16 under the pair's power-of-two scales (the
+  // q and grad_out tiles converted in place once loaded, each math thread its own 16-byte chunk,
+  // the weights and coefficients one fp16 term), unless the pair's largest |q| or |grad_out|
+  // exceeds 2^8: then bf16 operands with two terms per weight and coefficient.
+  constexpr bool kBf16 = tcb::Fmt<T>::v == 1;
+  bool f16ops = true;
+  float sq = 1.f, sg = 1.f;  // operand scales of the q and grad_out tiles
+  if constexpr (kBf16) {
+    float* smax = reinterpret_cast<float*>(sm + tcb::OFF_MISC + 104);
+    if (warp == 0) {
+      float mq = bs.amax[(size_t)bh * 64 + lane], mg = bs.amax[(size_t)bh * 64 + 32 + lane];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+        mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+      }
+      if (lane == 0) {
+        smax[0] = mq;
+        smax[1] = mg;
+      }
+    }
+    __syncthreads();
+    f16ops = smax[0] <= 256.f && smax[1] <= 256.f;  // false for inf / NaN maxima too
+    if (f16ops) {
+      sq = tcb::pow2i(tcb::scale_exp(smax[0]));
+      sg = tcb::pow2i(tcb::scale_exp(smax[1]));
+    }
+  }
+  const bool convert_tiles = kBf16 && f16ops;
+  const uint32_t id_upd = idesc_f16(f16ops ? 0u : tcb::Fmt<T>::v, 128, 64, 1, 1);
   // the issuer's bookkeeping of asynchronous copies: the last tile issued / waited for
   int q_issued = -1, g_issued = -1, w_issued = -1, q_done = -1, g_done = -1, w_done = -1;
   bool tab_pending = false;
@@ -487,7 +588,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       for (int kk = 0; kk < kBT / 16; ++kk)
         mma_f16(tmem + col + 64 * hh,
                 smem_desc(a_p + 2 * hh * tcb::kPBlock + kk * 2048, tcb::kPBlock, 1024, kSwizzle128B),
-                smem_desc(a_b + kk * 2048, tcb::kTileBytes, 1024, kSwizzle128B), ID_UPD,
+                smem_desc(a_b + kk * 2048, tcb::kTileBytes, 1024, kSwizzle128B), id_upd,
                 (first_acc && kk == 0) ? 0u : 1u);
   };
   auto wait_mma = [&]() {
@@ -517,15 +618,15 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
   //   bf16: weights and coefficients go in as two terms each (hi = rn(x), lo = rn(x - hi)),
   //         since bf16 alone rounds them to 2^-9: dV_hi during the math, then dV_lo, dK_hi, dK_lo.
   // The last phase is issued with the next tile's first (and is waited for with it).
-  constexpr int kTerms = tcb::Fmt<T>::v == 1 ? 2 : 1;
-  auto hi_bits = [](float x) -> uint16_t { return tcb::bits<T>(x); };
+  const int terms = f16ops ? 1 : 2;
+  auto hi_bits = [&](float x) -> uint16_t { return f16ops ? tcb::bits<__half>(x) : tcb::bits<T>(x); };
   auto lo_bits = [](float x) -> uint16_t {
     const uint16_t hb = tcb::bits<T>(x);
     return tcb::bits<T>(x - Elem<T>::load(reinterpret_cast<const T*>(&hb)));
   };
   auto pick_of = [](uint2 pk, int j) -> int { return (int)(((j < 4 ? pk.x : pk.y) >> (8 * (j & 3))) & 0xffu); };
   auto last_phase = [&](int j) {  // issuer: the deferred last scatter of tile j (fp16 dK; bf16 dK_lo)
-    issue_scatter(p_addr(j), q_addr(j), tcb::COL_DK, j == 0 && kTerms == 1);
+    issue_scatter(p_addr(j), q_addr(j), tcb::COL_DK, j == 0 && terms == 1);
   };
   // picks of this lane group's token of a tile
   auto fetch_ix = [&](int j) -> uint2 {
@@ -567,8 +668,27 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     else oslot0 = ns;
   };
 
+  // bf16 with fp16 operands: this thread's 16-byte chunk (row tok, chunk c8) of tile j's q and
+  // grad_out, kept as loaded for the token math and written back as fp16 under the pair's scales
+  uint4 qreg = make_uint4(0u, 0u, 0u, 0u), greg = qreg;
+  auto convert = [&](int j) {  // math threads
+    if (!tcb::timed_wait(&bar_q[j % 3], (j / 3) & 1) || !tcb::timed_wait(&bar_g[j % 3], (j / 3) & 1)) {
+      atomicOr(&g_device_error, tcb::kErrWait);
+      *s_abort = 1;
+      return;
+    }
+    const uint32_t rw = (uint32_t)tok * 128 + (((uint32_t)c8 ^ (tok & 7)) << 4);
+    uint4* pq = reinterpret_cast<uint4*>(sm + tcb::OFF_Q + (j % 3) * tcb::kTileBytes + rw);
+    uint4* pg = reinterpret_cast<uint4*>(sm + tcb::OFF_G + (j % 3) * tcb::kTileBytes + rw);
+    qreg = *pq;
+    greg = *pg;
+    *pq = tcb::bf16_to_f16_scaled(qreg, sq);
+    *pg = tcb::bf16_to_f16_scaled(greg, sg);
+  };
+
   fetch_prev(0);
   if (math_thread && ntiles > 0) records(0, fetch_ix(0));
+  if (convert_tiles && math_thread && ntiles > 0) convert(0);
   if (gw && first && ntiles > 0) fill_tgw(0);
   uint2 rq = fetch_ix(1);  // picks for the next records
   if (tid == tcb::kIssuer && ntiles > 0) {
@@ -600,7 +720,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     }
 
     // ---- token math: 8 lanes per token (8 head dims per lane), 4 tokens per warp ----
-    const uint8_t* sq = sm + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
+    const uint8_t* sq_t = sm + tcb::OFF_Q + (tile % 3) * tcb::kTileBytes;
     const uint8_t* sgo = sm + tcb::OFF_G + (tile % 3) * tcb::kTileBytes;
     const uint2* tix = tix_of(tile);
     const float* tw = tw_of(tile);
@@ -620,8 +740,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       w[0] = w0.x; w[1] = w0.y; w[2] = w0.z; w[3] = w0.w; w[4] = w1.x; w[5] = w1.y; w[6] = w1.z;
       // swizzled 128-byte rows of the TMA tiles: 16-byte chunk c8 of row t
       const uint32_t rw = (uint32_t)t * 128 + (((uint32_t)c8 ^ (t & 7)) << 4);
-      const uint4 qv = *reinterpret_cast<const uint4*>(sq + rw);
-      const uint4 gv = *reinterpret_cast<const uint4*>(sgo + rw);
+      const uint4 qv = convert_tiles ? qreg : *reinterpret_cast<const uint4*>(sq_t + rw);
+      const uint4 gv = convert_tiles ? greg : *reinterpret_cast<const uint4*>(sgo + rw);
       float dq[8] = {pv0.x, pv0.y, pv0.z, pv0.w, pv1.x, pv1.y, pv1.z, pv1.w};
       float part[8];
 #pragma unroll
@@ -673,7 +793,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       for (int j = 0; j < kTopK; ++j)
         if (c8 == j) { wl = w[j]; cl = c[j]; ml = ix[j]; }
       coef[tok * 8 + c8] = cl;
-      *p_entry(tile, tok, ml) = kTerms == 1 ? hi_bits(cl) : lo_bits(wl);
+      *p_entry(tile, tok, ml) = terms == 1 ? hi_bits(cl) : lo_bits(wl);
     }
     // the next tile's weights into P[(tile+1) & 1] (free: tile-1's dK is done)
     if (math_thread && tile + 1 < ntiles) {
@@ -684,8 +804,8 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
 
     // ---- bf16: dV_lo, dK_hi (the last phase, dK_lo, is issued with the next tile's first) ----
 #pragma unroll 1
-    for (int ph = 1; ph < 2 * kTerms - 1; ++ph) {
-      const bool is_k = ph >= kTerms;
+    for (int ph = 1; ph < 2 * terms - 1; ++ph) {
+      const bool is_k = ph >= terms;
       if (ph >= 2 && math_thread && tok < nt && c8 < kTopK) {  // P takes the coefficient's high term
         *p_entry(tile, tok, pick_of(tix[tok], c8)) = hi_bits(coef[tok * 8 + c8]);
       }
@@ -696,19 +816,20 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       if (stop) break;
       if (tid == tcb::kIssuer) {
         issue_scatter(p_addr(tile), is_k ? q_addr(tile) : g_addr(tile), is_k ? tcb::COL_DK : tcb::COL_DV,
-                      tile == 0 && is_k && ph == kTerms);
+                      tile == 0 && is_k && ph == terms);
         mma_commit(bar_mma);
       }
       wait_mma();
     }
     if (stop) break;
-    if (kTerms == 2 && math_thread && tok < nt && c8 < kTopK)  // bf16: the coefficient's low term
+    if (terms == 2 && math_thread && tok < nt && c8 < kTopK)  // bf16: the coefficient's low term
       *p_entry(tile, tok, pick_of(tix[tok], c8)) = lo_bits(coef[tok * 8 + c8]);
     if (tid == tcb::kIssuer && tile + 1 < ntiles) {  // the next tile's copies (issued two tiles ago)
       wait_copy(&bar_q[(tile + 1) % 3], tile + 1, q_done);
       wait_copy(&bar_g[(tile + 1) % 3], tile + 1, g_done);
       wait_copy(&bar_w[(tile + 1) % 3], tile + 1, w_done);
     }
+    if (convert_tiles && math_thread && tile + 1 < ntiles) convert(tile + 1);  // published by the next barrier
   }
 
   // the last tile's last scatter, once its P entries are written; every scatter finished before
@@ -728,6 +849,7 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
     const uint32_t lb = (uint32_t)(32 * quad) << 16;
     const bool is_k = warp >= 4;
     float* dst_base = is_k ? bs.dKpart : bs.dVpart;
+    const float unscale = 1.f / (is_k ? sq : sg);  // a power of two: exact
     const size_t po = (size_t)bh * g.bwd_chunks + chunk;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -737,6 +859,11 @@ __global__ void __launch_bounds__(tcb::kThreads, 1)
       tmem_ld32(tmem + lb + col, a);
       tmem_ld32(tmem + lb + col + 32, c2);
       tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        a[i] *= unscale;
+        c2[i] *= unscale;
+      }
       if (m < g.M) {  // chunk-major: a warp's store of one 4-column chunk covers 32 consecutive rows
         float4* dst = reinterpret_cast<float4*>(dst_base) + po * 16 * g.M + m;
 #pragma unroll
@@ -809,7 +936,9 @@ cudaError_t bwd_tc(const Geom& g, const BwdPtrs& p, const Saved& sv, const BwdSc
   uint8_t* tables = bs.tables;
   float* dWpad = reinterpret_cast<float*>(tables + (size_t)g.BH * tcb::kTables);
   const int slot_blocks = (g.M + kSlotRows - 1) / kSlotRows;
-  MURM_LAUNCH_PDL("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad);
+  static_assert(tcb::kSlotsPad * 32 / 256 == 32, "32 blocks per pair: the token kernel reads 32 maxima of each");
+  MURM_LAUNCH_PDL("bwd_tables", k_bwd_tables_last<T>, dim3(g.BH, tcb::kSlotsPad * 32 / 256), 256, 0, st, g, sv, tables, dWpad,
+                  static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, bs.amax);
   for (int r = g.R - 1; r >= 0; --r) {
     MURM_LAUNCH_PDL("bwd_tokens_tc", k_bwd_tokens_tc<T>, dim3(g.bwd_chunks, g.BH), tcb::kThreads, tcb::kSmem, st, g, r,
                 qmap, gmap, static_cast<const T*>(p.q), p.qs, static_cast<const T*>(p.go), p.gos, p.gw,

@@ -112,6 +112,26 @@ def test_matches_oracle_seeded(B, H, N, D, M, R, causal, dt):
     protocol_b(q, sk, sv, R, causal, res, go, gw, tol=TOL[dt])
 
 
+@pytest.mark.parametrize("gscale", [1.0, 512.0])
+def test_bf16_backward_operand_paths(gscale):
+    """The bf16 backward's scatter operands: q and grad_out tiles as fp16 under the pair's
+    power-of-two scales while their largest magnitudes stay within 2^8 (gscale 1), two bf16 terms
+    per weight and coefficient beyond that (gscale 512: grad_out up to ~2500). The backward is
+    linear in grad_out and the weights' gradient, so the GPU's gradients for the scaled ones,
+    divided by the (power-of-two) scale, are compared with the oracle's for the unscaled ones."""
+    g = torch.Generator().manual_seed(4242)
+    B, H, N, M, R = 1, 3, 640, 128, 3
+    q = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16)
+    sk = torch.randn(B, H, M, 64, generator=g).to(torch.bfloat16)
+    sv = (torch.randn(B, H, M, 64, generator=g) * 0.3).to(torch.bfloat16)
+    go = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16)
+    gw = torch.randn(B, H, N, 7, generator=g)
+    res = gpu_run(q, sk, sv, R, True, (go.float() * gscale).to(torch.bfloat16), gw * gscale)
+    for k in ("grad_q", "grad_sk", "grad_sv"):
+        res[k] = res[k] / gscale
+    protocol_b(q, sk, sv, R, True, res, go, gw, tol=TOL[torch.bfloat16])
+
+
 @pytest.mark.parametrize("B,H,N,M,causal", [(1, 150, 256, 64, False)])
 def test_forward_runs_spanning_pairs_bf16(B, H, N, M, causal):
     """bf16 forward where every CTA's run spans two (b,h) pairs: out / indices / weights. Cases of
