@@ -104,7 +104,7 @@ struct Sizes {
   size_t saved, fwd_ws, bwd_ws;
   // offsets inside each block
   size_t sK, sV, sU, sW, sIdx, sw;
-  size_t fS, fW, fImg, fCnt;
+  size_t fS, fW, fImg, fCnt, fAmax, fExp;
   size_t bdK0, bdK1, bdV0, bdV1, bdS, bdW, bdKdir, bdVdir, bdKpart, bdVpart, bcoef, bdq, btab, bamax;
 };
 
@@ -128,6 +128,8 @@ Sizes make_sizes(const Geom& g) {
   // operand images of the tensor-core path (16-bit dtypes, head_dim 64)
   z.fImg = take(tc_images_bytes(g));
   z.fCnt = take(2 * BH * sizeof(int));  // the multi-round tensor-core launch's counters per pair
+  z.fAmax = take(BH * 16 * 3 * sizeof(float));
+  z.fExp = take(BH * 4 * sizeof(int));
   z.fwd_ws = o;
   o = 0;
   z.bdK0 = take(slot); z.bdK1 = take(slot); z.bdV0 = take(slot); z.bdV1 = take(slot);
@@ -272,6 +274,8 @@ murm_status forward_entry(const murm_fwd_args* a, void* stream, int slots_f32) {
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fW);
   fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(a->workspace) + z.fImg);
   fs.counters = reinterpret_cast<int*>(static_cast<char*>(a->workspace) + z.fCnt);
+  fs.amax = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + z.fAmax);
+  fs.fexp = reinterpret_cast<int*>(static_cast<char*>(a->workspace) + z.fExp);
   return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }
 }  // namespace
@@ -408,5 +412,7 @@ extern "C" murm_status murm_slot_murmurate_fwd_noscratch(const murm_fwd_args* a,
   fs.Wpart = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fW);
   fs.images = reinterpret_cast<uint8_t*>(static_cast<char*>(base) + z.saved + z.fImg);
   fs.counters = reinterpret_cast<int*>(static_cast<char*>(base) + z.saved + z.fCnt);
+  fs.amax = reinterpret_cast<float*>(static_cast<char*>(base) + z.saved + z.fAmax);
+  fs.fexp = reinterpret_cast<int*>(static_cast<char*>(base) + z.saved + z.fExp);
   return run_forward(g, p, sv, fs, static_cast<cudaStream_t>(stream));
 }

@@ -174,6 +174,8 @@ struct FwdScratch {
   float* Wpart;     // [BH][parts][M]
   uint8_t* images;  // [BH][3][256][64] 16-bit operand images (tensor-core path)
   int* counters;    // [2][BH] partials written / finalize shares done (multi-round tensor-core launch)
+  float* amax;      // [BH][16][3] bf16 tensor-core path: block maxima of |q|, |slots_k|, |slots_v|
+  int* fexp;        // [BH][4] the pair's operand-scale exponents (q, keys, values; 0 for fp16)
 };
 struct BwdScratch {
   float* dK[2];  // [BH][M][D] ping-pong slot-key gradients

@@ -35,6 +35,7 @@
 //   XCH 14K (the threads' top-7 lists) | misc
 //   fp16: 2 key terms, 3 Q buffers; bf16: 3 key terms, 1 Q buffer
 #include <cstdlib>
+#include <type_traits>
 #include <cudaTypedefs.h>
 
 #include "murm_kernels.cuh"
@@ -267,12 +268,40 @@ constexpr int kRowLanes = 16;  // threads per slot row
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void st4(float* p, float4 x) { *reinterpret_cast<float4*>(p) = x; }
 
+// The MMA operand type of a forward over inputs of type T: fp16 for both fp16 and bf16 inputs.
+// bf16 inputs enter as fp16 under per-(b,h) power-of-two scales (q tiles converted in place, key
+// and value images written scaled): the largest |x| of a pair maps into [2^14, 2^15), so a bf16
+// value (8 significant bits) converts exactly unless it lies below 2^-39 of that largest value.
+// The slot state of every round stays within the largest |x| of the initial slots and of q (the
+// EMA and the diffusion are convex combinations, the update mean a weighted mean of q rows), so
+// the key and value scales are fixed once per pair, from the round-0 tables and q.
+using CT = __half;
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }  // e in [-126, 126]
+__device__ __forceinline__ int scale_exp(float m) {  // m * 2^e in [2^14, 2^15); 0 for m = 0 or not finite
+  if (!(m > 0.f) || !(m < INFINITY)) return 0;
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
+  return max(-126, min(126, 14 - ex));
+}
+__device__ __forceinline__ float absmax4(float4 x) { return fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))); }
+__device__ __forceinline__ uint4 bf16_to_f16_scaled(const uint4& u, float s) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(w[i] << 16) * s, hi = __uint_as_float(w[i] & 0xFFFF0000u) * s;
+    o[i] = (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Write columns 4*l .. 4*l+3 of slot row m into the operand images (row m at
-// m*128 bytes, 16-byte chunks XOR-swizzled by m & 7).
+// m*128 bytes, 16-byte chunks XOR-swizzled by m & 7), keys and values multiplied by their
+// scales (powers of two, 1 for fp16 inputs) first.
 template <typename T>
-__device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k, float4 v) {
+__device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k, float4 v, float sk, float sv) {
   const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)l >> 1) ^ (m & 7)) << 4) + (l & 1) * 8;
-  float kk[4] = {k.x, k.y, k.z, k.w};
+  float kk[4] = {k.x * sk, k.y * sk, k.z * sk, k.w * sk};
+  v = make_float4(v.x * sv, v.y * sv, v.z * sv, v.w * sv);
 #pragma unroll
   for (int s = 0; s < Cfg<T>::kSplits; ++s) {
     uint32_t a[4];
@@ -288,22 +317,89 @@ __device__ __forceinline__ void put_images(uint8_t* base, int m, int l, float4 k
 }
 }  // namespace tc
 
+// bf16 inputs: the largest |q|, |slots_k|, |slots_v| over block y's 1/16 of a pair's tokens and
+// slot rows -> amax[bh][y][0..2]. grid (BH, 16), 256 threads.
+template <typename T, typename S>
+__global__ void __launch_bounds__(256) k_tc_amax(Geom g, const T* q, Strides3 qs, const S* sk, Strides3 sks,
+                                                 const S* svv, Strides3 svs, float* amax) {
+  pdl_wait();  // the previous step's kernels may still read amax
+  pdl_trigger();
+  __shared__ float red[3][8];
+  const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, y = blockIdx.y, ny = gridDim.y;
+  const int n0 = (int)((int64_t)g.N * y / ny), n1 = (int)((int64_t)g.N * (y + 1) / ny);
+  float mq = 0.f, mk = 0.f, mv = 0.f;
+  for (int e = threadIdx.x; e < (n1 - n0) * 8; e += blockDim.x) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n0 + (e >> 3)) + 8 * (e & 7));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      mq = fmaxf(mq, fmaxf(__uint_as_float((w[i] & 0x7FFFu) << 16), __uint_as_float(w[i] & 0x7FFF0000u)));
+  }
+  const int m0 = g.M * y / ny, m1 = g.M * (y + 1) / ny;
+  for (int e = threadIdx.x; e < (m1 - m0) * tc::kD; e += blockDim.x) {
+    const int m = m0 + e / tc::kD, c = e % tc::kD;
+    mk = fmaxf(mk, fabsf(Elem<S>::load(row_ptr(sk, sks, b, h, m) + c)));
+    mv = fmaxf(mv, fabsf(Elem<S>::load(row_ptr(svv, svs, b, h, m) + c)));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+    mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+    mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = mq;
+    red[1][threadIdx.x >> 5] = mk;
+    red[2][threadIdx.x >> 5] = mv;
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, red[threadIdx.x][i]);
+    amax[((size_t)bh * ny + y) * 3 + threadIdx.x] = m;
+  }
+}
+constexpr int kAmaxBlocks = 16;
+
+// The pair's operand-scale exponents (bf16 inputs: from the k_tc_amax maxima; fp16: 0): q, keys, values.
+template <typename T>
+__device__ __forceinline__ int3 pair_exps(const float* amax, int bh) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return make_int3(0, 0, 0);
+  } else {
+    float mq = 0.f, mk = 0.f, mv = 0.f;
+#pragma unroll 4
+    for (int y = 0; y < kAmaxBlocks; ++y) {
+      const float* a = amax + ((size_t)bh * kAmaxBlocks + y) * 3;
+      mq = fmaxf(mq, a[0]);
+      mk = fmaxf(mk, a[1]);
+      mv = fmaxf(mv, a[2]);
+    }
+    return make_int3(tc::scale_exp(mq), tc::scale_exp(fmaxf(mk, mq)), tc::scale_exp(fmaxf(mv, mq)));
+  }
+}
+
 // Round-0 state: slot tables (element type S: the dtype of q, or fp32 slot state; strided, batch
 // stride 0 broadcasts) -> fp32 state + images. grid (BH, 256/16): block y covers 16 slot rows,
 // 16 threads each (rows >= M write zero images). Also zeroes the pair's two counters of the
-// multi-round forward launch that follows.
+// multi-round forward launch that follows and records the pair's operand-scale exponents.
 template <typename T, typename S>
 __global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, const S* sk, Strides3 sks, const S* svv,
                                                                         Strides3 svs, Saved sv, uint8_t* images,
-                                                                        int* counters) {
+                                                                        int* counters, const float* amax, int* fexp) {
   pdl_wait();  // the previous step's kernels may still read the state, images and counters
   pdl_trigger();
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, l = threadIdx.x & 15;
+  const int3 ex = pair_exps<T>(amax, bh);
   if (blockIdx.y == 0 && threadIdx.x == 0) {
     counters[bh] = 0;
     counters[g.BH + bh] = 0;
+    fexp[4 * bh] = ex.x;
+    fexp[4 * bh + 1] = ex.y;
+    fexp[4 * bh + 2] = ex.z;
   }
-  uint8_t* base = images + (size_t)bh * tc::Layout<T>::kImages;
+  uint8_t* base = images + (size_t)bh * tc::Layout<tc::CT>::kImages;
   const int m = blockIdx.y * kSlotRows + (threadIdx.x >> 4);
   float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
   if (m < g.M) {
@@ -315,7 +411,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotRows) k_tc_load(Geom g, c
     tc::st4(sv.K + e, k);
     tc::st4(sv.V + e, v);
   }
-  tc::put_images<T>(base, m, l, k, v);
+  tc::put_images<tc::CT>(base, m, l, k, v, tc::pow2f(ex.y), tc::pow2f(ex.z));
 }
 
 __device__ __forceinline__ float4 ema4(float a, float b, float4 x, float4 u) {
@@ -394,7 +490,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
   }
   __syncthreads();
   if (rr < 1 || rr > kSlotRows) return;
-  uint8_t* base = fs.images + (size_t)bh * tc::Layout<T>::kImages;
+  uint8_t* base = fs.images + (size_t)bh * tc::Layout<tc::CT>::kImages;
   const size_t nxt = ((size_t)(r + 1) * g.BH + bh) * MD;
   float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
   if (m < g.M) {
@@ -408,7 +504,7 @@ __global__ void __launch_bounds__(tc::kRowLanes * kSlotHalo, 2) k_tc_finalize(Ge
     tc::st4(sv.K + e, k);
     tc::st4(sv.V + e, v);
   }
-  tc::put_images<T>(base, m, l, k, v);  // rows >= M: zero
+  tc::put_images<tc::CT>(base, m, l, k, v, tc::pow2f(fs.fexp[4 * bh + 1]), tc::pow2f(fs.fexp[4 * bh + 2]));  // rows >= M: zero
 }
 
 // ---------------------------------------------------------------------------
@@ -426,8 +522,9 @@ template <typename T>
 __global__ void __launch_bounds__(tc::kThreads, 1)
     k_fwd_tc(Geom g, int r0, int r1, const __grid_constant__ CUtensorMap qmap, T* out, Strides3 os, int64_t* indices,
              float* weights, Saved sv, FwdScratch fs, const __grid_constant__ TileSplit split) {
-  using C = tc::Cfg<T>;
-  using L = tc::Layout<T>;
+  using C = tc::Cfg<tc::CT>;  // MMA operands: fp16 (bf16 inputs converted under the pair's scales)
+  using L = tc::Layout<tc::CT>;
+  constexpr bool kConv = !std::is_same<T, __half>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t s_base = smem_u32(sm);
@@ -440,6 +537,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   uint64_t* hand_free = bar_img + 11;  // [4] per lane quadrant: the epilogue warp has read them
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_MISC + 128);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + L::OFF_MISC + 132);
+  uint64_t* q_conv = reinterpret_cast<uint64_t*>(sm + L::OFF_MISC + 136);  // [3] bf16: Q buffer converted
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool issuer_warp = warp == tc::kIssuerWarp;
@@ -481,6 +579,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // ---- set-up: barriers, zeroed P, ones, TMEM ----
   if (tid == 0) {
     mbar_init(bar_img, 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&q_conv[i], 96);  // warps 13-15 (bf16 inputs)
     for (int i = 0; i < 3; ++i) mbar_init(&bar_q[i], 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
@@ -544,6 +643,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     tma_load_4d(sm + L::OFF_Q + bs * tc::kQBytes, &qmap, 0, t_beg + tile_idx * kTile, h, b, &bar_q[bs]);
     q_pending[bs] = true;
   };
+  uint32_t qc_phase[3] = {0, 0, 0};  // issuer: conversions of the Q buffers waited for (bf16 inputs)
   auto wait_q = [&](int tile_idx) -> bool {  // issuer
     const int bs = q_slot(tile_idx);
     if (!tc::timed_wait(&bar_q[bs], q_phase[bs])) {
@@ -552,6 +652,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     }
     q_phase[bs] ^= 1;
     q_pending[bs] = false;
+    if (kConv) {  // warps 13-15 have converted the tile to fp16 in place
+      if (!tc::timed_wait(&q_conv[bs], qc_phase[bs])) {
+        fail(tc::kErrQWait);
+        return false;
+      }
+      qc_phase[bs] ^= 1;
+    }
     return true;
   };
   // operand descriptors (start addresses moved per MMA by SDesc::at)
@@ -623,6 +730,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       const size_t MD = (size_t)g.M * tc::kD;
       const size_t cur = ((size_t)r * g.BH + p) * MD, nxt = cur + (size_t)g.BH * MD;
       uint8_t* img = fs.images + (size_t)p * L::kImages;
+      const float img_sk = kConv ? tc::pow2f(fs.fexp[4 * p + 1]) : 1.f;
+      const float img_sv = kConv ? tc::pow2f(fs.fexp[4 * p + 2]) : 1.f;
       const int lo = k * tc::kSlotsPad / count, hi = (k + 1) * tc::kSlotsPad / count;
       const int c8 = warp * 8;  // this warp's first column
       for (int base = lo; base < hi; base += 30) {
@@ -706,23 +815,29 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             vd[0] = make_float4(vn[0], vn[1], vn[2], vn[3]);
             vd[1] = make_float4(vn[4], vn[5], vn[6], vn[7]);
           }
-          // the 8 columns are one 16-byte chunk of each 16-bit image (128-byte swizzle)
+          // the 8 columns are one 16-byte chunk of each 16-bit image (128-byte swizzle), keys and
+          // values under the pair's scales
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kn[i] *= img_sk;
+            vn[i] *= img_sv;
+          }
           const uint32_t off = (uint32_t)m * 128 + (((uint32_t)warp ^ ((uint32_t)m & 7)) << 4);
 #pragma unroll
           for (int sp = 0; sp < C::kSplits; ++sp) {
             uint32_t w4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint32_t a = tc::to_bits<T>(kn[2 * i]), b2 = tc::to_bits<T>(kn[2 * i + 1]);
-              kn[2 * i] -= tc::from_bits<T>((uint16_t)a);  // exact in fp32: the next term carries the residual
-              kn[2 * i + 1] -= tc::from_bits<T>((uint16_t)b2);
+              const uint32_t a = tc::to_bits<tc::CT>(kn[2 * i]), b2 = tc::to_bits<tc::CT>(kn[2 * i + 1]);
+              kn[2 * i] -= tc::from_bits<tc::CT>((uint16_t)a);  // exact in fp32: the next term carries the residual
+              kn[2 * i + 1] -= tc::from_bits<tc::CT>((uint16_t)b2);
               w4[i] = a | (b2 << 16);
             }
             *reinterpret_cast<uint4*>(img + sp * tc::kImg + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
           uint32_t w4[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) w4[i] = tc::to_bits<T>(vn[2 * i]) | (tc::to_bits<T>(vn[2 * i + 1]) << 16);
+          for (int i = 0; i < 4; ++i) w4[i] = tc::to_bits<tc::CT>(vn[2 * i]) | (tc::to_bits<tc::CT>(vn[2 * i + 1]) << 16);
           *reinterpret_cast<uint4*>(img + L::OFF_V + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
@@ -1077,6 +1192,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     last_round = r == g.R - 1;
     for (int u = split.start[cta]; u < u_end; u = next_segment()) {
     set_segment(u);
+    // bf16 inputs: scores, attend outputs and slot sums come out of the MMAs under the pair's
+    // scales (q 2^eq, keys 2^ek, values 2^ev): undone exactly here
+    const float usq = kConv ? tc::pow2f(-fs.fexp[4 * bh]) : 1.f;
+    const float usk = kConv ? tc::pow2f(-fs.fexp[4 * bh + 1]) : 1.f;
+    const float usv = kConv ? tc::pow2f(-fs.fexp[4 * bh + 2]) : 1.f;
     for (int tile = 0; tile < ntiles; ++tile) {
       const int n0 = t_beg + tile * kTile;
       const int n = n0 + row;
@@ -1113,7 +1233,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
         if (__float_as_uint(hf[9]) != 0u) {  // final list: an exact-scan row's picks and scores
 #pragma unroll
-          for (int j = 0; j < kTopK; ++j) wgt[j] = hf[j] * g.scale;
+          for (int j = 0; j < kTopK; ++j) wgt[j] = hf[j] * usq * usk * g.scale;
         } else {  // merge the two threads' lists: the row's top 7, ties to the lower slot
           other[7] = mine[7] = 0;
           tc::merge8_rank(mine, other, top);
@@ -1121,7 +1241,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           for (int j = 0; j < kTopK; ++j) {
             const uint32_t kk = tc::rank_score_key(top[j]);
             pick[j] = tc::rank_slot(top[j]);
-            wgt[j] = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk) * g.scale;
+            wgt[j] = __uint_as_float((kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk) * usq * usk * g.scale;
           }
         }
       }
@@ -1150,7 +1270,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           if (old_off[j]) *p_at(old_off[j]) = 0;
         if (valid) {
 #pragma unroll
-          for (int j = 0; j < kTopK; ++j) *p_at(poff[j]) = tc::to_bits<T>(wgt[j]);
+          for (int j = 0; j < kTopK; ++j) *p_at(poff[j]) = tc::to_bits<tc::CT>(wgt[j]);
         }
         fence_proxy_async_smem();
       }
@@ -1191,8 +1311,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         if (valid) {
 #pragma unroll
           for (int j = 0; j < kTopK; ++j) {
-            const uint16_t hb = tc::to_bits<T>(wgt[j]);
-            *p_at(poff[j]) = tc::to_bits<T>(wgt[j] - tc::from_bits<T>(hb));
+            const uint16_t hb = tc::to_bits<tc::CT>(wgt[j]);
+            *p_at(poff[j]) = tc::to_bits<tc::CT>(wgt[j] - tc::from_bits<tc::CT>(hb));
           }
         }
         fence_proxy_async_smem();
@@ -1206,6 +1326,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           float o[32];
           tmem_ld32(tmem + lane_base + tc::COL_O + 32 * hc, o);
           tmem_wait_ld();
+          if (kConv) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= usv;
+          }
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -1237,6 +1361,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
           float s32[32];
           tmem_ld32(tmem + lane_base + tc::COL_U + tc::kUW * hh + 32 * hc, s32);
           tmem_wait_ld();
+          if (kConv) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s32[i] *= usq;
+          }
           if (m < g.M) {  // chunk-major: a warp's store of one 4-column chunk covers 32 consecutive rows
             float4* dst = reinterpret_cast<float4*>(fs.Spart) + (po * 16 + 8 * hc) * g.M + m;
 #pragma unroll
@@ -1257,6 +1385,30 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         __threadfence();
         counter_release_add(&cnt_part[bh], 1);
       }
+    }
+    }  // segments
+    }  // rounds
+  } else if (kConv && warp > tc::kIssuerWarp) {
+    // ================= warps 13-15, bf16 inputs =================
+    // Each token tile of q, once loaded, converted in place to fp16 under the pair's scale (the
+    // Q buffers are loaded and read in the issuer's order: tile i of a segment into buffer i % 3).
+    const int ct = tid - (tc::kIssuerWarp + 1) * 32;  // 0..95
+    uint32_t cph[3] = {0, 0, 0};
+    for (r = r0; r < r1; ++r) {
+    for (int u = split.start[cta]; u < u_end; u = next_segment()) {
+    set_segment(u);
+    const float sq = tc::pow2f(fs.fexp[4 * bh]);
+    for (int tile = 0; tile < ntiles; ++tile) {
+      const int bs = tile % C::kQBufs;
+      if (!*s_abort && !tc::timed_wait(&bar_q[bs], cph[bs])) fail(tc::kErrQWait);
+      cph[bs] ^= 1;
+      if (!*s_abort) {
+        uint4* qb = reinterpret_cast<uint4*>(sm + L::OFF_Q + bs * tc::kQBytes);
+#pragma unroll 2
+        for (int c = ct; c < (int)(tc::kQBytes / 16); c += 96) qb[c] = tc::bf16_to_f16_scaled(qb[c], sq);
+        fence_proxy_async_smem();  // generic writes, read by the MMAs (async proxy)
+      }
+      mbar_arrive(&q_conv[bs]);
     }
     }  // segments
     }  // rounds
@@ -1296,8 +1448,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tc_tensor_map_encoder() { return get_encode();
 
 size_t tc_images_bytes(const Geom& g) {
   if (g.D != tc::kD) return 0;
-  if (g.dtype == MURM_F16) return (size_t)g.BH * tc::Layout<__half>::kImages;
-  if (g.dtype == MURM_BF16) return (size_t)g.BH * tc::Layout<__nv_bfloat16>::kImages;
+  if (g.dtype == MURM_F16 || g.dtype == MURM_BF16) return (size_t)g.BH * tc::Layout<tc::CT>::kImages;
   return 0;
 }
 
@@ -1363,14 +1514,24 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (cudaError_t e = smem_opt_in(k_fwd_tc<T>, tc::Layout<T>::kSmem)) return e;
-  if (p.slots_f32)
+  constexpr uint32_t kSmem = tc::Layout<tc::CT>::kSmem;
+  if (cudaError_t e = smem_opt_in(k_fwd_tc<T>, kSmem)) return e;
+  constexpr bool kConv = !std::is_same<T, __half>::value;
+  if (p.slots_f32) {
+    if (kConv)
+      MURM_LAUNCH_PDL("tc_amax", (k_tc_amax<T, float>), dim3(g.BH, kAmaxBlocks), 256, 0, st, g, static_cast<const T*>(p.q),
+                      p.qs, static_cast<const float*>(p.sk), p.sks, static_cast<const float*>(p.sv), p.svs, fs.amax);
     MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, float>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
                     static_cast<const float*>(p.sk), p.sks, static_cast<const float*>(p.sv), p.svs, sv, images,
-                    fs.counters);
-  else
+                    fs.counters, fs.amax, fs.fexp);
+  } else {
+    if (kConv)
+      MURM_LAUNCH_PDL("tc_amax", (k_tc_amax<T, T>), dim3(g.BH, kAmaxBlocks), 256, 0, st, g, static_cast<const T*>(p.q), p.qs,
+                      static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, fs.amax);
     MURM_LAUNCH_PDL("tc_load", (k_tc_load<T, T>), dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotRows, 0, st, g,
-                    static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, sv, images, fs.counters);
+                    static_cast<const T*>(p.sk), p.sks, static_cast<const T*>(p.sv), p.svs, sv, images, fs.counters,
+                    fs.amax, fs.fexp);
+  }
   TileSplit split;  // the plan the workspace was sized for (make_geom)
   plan_split(g.BH, g.N, kTile, kMaxSplitCtas, &split);
   // All rounds in one launch when every CTA can be resident at once (a cooperative launch): the
@@ -1378,13 +1539,13 @@ cudaError_t fwd_tc(const Geom& g, const FwdPtrs& p, const Saved& sv, const FwdSc
   // between them. MURM_FWD_LAUNCH_PER_ROUND=1 forces the latter.
   const char* per_round = getenv("MURM_FWD_LAUNCH_PER_ROUND");
   if (g.R > 1 && !(per_round && per_round[0] == '1') &&
-      coop_fits(reinterpret_cast<const void*>(k_fwd_tc<T>), tc::kThreads, tc::Layout<T>::kSmem, split.G)) {
-    MURM_LAUNCH_COOP_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st,
+      coop_fits(reinterpret_cast<const void*>(k_fwd_tc<T>), tc::kThreads, kSmem, split.G)) {
+    MURM_LAUNCH_COOP_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, kSmem, st,
                          g, 0, g.R, qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, split);
     return cudaGetLastError();
   }
   for (int r = 0; r < g.R; ++r) {
-    MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, tc::Layout<T>::kSmem, st, g, r,
+    MURM_LAUNCH_PDL("select_attend_update_tc", k_fwd_tc<T>, dim3(split.G), tc::kThreads, kSmem, st, g, r,
                 r + 1, qmap, static_cast<T*>(p.out), p.os, p.indices, p.weights, sv, fs, split);
     if (r + 1 < g.R)
       MURM_LAUNCH_PDL("tc_finalize", k_tc_finalize<T>, dim3(g.BH, kSlotBlocks), tc::kRowLanes * kSlotHalo, 0, st, g, r, sv, fs,
