@@ -128,7 +128,7 @@ Sizes make_sizes(const Geom& g) {
   // operand images of the tensor-core path (16-bit dtypes, head_dim 64)
   z.fImg = take(tc_images_bytes(g));
   z.fCnt = take(2 * BH * sizeof(int));  // the multi-round tensor-core launch's counters per pair
-  z.fAmax = take(BH * 16 * 3 * sizeof(float));
+  z.fAmax = take(BH * kAmaxBlocks * 3 * sizeof(float));
   z.fExp = take(BH * 4 * sizeof(int));
   z.fwd_ws = o;
   o = 0;

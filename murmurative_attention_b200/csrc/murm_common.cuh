@@ -168,13 +168,14 @@ struct Saved {
   uint8_t* idx;  // [R][BH][N][8] selected slots (7 used)
   float* w;      // [R][BH][N][8] softmax weights (7 used)
 };
+constexpr int kAmaxBlocks = 32;  // blocks per (b,h) pair of the forward's maxima pass (bf16 tensor-core path)
 struct FwdScratch {
   float* Spart;     // CUDA-core path: [BH][red_chunks][M][D]; tensor-core path: [BH][ft_parts][D/4][M][4]
                     // (4-column chunks, slot rows contiguous: coalesced stores from the TMEM lanes)
   float* Wpart;     // [BH][parts][M]
   uint8_t* images;  // [BH][3][256][64] 16-bit operand images (tensor-core path)
   int* counters;    // [2][BH] partials written / finalize shares done (multi-round tensor-core launch)
-  float* amax;      // [BH][16][3] bf16 tensor-core path: block maxima of |q|, |slots_k|, |slots_v|
+  float* amax;      // [BH][kAmaxBlocks][3] bf16 tensor-core path: block maxima of |q|, |slots_k|, |slots_v|
   int* fexp;        // [BH][4] the pair's operand-scale exponents (q, keys, values; 0 for fp16)
 };
 struct BwdScratch {

@@ -53,11 +53,10 @@ constexpr int kRowThreads = 256;                // 8 row warps: 2 per TMEM lane 
 constexpr int kEpiWarp = kRowThreads / 32;       // 4 epilogue warps (8..11), one per lane quadrant
 constexpr int kEpiThreads = 128;
 constexpr int kIssuerWarp = kEpiWarp + 4;        // a fourth warpgroup: warp 12's lane 0 issues MMAs and
-constexpr int kThreads = kRowThreads + kEpiThreads + 128;  // copies, warps 13-15 only give up registers
-// Registers per thread: launched at 128 (512 threads, the whole register file); the row warpgroups
-// raise theirs to kRowRegs, the fourth warpgroup lowers its to kIdleRegs, the epilogue keeps 128.
-constexpr int kRowRegs = 152, kIdleRegs = 80;
-static_assert(2 * 128 * kRowRegs + 128 * 128 + 128 * kIdleRegs == 65536, "register split must sum to the launch's");
+constexpr int kThreads = kRowThreads + kEpiThreads + 128;  // copies, warps 13-15 convert bf16 q tiles
+// Registers: one allocation for all warps (126 a thread, no spills). No `setmaxnreg` split: ptxas
+// ignores it in relocatable device code, and compiled whole, any split that lowers the fourth
+// warpgroup (the issuer's code) below ~128 spills.
 constexpr int kParts = 2;        // each token row's 256 scores are split over 2 threads
 constexpr uint32_t kImg = kSlotsPad * 128;  // one [256][64] 16-bit operand image
 constexpr uint32_t kTmemCols = 512;
@@ -328,12 +327,24 @@ __global__ void __launch_bounds__(256) k_tc_amax(Geom g, const T* q, Strides3 qs
   const int bh = blockIdx.x, b = bh / g.H, h = bh - b * g.H, y = blockIdx.y, ny = gridDim.y;
   const int n0 = (int)((int64_t)g.N * y / ny), n1 = (int)((int64_t)g.N * (y + 1) / ny);
   float mq = 0.f, mk = 0.f, mv = 0.f;
-  for (int e = threadIdx.x; e < (n1 - n0) * 8; e += blockDim.x) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n0 + (e >> 3)) + 8 * (e & 7));
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  // eight independent 16-byte loads in flight per thread: the pass is bound by loads outstanding
+  constexpr int kU = 8;
+  const int cnt = (n1 - n0) * 8;
+  for (int e0 = threadIdx.x; e0 < cnt; e0 += kU * blockDim.x) {
+    uint4 u[kU];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      mq = fmaxf(mq, fmaxf(__uint_as_float((w[i] & 0x7FFFu) << 16), __uint_as_float(w[i] & 0x7FFF0000u)));
+    for (int j = 0; j < kU; ++j) {
+      const int e = e0 + j * blockDim.x;
+      u[j] = e < cnt ? *reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n0 + (e >> 3)) + 8 * (e & 7))
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        mq = fmaxf(mq, fmaxf(__uint_as_float((w[i] & 0x7FFFu) << 16), __uint_as_float(w[i] & 0x7FFF0000u)));
+    }
   }
   const int m0 = g.M * y / ny, m1 = g.M * (y + 1) / ny;
   for (int e = threadIdx.x; e < (m1 - m0) * tc::kD; e += blockDim.x) {
@@ -360,7 +371,6 @@ __global__ void __launch_bounds__(256) k_tc_amax(Geom g, const T* q, Strides3 qs
     amax[((size_t)bh * ny + y) * 3 + threadIdx.x] = m;
   }
 }
-constexpr int kAmaxBlocks = 16;
 
 // The pair's operand-scale exponents (bf16 inputs: from the k_tc_amax maxima; fp16: 0): q, keys, values.
 template <typename T>
@@ -609,13 +619,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // kernel, whose outputs (the round's state and operand images) are read from here on
   pdl_wait();
   pdl_trigger();
-  // the register split between the warpgroups; it sums to the launch's allocation, so the row
-  // warpgroups' increase is met once the fourth warpgroup has given its registers back
-  if (warp >= tc::kIssuerWarp) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(tc::kIdleRegs));
-  } else if (warp < tc::kEpiWarp) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(tc::kRowRegs));
-  }
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * quadrant) << 16;
   const uint32_t a_v = s_base + L::OFF_V, a_p = s_base + L::OFF_P, a_ones = s_base + L::OFF_ONES;

@@ -387,10 +387,23 @@ __global__ void __launch_bounds__(256) k_bwd_tables_last(Geom g, Saved sv, uint8
     const int b = bh / g.H, h = bh - b * g.H;
     const int n0 = (int)((int64_t)g.N * blockIdx.y / gridDim.y), n1 = (int)((int64_t)g.N * (blockIdx.y + 1) / gridDim.y);
     float mq = 0.f, mg = 0.f;
-    for (int e = threadIdx.x; e < (n1 - n0) * 8; e += blockDim.x) {
-      const int n = n0 + (e >> 3), c = (e & 7) * 8;
-      mq = fmaxf(mq, tcb::absmax8_bf16(*reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n) + c)));
-      mg = fmaxf(mg, tcb::absmax8_bf16(*reinterpret_cast<const uint4*>(row_ptr(go, gos, b, h, n) + c)));
+    // four q and four grad_out 16-byte loads in flight per thread: the pass is bound by loads outstanding
+    constexpr int kU = 4;
+    const int cnt = (n1 - n0) * 8;
+    for (int e0 = threadIdx.x; e0 < cnt; e0 += kU * blockDim.x) {
+      uint4 uq[kU], ug[kU];
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int e = e0 + j * blockDim.x;
+        const int n = n0 + (e >> 3), c = (e & 7) * 8;
+        uq[j] = e < cnt ? *reinterpret_cast<const uint4*>(row_ptr(q, qs, b, h, n) + c) : make_uint4(0u, 0u, 0u, 0u);
+        ug[j] = e < cnt ? *reinterpret_cast<const uint4*>(row_ptr(go, gos, b, h, n) + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        mq = fmaxf(mq, tcb::absmax8_bf16(uq[j]));
+        mg = fmaxf(mg, tcb::absmax8_bf16(ug[j]));
+      }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
