@@ -100,14 +100,10 @@ __device__ __forceinline__ int64_t off4(const int64_t* s, int b, int h, int n, i
 // Shared memory: the (b,h) key table transposed to [d][Mp] fp32 (lanes read
 // consecutive slots), and each warp's q row.
 // ---------------------------------------------------------------------------
+// The (b,h) key table into shared memory, transposed to [D][Mp] fp32.
 template <typename T>
-__global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args a, int Mp, int vec) {
-  extern __shared__ float sh[];
-  const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
-  float* Kt = sh;                       // [D][Mp]
-  float* qs = sh + (size_t)D * Mp;      // [kWarps][D]
-  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void stage_keys(const murm_select_attend_args& a, float* Kt, int Mp, int vec, int b, int h) {
+  const int M = a.shape.slots, D = a.shape.head_dim;
   if (vec) {  // 16-byte loads (rows 16-byte aligned), several in flight per thread
     constexpr int E = 16 / (int)sizeof(T);
     const int C = D / E;
@@ -126,6 +122,17 @@ __global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args 
       Kt[(size_t)d * Mp + m] = ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
     }
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args a, int Mp, int vec) {
+  extern __shared__ float sh[];
+  const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
+  float* Kt = sh;                       // [D][Mp]
+  float* qs = sh + (size_t)D * Mp;      // [kWarps][D]
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  stage_keys<T>(a, Kt, Mp, vec, b, h);
   __syncthreads();
   const int em = (a.effective_m > 0 && a.effective_m < M) ? a.effective_m : M;
   const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
@@ -205,6 +212,156 @@ __global__ void __launch_bounds__(32 * kWarps) k_sa_fwd(murm_select_attend_args 
         if (lane == j) { pj = pick[j]; wj = sc[j]; }
       a.indices[rec + lane] = pj;
       a.weights[rec + lane] = wj;
+    }
+    __syncwarp();
+  }
+}
+
+// x[j] for a run-time j in [0, 8) over 8 values held in registers (select tree).
+__device__ __forceinline__ uint32_t pick8(const uint32_t (&x)[8], int j) {
+  const uint32_t a0 = (j & 1) ? x[1] : x[0], a1 = (j & 1) ? x[3] : x[2];
+  const uint32_t a2 = (j & 1) ? x[5] : x[4], a3 = (j & 1) ? x[7] : x[6];
+  const uint32_t b0 = (j & 2) ? a1 : a0, b1 = (j & 2) ? a3 : a2;
+  return (j & 4) ? b1 : b0;
+}
+
+// ---------------------------------------------------------------------------
+// select + attend, forward, M <= 256 and selection on the GPU: the same results as k_sa_fwd
+// (the same scores, in the same operation order, and the same picks), with the key table read
+// once per four tokens. A warp scores four tokens at a time (lane: slots lane + 32 j, 8 x 4
+// independent dot products over the key rows it loads once); for each token the row's keys
+// >= the 7th largest of the 32 lanes' maxima (a lower bound of the row's 7th largest key) are
+// the only ones a lane ranks, then the lanes' lists are merged. Shared memory: the transposed
+// key table and each warp's four q rows, [D][4] fp32.
+// ---------------------------------------------------------------------------
+constexpr int kTokGroup = 4;
+template <typename T>
+__global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_args a, int Mp, int vec) {
+  extern __shared__ float sh[];
+  const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
+  float* Kt = sh;                                                   // [D][Mp]
+  float4* qs = reinterpret_cast<float4*>(sh + (((size_t)D * Mp + 3) & ~(size_t)3));  // [kWarps][D]
+  const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  stage_keys<T>(a, Kt, Mp, vec, b, h);
+  __syncthreads();
+  const int em = (a.effective_m > 0 && a.effective_m < M) ? a.effective_m : M;
+  const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
+  float4* q4 = qs + warp * D;
+  const float* qf = reinterpret_cast<const float*>(q4);
+  int col[8];  // clamped columns: reads stay inside Kt
+#pragma unroll
+  for (int j = 0; j < 8; ++j) col[j] = min(M - 1, lane + 32 * j);
+  for (int g0 = 0; g0 < kTokPerWarp; g0 += kTokGroup) {
+    const int nb = (blockIdx.x * kWarps + warp) * kTokPerWarp + g0;
+    if (nb >= N) break;
+    for (int d = lane; d < D; d += 32) {
+      float v[kTokGroup];
+#pragma unroll
+      for (int t = 0; t < kTokGroup; ++t) v[t] = nb + t < N ? ld<T>(a.q, off3(a.q_stride, b, h, nb + t) + d) : 0.f;
+      q4[d] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    __syncwarp();
+    float sj[kTokGroup][8];
+#pragma unroll
+    for (int t = 0; t < kTokGroup; ++t)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sj[t][j] = 0.f;
+    for (int d = 0; d < D; ++d) {  // each score in d order, as k_sa_fwd
+      const float4 qd = q4[d];
+      const float* row = Kt + (size_t)d * Mp;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float kv = row[col[j]];
+        sj[0][j] = fmaf(qd.x, kv, sj[0][j]);
+        sj[1][j] = fmaf(qd.y, kv, sj[1][j]);
+        sj[2][j] = fmaf(qd.z, kv, sj[2][j]);
+        sj[3][j] = fmaf(qd.w, kv, sj[3][j]);
+      }
+    }
+#pragma unroll 1
+    for (int t = 0; t < kTokGroup; ++t) {
+      const int n = nb + t;
+      if (n >= N) break;
+      uint32_t kk[8];  // rank keys of this lane's slots (0: no slot)
+      uint32_t lm = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = lane + 32 * j;
+        kk[j] = 0u;
+        if (m < M) {
+          float sc = sj[0][j];
+          if (a.position_bias) sc += ld<T>(a.position_bias, off4(a.bias_stride, b, h, n, m));     // reference.py:21-22
+          bool masked = m >= em || (a.causal && m > n);                                             // :27-36
+          if (a.mask) masked = masked || a.mask[off4(a.mask_stride, b, h, n, m)] == 0;                // :24-25
+          kk[j] = rank_key(masked ? -INFINITY : sc);
+        }
+        lm = max(lm, kk[j]);
+      }
+      // thr = the 7th largest lane maximum (ties counted): at least 7 of the row's keys are >= thr,
+      // so each of its top 7 is too
+      uint32_t thr = 0u, v = lm;
+      int cnt = 0;
+#pragma unroll 1
+      for (int r = 0; r < kTopK && cnt < kTopK; ++r) {
+        const uint32_t best = __reduce_max_sync(0xffffffffu, v);
+        thr = best;
+        cnt += __popc(__ballot_sync(0xffffffffu, v == best));
+        v = v == best ? 0u : v;
+      }
+      uint32_t cm = 0u;  // this lane's candidates
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cm |= (kk[j] != 0u && kk[j] >= thr ? 1u : 0u) << j;
+      uint32_t tk[kTopK];
+      int ts[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
+      while (cm) {  // ascending slot order within the lane
+        const int j = __ffs(cm) - 1;
+        cm &= cm - 1;
+        offer7(tk, ts, pick8(kk, j), lane + 32 * j);
+      }
+      warp_top7(tk, ts);
+      // attend over the picks with the plain scaled scores (reference.py:58-66)
+      float sc[kTopK], mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        float p = 0.f;
+        for (int d = lane; d < D; d += 32) p = fmaf(qf[4 * d + t], Kt[(size_t)d * Mp + ts[j]], p);
+        sc[j] = warp_sum(p) * scale;
+        mx = fmaxf(mx, sc[j]);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        sc[j] = expf(sc[j] - mx);
+        sum += sc[j];
+      }
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) sc[j] = sc[j] / sum;
+      for (int d = lane; d < D; d += 32) {
+        float o = 0.f;
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) o = fmaf(sc[j], ld<T>(a.slot_values, off3(a.sv_stride, b, h, ts[j]) + d), o);
+        st<T>(a.out, off3(a.out_stride, b, h, n) + d, o);
+      }
+      const int64_t rec = ((int64_t)bh * N + n) * kTopK;
+      if (lane < kTopK) {
+        int pj = ts[0];
+        float wj = sc[0];
+#pragma unroll
+        for (int j = 1; j < kTopK; ++j)
+          if (lane == j) { pj = ts[j]; wj = sc[j]; }
+        a.indices[rec + lane] = pj;
+        a.weights[rec + lane] = wj;
+      }
+      // the next token's scores to the front
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sj[0][j] = sj[1][j];
+        sj[1][j] = sj[2][j];
+        sj[2][j] = sj[3][j];
+      }
     }
     __syncwarp();
   }
@@ -306,8 +463,8 @@ __global__ void __launch_bounds__(256) k_csr_fill(const int64_t* idx, int N, int
 //   dw_j = g . V[i_j] (+ grad_weights), da_j = w_j (dw_j - sum_k w_k dw_k),
 //   dq = scale sum_j da_j K[i_j]; coef[t][j] = scale da_j for the slot side.
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args a, float* coef) {
+template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(256, 3) k_sa_bwd_tok(murm_select_attend_bwd_args a, float* coef) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -322,9 +479,9 @@ __global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args 
     pick[j] = clampi(a.indices[rec + j], M);
     w[j] = a.weights[rec + j];
   }
-  float g[kMaxD / 32];
+  float g[U];
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     g[u] = d < D ? ld<T>(a.grad_out, off3(a.go_stride, b, h, n) + d) : 0.f;
   }
@@ -333,7 +490,7 @@ __global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args 
   for (int j = 0; j < kTopK; ++j) {
     float p = 0.f;
 #pragma unroll
-    for (int u = 0; u < kMaxD / 32; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int d = lane + 32 * u;
       if (d < D) p = fmaf(g[u], ld<T>(a.slot_values, off3(a.sv_stride, b, h, pick[j]) + d), p);
     }
@@ -344,7 +501,7 @@ __global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args 
 #pragma unroll
   for (int j = 0; j < kTopK; ++j) c[j] = scale * (w[j] * (dw[j] - s));
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     if (d < D) {
       float dq = 0.f;
@@ -363,28 +520,28 @@ __global__ void __launch_bounds__(256) k_sa_bwd_tok(murm_select_attend_bwd_args 
 }
 
 // Over a slot's (token, pick) entries [e0, e1) in token order: acc1 += f1 * A[t] and
-// acc2 += f2 * B[t] (lane's dims d = lane + 32 u), with f1, f2 per-pair factors
-// (f[(rec0 + t) * stride + pick]) and, when fsum is given, *fsum += f2. The loads of four
-// entries are issued before their sums, so that four rows are in flight; the sums are taken in
-// entry order all the same.
-template <typename T>
+// acc2 += f2 * B[t] (lane's dims d = lane + 32 u, u < U, D <= 32 U), with f1, f2 per-pair
+// factors (f[(rec0 + t) * stride + pick]) and, when fsum is given, *fsum += f2. The loads of
+// several entries (8 for D <= 64, else 4) are issued before their sums, so that as many rows are
+// in flight; the sums are taken in entry order all the same.
+template <typename T, int U>
 __device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_t rec0, const float* f1, int s1,
                                           const float* f2, int s2, const T* A, const int64_t* as, const T* Bp,
                                           const int64_t* bs, int b, int h, int D, int lane,
-                                          float (&acc1)[kMaxD / 32], float (&acc2)[kMaxD / 32], float* fsum) {
-  constexpr int U = kMaxD / 32;
+                                          float (&acc1)[U], float (&acc2)[U], float* fsum) {
+  constexpr int F = U <= 2 ? 8 : 4;  // entries in flight
   int e = e0;
-  for (; e + 4 <= e1; e += 4) {
-    int tt[4], jj[4];
-    float x1[4], x2[4], ra[4][U], rb[4][U];
+  for (; e + F <= e1; e += F) {
+    int tt[F], jj[F];
+    float x1[F], x2[F], ra[F][U], rb[F][U];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < F; ++r) {
       const int en = ent[e + r];
       tt[r] = en >> 3;
       jj[r] = en & 7;
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < F; ++r) {
       x1[r] = f1[(rec0 + tt[r]) * s1 + jj[r]];
       x2[r] = f2[(rec0 + tt[r]) * s2 + jj[r]];
 #pragma unroll
@@ -395,7 +552,7 @@ __device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_
       }
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < F; ++r) {
       if (fsum) *fsum += x2[r];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -423,8 +580,8 @@ __device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_
 
 // slot side: a warp per (b,h, slot), its pairs in token order:
 //   dK[m] = sum coef * q[t],  dV[m] = sum w * g[t]
-template <typename T>
-__global__ void __launch_bounds__(256) k_sa_bwd_slot(murm_select_attend_bwd_args a, const float* coef,
+template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(256, 3) k_sa_bwd_slot(murm_select_attend_bwd_args a, const float* coef,
                                                      const int* offsets, const int* entries) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
@@ -433,13 +590,13 @@ __global__ void __launch_bounds__(256) k_sa_bwd_slot(murm_select_attend_bwd_args
   if (m >= M) return;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
-  float dk[kMaxD / 32], dv[kMaxD / 32];
+  float dk[U], dv[U];
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) dk[u] = dv[u] = 0.f;
-  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, coef, 8, a.weights, kTopK, static_cast<const T*>(a.q),
+  for (int u = 0; u < U; ++u) dk[u] = dv[u] = 0.f;
+  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, coef, 8, a.weights, kTopK, static_cast<const T*>(a.q),
                a.q_stride, static_cast<const T*>(a.grad_out), a.go_stride, b, h, D, lane, dk, dv, nullptr);
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     if (d < D) {
       st<T>(a.grad_slot_keys, off3(a.gsk_stride, b, h, m) + d, dk[u]);
@@ -452,8 +609,8 @@ __global__ void __launch_bounds__(256) k_sa_bwd_slot(murm_select_attend_bwd_args
 // slot update, forward: a warp per (b,h, slot). saved = U_k, U_v [BH][M][D] and
 // W [BH][M] (fp32).
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const int* offsets, const int* entries,
+template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(256, 3) k_upd_fwd(murm_slot_update_args a, const int* offsets, const int* entries,
                                                  float* Uk, float* Uv, float* Wsum) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
@@ -462,11 +619,11 @@ __global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const 
   if (m >= M) return;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
-  float sk[kMaxD / 32], sv[kMaxD / 32];
+  float sk[U], sv[U];
   float W = 0.f;
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
-  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+  for (int u = 0; u < U; ++u) sk[u] = sv[u] = 0.f;
+  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
                static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
                b, h, D, lane, sk, sv, &W);
   const bool valid = W > 0.f;                       // reference.py:105
@@ -474,7 +631,7 @@ __global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const 
   const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
   const size_t so = ((size_t)bh * M + m) * D;
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     if (d < D) {
       const float uk = __fdiv_rn(sk[u], den), uv = __fdiv_rn(sv[u], den);
@@ -493,8 +650,8 @@ __global__ void __launch_bounds__(256) k_upd_fwd(murm_slot_update_args a, const 
 }
 
 // slot sums alone (a warp per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
-template <typename T>
-__global__ void __launch_bounds__(256) k_sums_fwd(murm_slot_sums_args a, const int* offsets, const int* entries) {
+template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(256, 3) k_sums_fwd(murm_slot_sums_args a, const int* offsets, const int* entries) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -502,16 +659,16 @@ __global__ void __launch_bounds__(256) k_sums_fwd(murm_slot_sums_args a, const i
   if (m >= M) return;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
-  float sk[kMaxD / 32], sv[kMaxD / 32];
+  float sk[U], sv[U];
   float W = 0.f;
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) sk[u] = sv[u] = 0.f;
-  pair_sums<T>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+  for (int u = 0; u < U; ++u) sk[u] = sv[u] = 0.f;
+  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
                static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
                b, h, D, lane, sk, sv, &W);
   const size_t so = ((size_t)bh * M + m) * D;
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     if (d < D) {
       a.key_sums[so + d] = sk[u];
@@ -552,7 +709,7 @@ __global__ void __launch_bounds__(256) k_upd_bwd_slot(murm_slot_update_bwd_args 
 }
 
 // slot update, backward, token side: a warp per token.
-template <typename T>
+template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
 __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a, const float* dks, const float* dvs,
                                                      const float* dW) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
@@ -561,9 +718,9 @@ __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a
   const int n = blockIdx.x * 8 + warp;
   if (n >= N) return;
   const int64_t rec = ((int64_t)bh * N + n) * kTopK;
-  float tk[kMaxD / 32], tv[kMaxD / 32], gk[kMaxD / 32], gv[kMaxD / 32];
+  float tk[U], tv[U], gk[U], gv[U];
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     tk[u] = d < D ? ld<T>(a.token_keys, off3(a.tk_stride, b, h, n) + d) : 0.f;
     tv[u] = d < D ? ld<T>(a.token_values, off3(a.tv_stride, b, h, n) + d) : 0.f;
@@ -577,7 +734,7 @@ __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a
     const size_t so = ((size_t)bh * M + m) * D;
     float p = 0.f;
 #pragma unroll
-    for (int u = 0; u < kMaxD / 32; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int d = lane + 32 * u;
       if (d < D) {
         const float k2 = dks[so + d], v2 = dvs[so + d];
@@ -589,7 +746,7 @@ __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a
     gw[j] = warp_sum(p) + dW[(size_t)bh * M + m];
   }
 #pragma unroll
-  for (int u = 0; u < kMaxD / 32; ++u) {
+  for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
     if (d < D) {
       st<T>(a.grad_token_keys, off3(a.gtk_stride, b, h, n) + d, gk[u]);
@@ -964,6 +1121,13 @@ murm_status check(const murm_phase_shape& s) {
   return MURM_OK;
 }
 
+// The instance of a warp-per-row kernel for the head dims per lane (1, 2 or 4: D <= 32, 64,
+// 128), so that a lane holds registers for the dims it owns only.
+template <typename F>
+F per_lane_dims(int D, F u1, F u2, F u4) {
+  return D <= 32 ? u1 : (D <= 64 ? u2 : u4);
+}
+
 murm_status launched(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return bad(MURM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -997,13 +1161,19 @@ void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cuda
 template <typename T>
 murm_status sa_fwd(const murm_select_attend_args& a, cudaStream_t st) {
   const int Mp = ((a.shape.slots + 31) / 32) * 32 + 1;
-  const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
-  smem_opt_in(k_sa_fwd<T>, smem);
   const dim3 grid((a.shape.tokens + kWarps * kTokPerWarp - 1) / (kWarps * kTokPerWarp), a.shape.batch * a.shape.heads);
   const int64_t es = (int64_t)sizeof(T);
   int vec = (a.shape.head_dim * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.slot_keys) & 15) == 0;
   for (int i = 0; i < 3; ++i) vec = vec && (a.sk_stride[i] * es) % 16 == 0;
-  MURM_LAUNCH("phase_select_attend", k_sa_fwd<T>, grid, 32 * kWarps, smem, st, a, Mp, vec);
+  if (!a.indices_in && a.shape.slots <= 256) {  // four tokens per pass over the key table
+    const size_t smem = ((((size_t)a.shape.head_dim * Mp + 3) & ~(size_t)3) + (size_t)kWarps * a.shape.head_dim * 4) * 4;
+    smem_opt_in(k_sa_fwd4<T>, smem);
+    MURM_LAUNCH("phase_select_attend", k_sa_fwd4<T>, grid, 32 * kWarps, smem, st, a, Mp, vec);
+  } else {
+    const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
+    smem_opt_in(k_sa_fwd<T>, smem);
+    MURM_LAUNCH("phase_select_attend", k_sa_fwd<T>, grid, 32 * kWarps, smem, st, a, Mp, vec);
+  }
   return launched("select_attend forward");
 }
 
@@ -1014,9 +1184,11 @@ murm_status sa_bwd(const murm_select_attend_bwd_args& a, cudaStream_t st) {
   const int BH = a.shape.batch * a.shape.heads;
   launch_csr(a.shape, a.indices, ws, st);
   float* coef = reinterpret_cast<float*>(ws + z.off_coef);
-  MURM_LAUNCH("phase_select_attend_bwd_tokens", k_sa_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a,
-              coef);
-  MURM_LAUNCH("phase_select_attend_bwd_slots", k_sa_bwd_slot<T>, dim3((a.shape.slots + 7) / 8, BH), 256, 0, st, a,
+  const int D = a.shape.head_dim;
+  const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1>, k_sa_bwd_tok<T, 2>, k_sa_bwd_tok<T, 4>);
+  const auto kslot = per_lane_dims(D, k_sa_bwd_slot<T, 1>, k_sa_bwd_slot<T, 2>, k_sa_bwd_slot<T, 4>);
+  MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, coef);
+  MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 7) / 8, BH), 256, 0, st, a,
               coef, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("select_attend backward");
 }
@@ -1031,7 +1203,8 @@ murm_status upd_fwd(const murm_slot_update_args& a, cudaStream_t st) {
   float* Uk = reinterpret_cast<float*>(sv);
   float* Uv = reinterpret_cast<float*>(sv + a256(BH * MD * 4));
   float* W = reinterpret_cast<float*>(sv + 2 * a256(BH * MD * 4));
-  MURM_LAUNCH("phase_update", k_upd_fwd<T>, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st, a,
+  const auto kupd = per_lane_dims(a.shape.head_dim, k_upd_fwd<T, 1>, k_upd_fwd<T, 2>, k_upd_fwd<T, 4>);
+  MURM_LAUNCH("phase_update", kupd, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st, a,
               reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries), Uk, Uv, W);
   return launched("slot_update forward");
 }
@@ -1050,7 +1223,8 @@ murm_status upd_bwd(const murm_slot_update_bwd_args& a, cudaStream_t st) {
   float* dW = reinterpret_cast<float*>(ws + z.off_dw);
   MURM_LAUNCH("phase_update_bwd_slots", k_upd_bwd_slot<T>, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st,
               a, Uk, Uv, W, dks, dvs, dW);
-  MURM_LAUNCH("phase_update_bwd_tokens", k_upd_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, (unsigned)BH), 256, 0, st,
+  const auto ktok = per_lane_dims(a.shape.head_dim, k_upd_bwd_tok<T, 1>, k_upd_bwd_tok<T, 2>, k_upd_bwd_tok<T, 4>);
+  MURM_LAUNCH("phase_update_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, (unsigned)BH), 256, 0, st,
               a, dks, dvs, dW);
   return launched("slot_update backward");
 }
@@ -1060,7 +1234,8 @@ murm_status sums_fwd(const murm_slot_sums_args& a, cudaStream_t st) {
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   const Sizes z = sizes(a.shape);
   launch_csr(a.shape, a.indices, ws, st);
-  MURM_LAUNCH("phase_sums", k_sums_fwd<T>, dim3((a.shape.slots + 7) / 8, a.shape.batch * a.shape.heads), 256, 0, st,
+  const auto ksum = per_lane_dims(a.shape.head_dim, k_sums_fwd<T, 1>, k_sums_fwd<T, 2>, k_sums_fwd<T, 4>);
+  MURM_LAUNCH("phase_sums", ksum, dim3((a.shape.slots + 7) / 8, a.shape.batch * a.shape.heads), 256, 0, st,
               a, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("slot sums forward");
 }
@@ -1083,7 +1258,8 @@ murm_status sums_bwd(const murm_slot_sums_bwd_args& a, cudaStream_t st) {
   u.grad_token_keys = a.grad_token_keys;
   u.grad_token_values = a.grad_token_values;
   u.grad_weights = a.grad_weights;
-  MURM_LAUNCH("phase_sums_bwd", k_upd_bwd_tok<T>, dim3((a.shape.tokens + 7) / 8, a.shape.batch * a.shape.heads), 256,
+  const auto ktok = per_lane_dims(a.shape.head_dim, k_upd_bwd_tok<T, 1>, k_upd_bwd_tok<T, 2>, k_upd_bwd_tok<T, 4>);
+  MURM_LAUNCH("phase_sums_bwd", ktok, dim3((a.shape.tokens + 7) / 8, a.shape.batch * a.shape.heads), 256,
               0, st, u, a.grad_key_sums, a.grad_value_sums, a.grad_weight_sums);
   return launched("slot sums backward");
 }

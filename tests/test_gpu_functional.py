@@ -79,6 +79,28 @@ def test_select_attend_forward_backward(dt, case):
     close(svd.grad, svo.grad, dt, s)
 
 
+@pytest.mark.parametrize("M", [256, 300])
+def test_select_ties_take_the_lowest_slot(M):
+    """Equal scores rank by ascending slot (the oracle's stable sort): every key row appears
+    four times, at slots r, r+64, r+128, r+192 (the same lane of the selecting warp and other
+    lanes), so each row's top 7 is a four-way tie and three of the next one. M = 256 takes the
+    four-token select kernel, M = 300 the one-token kernel."""
+    g = torch.Generator().manual_seed(14)
+    B, H, N, D = 1, 2, 41, 64
+    base = rnd(g, B, H, 64, D)
+    sk = torch.cat([base] * (M // 64) + [base[:, :, : M % 64]], dim=2)
+    q, sv = rnd(g, B, H, N, D), rnd(g, B, H, M, D)
+    out, w, idx = F.slot_select_attend(q.cuda(), sk.cuda(), sv.cuda())
+    scores = om.slot_scores(q, sk)
+    distinct = torch.sort(scores[..., :64], dim=-1, descending=True).values[..., :3]
+    ok = om.row_gap_ok(distinct)
+    assert float(ok.float().mean()) > 0.9
+    assert torch.equal(idx.cpu()[ok], om.topk_indices(scores)[ok])
+    ro, rw = om.slot_attend(q, sk, sv, idx.cpu())
+    close(out, ro, torch.float32)
+    close(w, rw, torch.float32)
+
+
 def test_slot_attend_given_indices_clamps():
     g = torch.Generator().manual_seed(12)
     B, H, N, M, D = 1, 2, 33, 40, 16
