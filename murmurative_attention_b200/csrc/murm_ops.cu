@@ -226,32 +226,42 @@ __device__ __forceinline__ uint32_t pick8(const uint32_t (&x)[8], int j) {
 }
 
 // ---------------------------------------------------------------------------
-// select + attend, forward, M <= 256 and selection on the GPU: the same results as k_sa_fwd
-// (the same scores, in the same operation order, and the same picks), with the key table read
-// once per four tokens. A warp scores four tokens at a time (lane: slots lane + 32 j, 8 x 4
-// independent dot products over the key rows it loads once); for each token the row's keys
-// >= the 7th largest of the 32 lanes' maxima (a lower bound of the row's 7th largest key) are
-// the only ones a lane ranks, then the lanes' lists are merged. Shared memory: the transposed
-// key table and each warp's four q rows, [D][4] fp32.
+// select + attend, forward, M <= 256 and selection on the GPU: the picks of k_sa_fwd (the same
+// scores, in the same operation order; ties to the lowest slot) with the key table read once
+// per four tokens. Shared memory: the transposed key table [D][kMp4] (columns M..255 zero), each
+// warp's four q rows [D][4], and per warp a candidate list and the picks.
+//   - scores: a warp takes four tokens at a time, a lane slots lane + 32 j (8 x 4 independent
+//     dot products in d order over the key rows it loads once);
+//   - candidates: thr = the 7th largest of the 32 lanes' maximum keys, ties counted; at least 7
+//     of the row's keys are >= thr, so its top 7 are among the keys >= thr (typically 7-10);
+//   - ranking: the candidates are packed into a per-warp list and each one's rank in the order
+//     (key descending, slot ascending) is counted over the list; more than 32 candidates (ties,
+//     rows with most slots masked) take the lane-list merge of k_sa_fwd instead;
+//   - attend: the picks' plain scores (without bias or mask), scaled, softmax, weighted values.
 // ---------------------------------------------------------------------------
 constexpr int kTokGroup = 4;
+constexpr int kMp4 = 257;  // key-table row stride of k_sa_fwd4 (odd: lanes read distinct banks)
 template <typename T>
-__global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_args a, int Mp, int vec) {
+__global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_args a, int vec) {
   extern __shared__ float sh[];
   const int M = a.shape.slots, D = a.shape.head_dim, N = a.shape.tokens;
-  float* Kt = sh;                                                   // [D][Mp]
-  float4* qs = reinterpret_cast<float4*>(sh + (((size_t)D * Mp + 3) & ~(size_t)3));  // [kWarps][D]
+  float* Kt = sh;                                                                  // [D][kMp4]
+  float4* qs = reinterpret_cast<float4*>(sh + (((size_t)D * kMp4 + 3) & ~(size_t)3));  // [kWarps][D]
+  uint2* cand = reinterpret_cast<uint2*>(qs + kWarps * D);                         // [kWarps][32]
+  uint2* picks = cand + kWarps * 32;                                               // [kWarps][8]
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  stage_keys<T>(a, Kt, Mp, vec, b, h);
+  if (M < 256)
+    for (int e = threadIdx.x; e < D * 256; e += blockDim.x)
+      if (e % 256 >= M) Kt[(size_t)(e / 256) * kMp4 + e % 256] = 0.f;
+  stage_keys<T>(a, Kt, kMp4, vec, b, h);
   __syncthreads();
   const int em = (a.effective_m > 0 && a.effective_m < M) ? a.effective_m : M;
   const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
   float4* q4 = qs + warp * D;
-  const float* qf = reinterpret_cast<const float*>(q4);
-  int col[8];  // clamped columns: reads stay inside Kt
-#pragma unroll
-  for (int j = 0; j < 8; ++j) col[j] = min(M - 1, lane + 32 * j);
+  uint2* cw = cand + warp * 32;
+  uint2* pw = picks + warp * 8;
+  const T* sv = static_cast<const T*>(a.slot_values) + (int64_t)b * a.sv_stride[0] + (int64_t)h * a.sv_stride[1];
   for (int g0 = 0; g0 < kTokPerWarp; g0 += kTokGroup) {
     const int nb = (blockIdx.x * kWarps + warp) * kTokPerWarp + g0;
     if (nb >= N) break;
@@ -267,23 +277,30 @@ __global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_a
     for (int t = 0; t < kTokGroup; ++t)
 #pragma unroll
       for (int j = 0; j < 8; ++j) sj[t][j] = 0.f;
+    const float* kp = Kt + lane;
+#pragma unroll 2
     for (int d = 0; d < D; ++d) {  // each score in d order, as k_sa_fwd
       const float4 qd = q4[d];
-      const float* row = Kt + (size_t)d * Mp;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float kv = row[col[j]];
+        const float kv = kp[32 * j];
         sj[0][j] = fmaf(qd.x, kv, sj[0][j]);
         sj[1][j] = fmaf(qd.y, kv, sj[1][j]);
         sj[2][j] = fmaf(qd.z, kv, sj[2][j]);
         sj[3][j] = fmaf(qd.w, kv, sj[3][j]);
       }
+      kp += kMp4;
     }
 #pragma unroll 1
     for (int t = 0; t < kTokGroup; ++t) {
       const int n = nb + t;
       if (n >= N) break;
-      uint32_t kk[8];  // rank keys of this lane's slots (0: no slot)
+      // this lane's rank keys (0: no slot); bias and mask rows walked 32 slots at a time
+      const T* bp = a.position_bias ? static_cast<const T*>(a.position_bias) + off4(a.bias_stride, b, h, n, lane)
+                                    : nullptr;
+      const uint8_t* mp = a.mask ? a.mask + off4(a.mask_stride, b, h, n, lane) : nullptr;
+      const int64_t bstep = 32 * a.bias_stride[3], mstep = 32 * a.mask_stride[3];
+      uint32_t kk[8];
       uint32_t lm = 0u;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -291,15 +308,13 @@ __global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_a
         kk[j] = 0u;
         if (m < M) {
           float sc = sj[0][j];
-          if (a.position_bias) sc += ld<T>(a.position_bias, off4(a.bias_stride, b, h, n, m));     // reference.py:21-22
-          bool masked = m >= em || (a.causal && m > n);                                             // :27-36
-          if (a.mask) masked = masked || a.mask[off4(a.mask_stride, b, h, n, m)] == 0;                // :24-25
+          if (bp) sc += Elem<T>::load(bp + j * bstep);                      // reference.py:21-22
+          bool masked = m >= em || (a.causal && m > n);                      // :27-36
+          if (mp) masked = masked || mp[j * mstep] == 0;                     // :24-25
           kk[j] = rank_key(masked ? -INFINITY : sc);
         }
         lm = max(lm, kk[j]);
       }
-      // thr = the 7th largest lane maximum (ties counted): at least 7 of the row's keys are >= thr,
-      // so each of its top 7 is too
       uint32_t thr = 0u, v = lm;
       int cnt = 0;
 #pragma unroll 1
@@ -312,23 +327,55 @@ __global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_a
       uint32_t cm = 0u;  // this lane's candidates
 #pragma unroll
       for (int j = 0; j < 8; ++j) cm |= (kk[j] != 0u && kk[j] >= thr ? 1u : 0u) << j;
-      uint32_t tk[kTopK];
-      int ts[kTopK];
+      const int c = __popc(cm);
+      int pre = c;  // inclusive prefix over the lanes
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ts[j] = 0; }
-      while (cm) {  // ascending slot order within the lane
-        const int j = __ffs(cm) - 1;
-        cm &= cm - 1;
-        offer7(tk, ts, pick8(kk, j), lane + 32 * j);
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += y;
       }
-      warp_top7(tk, ts);
-      // attend over the picks with the plain scaled scores (reference.py:58-66)
+      const int total = __shfl_sync(0xffffffffu, pre, 31);
+      int ps[kTopK];
+      if (total <= 32) {  // warp-uniform
+        int p = pre - c;
+        for (uint32_t mm = cm; mm; mm &= mm - 1) {
+          const int j = __ffs(mm) - 1;
+          cw[p++] = make_uint2(pick8(kk, j), (uint32_t)(lane + 32 * j));
+        }
+        __syncwarp();
+        if (lane < total) {
+          const uint2 me = cw[lane];
+          int rank = 0;
+          for (int i = 0; i < total; ++i) {
+            const uint2 o = cw[i];
+            rank += (o.x > me.x || (o.x == me.x && o.y < me.y)) ? 1 : 0;
+          }
+          if (rank < kTopK) pw[rank] = me;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) ps[j] = (int)pw[j].y;
+        __syncwarp();  // the lists are reused by the next token
+      } else {
+        uint32_t tk[kTopK];
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) { tk[j] = 0u; ps[j] = 0; }
+        for (uint32_t mm = cm; mm; mm &= mm - 1) {  // ascending slot order within the lane
+          const int j = __ffs(mm) - 1;
+          offer7(tk, ps, pick8(kk, j), lane + 32 * j);
+        }
+        warp_top7(tk, ps);
+      }
+      // attend over the picks with their plain scaled scores (reference.py:58-66): the score of
+      // slot s is lane s % 32's sj[s / 32]
       float sc[kTopK], mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        float p = 0.f;
-        for (int d = lane; d < D; d += 32) p = fmaf(qf[4 * d + t], Kt[(size_t)d * Mp + ts[j]], p);
-        sc[j] = warp_sum(p) * scale;
+        const int q = ps[j] >> 5;
+        const float a0 = (q & 1) ? sj[0][1] : sj[0][0], a1 = (q & 1) ? sj[0][3] : sj[0][2];
+        const float a2 = (q & 1) ? sj[0][5] : sj[0][4], a3 = (q & 1) ? sj[0][7] : sj[0][6];
+        const float b0 = (q & 2) ? a1 : a0, b1 = (q & 2) ? a3 : a2;
+        sc[j] = __shfl_sync(0xffffffffu, (q & 4) ? b1 : b0, ps[j] & 31) * scale;
         mx = fmaxf(mx, sc[j]);
       }
       float sum = 0.f;
@@ -342,16 +389,16 @@ __global__ void __launch_bounds__(32 * kWarps, 3) k_sa_fwd4(murm_select_attend_a
       for (int d = lane; d < D; d += 32) {
         float o = 0.f;
 #pragma unroll
-        for (int j = 0; j < kTopK; ++j) o = fmaf(sc[j], ld<T>(a.slot_values, off3(a.sv_stride, b, h, ts[j]) + d), o);
+        for (int j = 0; j < kTopK; ++j) o = fmaf(sc[j], Elem<T>::load(sv + (int64_t)ps[j] * a.sv_stride[2] + d), o);
         st<T>(a.out, off3(a.out_stride, b, h, n) + d, o);
       }
       const int64_t rec = ((int64_t)bh * N + n) * kTopK;
       if (lane < kTopK) {
-        int pj = ts[0];
+        int pj = ps[0];
         float wj = sc[0];
 #pragma unroll
         for (int j = 1; j < kTopK; ++j)
-          if (lane == j) { pj = ts[j]; wj = sc[j]; }
+          if (lane == j) { pj = ps[j]; wj = sc[j]; }
         a.indices[rec + lane] = pj;
         a.weights[rec + lane] = wj;
       }
@@ -1166,9 +1213,10 @@ murm_status sa_fwd(const murm_select_attend_args& a, cudaStream_t st) {
   int vec = (a.shape.head_dim * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.slot_keys) & 15) == 0;
   for (int i = 0; i < 3; ++i) vec = vec && (a.sk_stride[i] * es) % 16 == 0;
   if (!a.indices_in && a.shape.slots <= 256) {  // four tokens per pass over the key table
-    const size_t smem = ((((size_t)a.shape.head_dim * Mp + 3) & ~(size_t)3) + (size_t)kWarps * a.shape.head_dim * 4) * 4;
+    const size_t smem = ((((size_t)a.shape.head_dim * kMp4 + 3) & ~(size_t)3) + (size_t)kWarps * a.shape.head_dim * 4) * 4 +
+                        (size_t)kWarps * 40 * sizeof(uint2);
     smem_opt_in(k_sa_fwd4<T>, smem);
-    MURM_LAUNCH("phase_select_attend", k_sa_fwd4<T>, grid, 32 * kWarps, smem, st, a, Mp, vec);
+    MURM_LAUNCH("phase_select_attend", k_sa_fwd4<T>, grid, 32 * kWarps, smem, st, a, vec);
   } else {
     const size_t smem = ((size_t)a.shape.head_dim * Mp + (size_t)kWarps * a.shape.head_dim) * 4;
     smem_opt_in(k_sa_fwd<T>, smem);
