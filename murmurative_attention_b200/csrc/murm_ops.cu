@@ -506,16 +506,42 @@ __global__ void __launch_bounds__(256) k_csr_fill(const int64_t* idx, int N, int
 }
 
 // ---------------------------------------------------------------------------
-// select + attend, backward, token side: a warp per token.
+// select + attend, backward, token side: a warp per token. kStaged: the (b,h) key and value
+// tables are first copied into shared memory and a block's warps take kTokS tokens each (the
+// picked rows then come from shared memory instead of L2); the arithmetic is the same.
 //   dw_j = g . V[i_j] (+ grad_weights), da_j = w_j (dw_j - sum_k w_k dw_k),
 //   dq = scale sum_j da_j K[i_j]; coef[t][j] = scale da_j for the slot side.
 // ---------------------------------------------------------------------------
-template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
-__global__ void __launch_bounds__(256, 3) k_sa_bwd_tok(murm_select_attend_bwd_args a, float* coef) {
+constexpr int kTokS = 16;  // tokens per warp of the staged token-side kernels
+constexpr size_t kMaxStagedTables = 160 * 1024;  // shared memory for a staged (b,h) table pair
+template <typename T, int U, bool kStaged>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(kStaged ? 512 : 256, kStaged ? 2 : 3) k_sa_bwd_tok(murm_select_attend_bwd_args a, float* coef) {
+  extern __shared__ float sh_tab[];
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
+  T* tK = reinterpret_cast<T*>(sh_tab);  // [M][D] (kStaged)
+  T* tV = tK + (size_t)M * D;
+  if constexpr (kStaged) {
+    for (int e = threadIdx.x; e < M * D; e += blockDim.x) {
+      const int m = e / D, d = e - m * D;
+      tK[e] = static_cast<const T*>(a.slot_keys)[off3(a.sk_stride, b, h, m) + d];
+      tV[e] = static_cast<const T*>(a.slot_values)[off3(a.sv_stride, b, h, m) + d];
+    }
+    __syncthreads();
+  }
+  auto skey = [&](int m, int d) -> float {
+    if constexpr (kStaged) return Elem<T>::load(tK + (size_t)m * D + d);
+    else return ld<T>(a.slot_keys, off3(a.sk_stride, b, h, m) + d);
+  };
+  auto sval = [&](int m, int d) -> float {
+    if constexpr (kStaged) return Elem<T>::load(tV + (size_t)m * D + d);
+    else return ld<T>(a.slot_values, off3(a.sv_stride, b, h, m) + d);
+  };
+  const int nw = blockDim.x >> 5;
+  const int ntok = kStaged ? kTokS : 1;
+  for (int i = 0; i < ntok; ++i) {
+  const int n = kStaged ? (blockIdx.x * kTokS + i) * nw + warp : blockIdx.x * 8 + warp;
   if (n >= N) return;
   const float scale = a.scale > 0 ? (float)a.scale : rsqrtf((float)D);
   const int64_t rec = ((int64_t)bh * N + n) * kTopK;
@@ -539,7 +565,7 @@ __global__ void __launch_bounds__(256, 3) k_sa_bwd_tok(murm_select_attend_bwd_ar
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int d = lane + 32 * u;
-      if (d < D) p = fmaf(g[u], ld<T>(a.slot_values, off3(a.sv_stride, b, h, pick[j]) + d), p);
+      if (d < D) p = fmaf(g[u], sval(pick[j], d), p);
     }
     dw[j] = warp_sum(p) + (a.grad_weights ? a.grad_weights[rec + j] : 0.f);
     s = fmaf(w[j], dw[j], s);
@@ -553,7 +579,7 @@ __global__ void __launch_bounds__(256, 3) k_sa_bwd_tok(murm_select_attend_bwd_ar
     if (d < D) {
       float dq = 0.f;
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) dq = fmaf(c[j], ld<T>(a.slot_keys, off3(a.sk_stride, b, h, pick[j]) + d), dq);
+      for (int j = 0; j < kTopK; ++j) dq = fmaf(c[j], skey(pick[j], d), dq);
       st<T>(a.grad_q, off3(a.gq_stride, b, h, n) + d, dq);
     }
   }
@@ -564,6 +590,7 @@ __global__ void __launch_bounds__(256, 3) k_sa_bwd_tok(murm_select_attend_bwd_ar
       if (lane == j) cj = c[j];
     coef[((int64_t)bh * N + n) * 8 + lane] = cj;
   }
+  }  // tokens
 }
 
 // Over a slot's (token, pick) entries [e0, e1) in token order: acc1 += f1 * A[t] and
@@ -755,14 +782,35 @@ __global__ void __launch_bounds__(256) k_upd_bwd_slot(murm_slot_update_bwd_args 
   if (lane == 0) dW[(size_t)bh * M + m] = -dot;
 }
 
-// slot update, backward, token side: a warp per token.
-template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
-__global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a, const float* dks, const float* dvs,
-                                                     const float* dW) {
+// slot update, backward, token side: a warp per token. kStaged: the (b,h) slot adjoints (dks,
+// dvs, dW; fp32) are first copied into shared memory and a block's warps take kTokS tokens each.
+template <typename T, int U, bool kStaged>  // U head dims per lane: d = lane + 32 u, D <= 32 U
+__global__ void __launch_bounds__(kStaged ? 512 : 256) k_upd_bwd_tok(murm_slot_update_bwd_args a, const float* dks,
+                                                                     const float* dvs, const float* dW) {
+  extern __shared__ float sh_adj[];
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
+  const float* aK = dks + (size_t)bh * M * D;  // this (b,h)'s adjoints: global, or their shared copy
+  const float* aV = dvs + (size_t)bh * M * D;
+  const float* aW = dW + (size_t)bh * M;
+  if constexpr (kStaged) {
+    float* s = sh_adj;
+    const int q = M * D / 4;  // D is a multiple of 8: whole float4s
+    for (int e = threadIdx.x; e < q; e += blockDim.x) {
+      reinterpret_cast<float4*>(s)[e] = reinterpret_cast<const float4*>(aK)[e];
+      reinterpret_cast<float4*>(s + (size_t)M * D)[e] = reinterpret_cast<const float4*>(aV)[e];
+    }
+    for (int m = threadIdx.x; m < M; m += blockDim.x) s[2 * (size_t)M * D + m] = aW[m];
+    __syncthreads();
+    aK = s;
+    aV = s + (size_t)M * D;
+    aW = s + 2 * (size_t)M * D;
+  }
+  const int nw = blockDim.x >> 5;
+  const int ntok = kStaged ? kTokS : 1;
+  for (int i = 0; i < ntok; ++i) {
+  const int n = kStaged ? (blockIdx.x * kTokS + i) * nw + warp : blockIdx.x * 8 + warp;
   if (n >= N) return;
   const int64_t rec = ((int64_t)bh * N + n) * kTopK;
   float tk[U], tv[U], gk[U], gv[U];
@@ -778,19 +826,19 @@ __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a
   for (int j = 0; j < kTopK; ++j) {
     const int m = clampi(a.indices[rec + j], M);
     const float wt = a.weights[rec + j];
-    const size_t so = ((size_t)bh * M + m) * D;
+    const size_t so = (size_t)m * D;
     float p = 0.f;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int d = lane + 32 * u;
       if (d < D) {
-        const float k2 = dks[so + d], v2 = dvs[so + d];
+        const float k2 = aK[so + d], v2 = aV[so + d];
         gk[u] = fmaf(wt, k2, gk[u]);
         gv[u] = fmaf(wt, v2, gv[u]);
         p = fmaf(tk[u], k2, fmaf(tv[u], v2, p));
       }
     }
-    gw[j] = warp_sum(p) + dW[(size_t)bh * M + m];
+    gw[j] = warp_sum(p) + aW[m];
   }
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -807,6 +855,7 @@ __global__ void __launch_bounds__(256) k_upd_bwd_tok(murm_slot_update_bwd_args a
       if (lane == j) x = gw[j];
     a.grad_weights[rec + lane] = x;
   }
+  }  // tokens
 }
 
 // ---------------------------------------------------------------------------
@@ -1233,9 +1282,17 @@ murm_status sa_bwd(const murm_select_attend_bwd_args& a, cudaStream_t st) {
   launch_csr(a.shape, a.indices, ws, st);
   float* coef = reinterpret_cast<float*>(ws + z.off_coef);
   const int D = a.shape.head_dim;
-  const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1>, k_sa_bwd_tok<T, 2>, k_sa_bwd_tok<T, 4>);
   const auto kslot = per_lane_dims(D, k_sa_bwd_slot<T, 1>, k_sa_bwd_slot<T, 2>, k_sa_bwd_slot<T, 4>);
-  MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, coef);
+  const size_t tab = 2 * (size_t)a.shape.slots * D * sizeof(T);
+  if (tab <= kMaxStagedTables) {  // the (b,h) key and value tables in shared memory
+    const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1, true>, k_sa_bwd_tok<T, 2, true>, k_sa_bwd_tok<T, 4, true>);
+    smem_opt_in(ktok, tab);
+    MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 16 * kTokS - 1) / (16 * kTokS), BH), 512,
+                tab, st, a, coef);
+  } else {
+    const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1, false>, k_sa_bwd_tok<T, 2, false>, k_sa_bwd_tok<T, 4, false>);
+    MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, coef);
+  }
   MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 7) / 8, BH), 256, 0, st, a,
               coef, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("select_attend backward");
@@ -1257,6 +1314,24 @@ murm_status upd_fwd(const murm_slot_update_args& a, cudaStream_t st) {
   return launched("slot_update forward");
 }
 
+// The token side of the update's backward: with the (b,h) adjoints staged in shared memory where
+// they fit, else reading them from global memory.
+template <typename T>
+void launch_upd_bwd_tok(const char* name, const murm_slot_update_bwd_args& a, const float* dks, const float* dvs,
+                        const float* dW, cudaStream_t st) {
+  const int D = a.shape.head_dim;
+  const unsigned BH = (unsigned)(a.shape.batch * a.shape.heads);
+  const size_t tab = (2 * (size_t)a.shape.slots * D + a.shape.slots) * sizeof(float);
+  if (tab <= kMaxStagedTables) {
+    const auto k = per_lane_dims(D, k_upd_bwd_tok<T, 1, true>, k_upd_bwd_tok<T, 2, true>, k_upd_bwd_tok<T, 4, true>);
+    smem_opt_in(k, tab);
+    MURM_LAUNCH(name, k, dim3((a.shape.tokens + 16 * kTokS - 1) / (16 * kTokS), BH), 512, tab, st, a, dks, dvs, dW);
+  } else {
+    const auto k = per_lane_dims(D, k_upd_bwd_tok<T, 1, false>, k_upd_bwd_tok<T, 2, false>, k_upd_bwd_tok<T, 4, false>);
+    MURM_LAUNCH(name, k, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, dks, dvs, dW);
+  }
+}
+
 template <typename T>
 murm_status upd_bwd(const murm_slot_update_bwd_args& a, cudaStream_t st) {
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
@@ -1271,9 +1346,7 @@ murm_status upd_bwd(const murm_slot_update_bwd_args& a, cudaStream_t st) {
   float* dW = reinterpret_cast<float*>(ws + z.off_dw);
   MURM_LAUNCH("phase_update_bwd_slots", k_upd_bwd_slot<T>, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st,
               a, Uk, Uv, W, dks, dvs, dW);
-  const auto ktok = per_lane_dims(a.shape.head_dim, k_upd_bwd_tok<T, 1>, k_upd_bwd_tok<T, 2>, k_upd_bwd_tok<T, 4>);
-  MURM_LAUNCH("phase_update_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, (unsigned)BH), 256, 0, st,
-              a, dks, dvs, dW);
+  launch_upd_bwd_tok<T>("phase_update_bwd_tokens", a, dks, dvs, dW, st);
   return launched("slot_update backward");
 }
 
@@ -1306,9 +1379,7 @@ murm_status sums_bwd(const murm_slot_sums_bwd_args& a, cudaStream_t st) {
   u.grad_token_keys = a.grad_token_keys;
   u.grad_token_values = a.grad_token_values;
   u.grad_weights = a.grad_weights;
-  const auto ktok = per_lane_dims(a.shape.head_dim, k_upd_bwd_tok<T, 1>, k_upd_bwd_tok<T, 2>, k_upd_bwd_tok<T, 4>);
-  MURM_LAUNCH("phase_sums_bwd", ktok, dim3((a.shape.tokens + 7) / 8, a.shape.batch * a.shape.heads), 256,
-              0, st, u, a.grad_key_sums, a.grad_value_sums, a.grad_weight_sums);
+  launch_upd_bwd_tok<T>("phase_sums_bwd", u, a.grad_key_sums, a.grad_value_sums, a.grad_weight_sums, st);
   return launched("slot sums backward");
 }
 template <typename T> struct SumFwd { static murm_status run(const murm_slot_sums_args& a, cudaStream_t s) { return sums_fwd<T>(a, s); } };
