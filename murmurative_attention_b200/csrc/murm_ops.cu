@@ -441,19 +441,22 @@ __device__ __forceinline__ void tile_bitmap(const int64_t* ix, int N, int M, int
   __syncthreads();
 }
 
-// (1) grid (ntiles, BH): per-tile, per-slot pair counts -> cnt [BH][ntiles][M]
+// (1) grid (ntiles, BH): per-tile, per-slot pair counts -> cnt [BH][ntiles][M] (shared-memory
+// counters: the counts alone need no order)
 __global__ void __launch_bounds__(256) k_csr_count(const int64_t* idx, int N, int M, int tile, int words, int* cnt) {
-  extern __shared__ uint32_t smu[];
+  extern __shared__ uint32_t smu[];  // [M] counters
   const int bh = blockIdx.y, ti = blockIdx.x;
-  int mm[kTopK];
-  bool live;
-  tile_bitmap(idx + (int64_t)bh * N * kTopK, N, M, tile, words, ti * tile, smu, mm, live);
-  int* c = cnt + ((int64_t)bh * gridDim.x + ti) * M;
-  for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    int x = 0;
-    for (int w = 0; w < words; ++w) x += __popc(smu[m * words + w]);
-    c[m] = x;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) smu[m] = 0u;
+  __syncthreads();
+  const int t = ti * tile + threadIdx.x;
+  if (threadIdx.x < tile && t < N) {
+    const int64_t* ix = idx + ((int64_t)bh * N + t) * kTopK;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) atomicAdd(&smu[clampi(ix[j], M)], 1u);
   }
+  __syncthreads();
+  int* c = cnt + ((int64_t)bh * gridDim.x + ti) * M;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) c[m] = (int)smu[m];
 }
 
 // (2) grid BH: per slot, tile bases (in place) and the slot offsets
@@ -463,10 +466,15 @@ __global__ void __launch_bounds__(256) k_csr_scan(int ntiles, int M, int* cnt, i
   int* c = cnt + (int64_t)bh * ntiles * M;
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     int run = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      const int x = c[(int64_t)t * M + m];
-      c[(int64_t)t * M + m] = run;
-      run += x;
+    for (int t0 = 0; t0 < ntiles; t0 += 8) {  // eight tiles' counts loaded at once
+      int x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = t0 + i < ntiles ? c[(int64_t)(t0 + i) * M + m] : 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (t0 + i < ntiles) c[(int64_t)(t0 + i) * M + m] = run;
+        run += x[i];
+      }
     }
     tot[m] = run;
   }
@@ -485,11 +493,20 @@ __global__ void __launch_bounds__(256) k_csr_scan(int ntiles, int M, int* cnt, i
 // (3) grid (ntiles, BH): place the tile's pairs
 __global__ void __launch_bounds__(256) k_csr_fill(const int64_t* idx, int N, int M, int tile, int words,
                                                   const int* cnt, const int* offsets, int* entries) {
-  extern __shared__ uint32_t smu[];
+  extern __shared__ uint32_t smu[];  // [M][words] bitmap, then [M][words] uint16 prefix counts
+  uint16_t* pre = reinterpret_cast<uint16_t*>(smu + M * words);
   const int bh = blockIdx.y, ti = blockIdx.x;
   int mm[kTopK];
   bool live;
   tile_bitmap(idx + (int64_t)bh * N * kTopK, N, M, tile, words, ti * tile, smu, mm, live);
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {  // pairs of the slot in the row's earlier words
+    int acc = 0;
+    for (int w = 0; w < words; ++w) {
+      pre[m * words + w] = (uint16_t)acc;
+      acc += __popc(smu[m * words + w]);
+    }
+  }
+  __syncthreads();
   if (!live) return;
   const int* c = cnt + ((int64_t)bh * gridDim.x + ti) * M;
   const int* off = offsets + (int64_t)bh * (M + 1);
@@ -499,8 +516,7 @@ __global__ void __launch_bounds__(256) k_csr_fill(const int64_t* idx, int N, int
   for (int j = 0; j < kTopK; ++j) {
     const int p = threadIdx.x * kTopK + j, w = p >> 5;
     const uint32_t* row = smu + mm[j] * words;
-    int before = __popc(row[w] & ((1u << (p & 31)) - 1u));
-    for (int x = 0; x < w; ++x) before += __popc(row[x]);
+    const int before = pre[mm[j] * words + w] + __popc(row[w] & ((1u << (p & 31)) - 1u));
     ent[off[mm[j]] + c[mm[j]] + before] = t * 8 + j;
   }
 }
@@ -1241,16 +1257,16 @@ void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cuda
   const int tile = M <= 256 ? 256 : (M <= 512 ? 128 : 64);
   const int words = (tile * kTopK + 31) / 32;
   const int ntiles = (N + tile - 1) / tile;
-  const size_t smem = (size_t)M * words * 4;
+  const size_t smem = (size_t)M * words * 4;  // bitmap
+  const size_t smem_fill = smem + (size_t)M * words * 2;  // + prefix counts
   const Sizes z = sizes(s);
   int* offsets = reinterpret_cast<int*>(ws);
   int* entries = reinterpret_cast<int*>(ws + z.off_csr_entries);
   int* cnt = reinterpret_cast<int*>(ws + z.off_cnt);
-  smem_opt_in(k_csr_count, smem);
-  smem_opt_in(k_csr_fill, smem);
-  MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt);
+  smem_opt_in(k_csr_fill, smem_fill);
+  MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, (size_t)M * 4, st, idx, N, M, tile, words, cnt);
   MURM_LAUNCH("phase_csr_scan", k_csr_scan, dim3(BH), 256, 0, st, ntiles, M, cnt, offsets);
-  MURM_LAUNCH("phase_csr_fill", k_csr_fill, dim3(ntiles, BH), 256, smem, st, idx, N, M, tile, words, cnt, offsets,
+  MURM_LAUNCH("phase_csr_fill", k_csr_fill, dim3(ntiles, BH), 256, smem_fill, st, idx, N, M, tile, words, cnt, offsets,
               entries);
 }
 
