@@ -668,23 +668,60 @@ __device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_
   }
 }
 
-// slot side: a warp per (b,h, slot), its pairs in token order:
+// A slot's entry sums by two warps: block of 8 warps = 4 slots x 2 halves of each slot's entry
+// list; each half summed in token order by pair_sums, the second half's sums then added to the
+// first's (a fixed order: deterministic). Returns true in the first half's warp of a slot < M,
+// which holds the slot's sums (m set to the slot either way).
+template <typename T, int U>
+__device__ __forceinline__ bool slot_sums_2(const int* off, const int* ent, int64_t rec0, const float* f1, int s1,
+                                            const float* f2, int s2, const T* A, const int64_t* as, const T* Bp,
+                                            const int64_t* bs, int b, int h, int D, int M, int& m, float (&acc1)[U],
+                                            float (&acc2)[U], float* fsum) {
+  __shared__ float part[4][2 * U * 32 + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sl = warp >> 1, half = warp & 1;
+  m = blockIdx.x * 4 + sl;
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc1[u] = acc2[u] = 0.f;
+  if (fsum) *fsum = 0.f;
+  if (m < M) {
+    const int e0 = off[m], e1 = off[m + 1], mid = e0 + (e1 - e0 + 1) / 2;
+    pair_sums<T, U>(ent, half ? mid : e0, half ? e1 : mid, rec0, f1, s1, f2, s2, A, as, Bp, bs, b, h, D, lane, acc1,
+                    acc2, fsum);
+    if (half) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        part[sl][u * 32 + lane] = acc1[u];
+        part[sl][(U + u) * 32 + lane] = acc2[u];
+      }
+      if (fsum && lane == 0) part[sl][2 * U * 32] = *fsum;
+    }
+  }
+  __syncthreads();
+  if (m >= M || half) return false;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    acc1[u] += part[sl][u * 32 + lane];
+    acc2[u] += part[sl][(U + u) * 32 + lane];
+  }
+  if (fsum) *fsum += part[sl][2 * U * 32];
+  return true;
+}
+
+// slot side: two warps per (b,h, slot), its pairs in token order:
 //   dK[m] = sum coef * q[t],  dV[m] = sum w * g[t]
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
 __global__ void __launch_bounds__(256, 3) k_sa_bwd_slot(murm_select_attend_bwd_args a, const float* coef,
                                                      const int* offsets, const int* entries) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + warp;
-  if (m >= M) return;
+  const int lane = threadIdx.x & 31;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
+  int m;
   float dk[U], dv[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u) dk[u] = dv[u] = 0.f;
-  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, coef, 8, a.weights, kTopK, static_cast<const T*>(a.q),
-               a.q_stride, static_cast<const T*>(a.grad_out), a.go_stride, b, h, D, lane, dk, dv, nullptr);
+  if (!slot_sums_2<T, U>(off, ent, (int64_t)bh * N, coef, 8, a.weights, kTopK, static_cast<const T*>(a.q), a.q_stride,
+                         static_cast<const T*>(a.grad_out), a.go_stride, b, h, D, M, m, dk, dv, nullptr))
+    return;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
@@ -696,7 +733,7 @@ __global__ void __launch_bounds__(256, 3) k_sa_bwd_slot(murm_select_attend_bwd_a
 }
 
 // ---------------------------------------------------------------------------
-// slot update, forward: a warp per (b,h, slot). saved = U_k, U_v [BH][M][D] and
+// slot update, forward: two warps per (b,h, slot). saved = U_k, U_v [BH][M][D] and
 // W [BH][M] (fp32).
 // ---------------------------------------------------------------------------
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
@@ -704,18 +741,16 @@ __global__ void __launch_bounds__(256, 3) k_upd_fwd(murm_slot_update_args a, con
                                                  float* Uk, float* Uv, float* Wsum) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + warp;
-  if (m >= M) return;
+  const int lane = threadIdx.x & 31;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
+  int m;
   float sk[U], sv[U];
   float W = 0.f;
-#pragma unroll
-  for (int u = 0; u < U; ++u) sk[u] = sv[u] = 0.f;
-  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
-               static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
-               b, h, D, lane, sk, sv, &W);
+  if (!slot_sums_2<T, U>(off, ent, (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+                         static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values),
+                         a.tv_stride, b, h, D, M, m, sk, sv, &W))
+    return;
   const bool valid = W > 0.f;                       // reference.py:105
   const float den = __fadd_rn(W, kEmaEps);          // :106-107
   const float al = (float)a.alpha, om = (float)(1.0 - a.alpha);
@@ -739,23 +774,21 @@ __global__ void __launch_bounds__(256, 3) k_upd_fwd(murm_slot_update_args a, con
   if (lane == 0) Wsum[(size_t)bh * M + m] = W;
 }
 
-// slot sums alone (a warp per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
+// slot sums alone (two warps per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
 __global__ void __launch_bounds__(256, 3) k_sums_fwd(murm_slot_sums_args a, const int* offsets, const int* entries) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
   const int bh = blockIdx.y, b = bh / a.shape.heads, h = bh - b * a.shape.heads;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + warp;
-  if (m >= M) return;
+  const int lane = threadIdx.x & 31;
   const int* off = offsets + (int64_t)bh * (M + 1);
   const int* ent = entries + (int64_t)bh * N * kTopK;
+  int m;
   float sk[U], sv[U];
   float W = 0.f;
-#pragma unroll
-  for (int u = 0; u < U; ++u) sk[u] = sv[u] = 0.f;
-  pair_sums<T, U>(ent, off[m], off[m + 1], (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
-               static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values), a.tv_stride,
-               b, h, D, lane, sk, sv, &W);
+  if (!slot_sums_2<T, U>(off, ent, (int64_t)bh * N, a.weights, kTopK, a.weights, kTopK,
+                         static_cast<const T*>(a.token_keys), a.tk_stride, static_cast<const T*>(a.token_values),
+                         a.tv_stride, b, h, D, M, m, sk, sv, &W))
+    return;
   const size_t so = ((size_t)bh * M + m) * D;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -1309,7 +1342,7 @@ murm_status sa_bwd(const murm_select_attend_bwd_args& a, cudaStream_t st) {
     const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1, false>, k_sa_bwd_tok<T, 2, false>, k_sa_bwd_tok<T, 4, false>);
     MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, coef);
   }
-  MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 7) / 8, BH), 256, 0, st, a,
+  MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 3) / 4, BH), 256, 0, st, a,
               coef, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("select_attend backward");
 }
@@ -1325,7 +1358,7 @@ murm_status upd_fwd(const murm_slot_update_args& a, cudaStream_t st) {
   float* Uv = reinterpret_cast<float*>(sv + a256(BH * MD * 4));
   float* W = reinterpret_cast<float*>(sv + 2 * a256(BH * MD * 4));
   const auto kupd = per_lane_dims(a.shape.head_dim, k_upd_fwd<T, 1>, k_upd_fwd<T, 2>, k_upd_fwd<T, 4>);
-  MURM_LAUNCH("phase_update", kupd, dim3((a.shape.slots + 7) / 8, (unsigned)BH), 256, 0, st, a,
+  MURM_LAUNCH("phase_update", kupd, dim3((a.shape.slots + 3) / 4, (unsigned)BH), 256, 0, st, a,
               reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries), Uk, Uv, W);
   return launched("slot_update forward");
 }
@@ -1372,7 +1405,7 @@ murm_status sums_fwd(const murm_slot_sums_args& a, cudaStream_t st) {
   const Sizes z = sizes(a.shape);
   launch_csr(a.shape, a.indices, ws, st);
   const auto ksum = per_lane_dims(a.shape.head_dim, k_sums_fwd<T, 1>, k_sums_fwd<T, 2>, k_sums_fwd<T, 4>);
-  MURM_LAUNCH("phase_sums", ksum, dim3((a.shape.slots + 7) / 8, a.shape.batch * a.shape.heads), 256, 0, st,
+  MURM_LAUNCH("phase_sums", ksum, dim3((a.shape.slots + 3) / 4, a.shape.batch * a.shape.heads), 256, 0, st,
               a, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("slot sums forward");
 }
