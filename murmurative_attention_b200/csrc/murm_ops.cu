@@ -668,46 +668,52 @@ __device__ __forceinline__ void pair_sums(const int* ent, int e0, int e1, int64_
   }
 }
 
-// A slot's entry sums by two warps: block of 8 warps = 4 slots x 2 halves of each slot's entry
-// list; each half summed in token order by pair_sums, the second half's sums then added to the
-// first's (a fixed order: deterministic). Returns true in the first half's warp of a slot < M,
-// which holds the slot's sums (m set to the slot either way).
+// A slot's entry sums by kSumParts warps: a block of 8 warps takes 8 / kSumParts slots, each
+// slot's entry list cut into kSumParts contiguous parts, each summed in token order by pair_sums;
+// the first part's warp then adds the others' sums in part order (a fixed order: deterministic).
+// Returns true in the first part's warp of a slot < M, which holds the slot's sums (m set to the
+// slot either way).
+constexpr int kSumParts = 4;
 template <typename T, int U>
 __device__ __forceinline__ bool slot_sums_2(const int* off, const int* ent, int64_t rec0, const float* f1, int s1,
                                             const float* f2, int s2, const T* A, const int64_t* as, const T* Bp,
                                             const int64_t* bs, int b, int h, int D, int M, int& m, float (&acc1)[U],
                                             float (&acc2)[U], float* fsum) {
-  __shared__ float part[4][2 * U * 32 + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sl = warp >> 1, half = warp & 1;
-  m = blockIdx.x * 4 + sl;
+  constexpr int P = kSumParts, S = 8 / P;
+  __shared__ float part[S][P][2 * U * 32 + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sl = warp / P, pi = warp % P;
+  m = blockIdx.x * S + sl;
 #pragma unroll
   for (int u = 0; u < U; ++u) acc1[u] = acc2[u] = 0.f;
   if (fsum) *fsum = 0.f;
   if (m < M) {
-    const int e0 = off[m], e1 = off[m + 1], mid = e0 + (e1 - e0 + 1) / 2;
-    pair_sums<T, U>(ent, half ? mid : e0, half ? e1 : mid, rec0, f1, s1, f2, s2, A, as, Bp, bs, b, h, D, lane, acc1,
-                    acc2, fsum);
-    if (half) {
+    const int e0 = off[m], n = off[m + 1] - e0;
+    pair_sums<T, U>(ent, e0 + (int)((int64_t)n * pi / P), e0 + (int)((int64_t)n * (pi + 1) / P), rec0, f1, s1, f2, s2,
+                    A, as, Bp, bs, b, h, D, lane, acc1, acc2, fsum);
+    if (pi) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        part[sl][u * 32 + lane] = acc1[u];
-        part[sl][(U + u) * 32 + lane] = acc2[u];
+        part[sl][pi][u * 32 + lane] = acc1[u];
+        part[sl][pi][(U + u) * 32 + lane] = acc2[u];
       }
-      if (fsum && lane == 0) part[sl][2 * U * 32] = *fsum;
+      if (fsum && lane == 0) part[sl][pi][2 * U * 32] = *fsum;
     }
   }
   __syncthreads();
-  if (m >= M || half) return false;
+  if (m >= M || pi) return false;
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    acc1[u] += part[sl][u * 32 + lane];
-    acc2[u] += part[sl][(U + u) * 32 + lane];
+  for (int p = 1; p < P; ++p) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      acc1[u] += part[sl][p][u * 32 + lane];
+      acc2[u] += part[sl][p][(U + u) * 32 + lane];
+    }
+    if (fsum) *fsum += part[sl][p][2 * U * 32];
   }
-  if (fsum) *fsum += part[sl][2 * U * 32];
   return true;
 }
 
-// slot side: two warps per (b,h, slot), its pairs in token order:
+// slot side: kSumParts warps per (b,h, slot), its pairs in token order:
 //   dK[m] = sum coef * q[t],  dV[m] = sum w * g[t]
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
 __global__ void __launch_bounds__(256, 3) k_sa_bwd_slot(murm_select_attend_bwd_args a, const float* coef,
@@ -733,7 +739,7 @@ __global__ void __launch_bounds__(256, 3) k_sa_bwd_slot(murm_select_attend_bwd_a
 }
 
 // ---------------------------------------------------------------------------
-// slot update, forward: two warps per (b,h, slot). saved = U_k, U_v [BH][M][D] and
+// slot update, forward: kSumParts warps per (b,h, slot). saved = U_k, U_v [BH][M][D] and
 // W [BH][M] (fp32).
 // ---------------------------------------------------------------------------
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
@@ -774,7 +780,7 @@ __global__ void __launch_bounds__(256, 3) k_upd_fwd(murm_slot_update_args a, con
   if (lane == 0) Wsum[(size_t)bh * M + m] = W;
 }
 
-// slot sums alone (two warps per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
+// slot sums alone (kSumParts warps per (b,h, slot)): fp32 [BH][M][D] key/value sums, [BH][M] weights.
 template <typename T, int U>  // U head dims per lane: d = lane + 32 u, D <= 32 U
 __global__ void __launch_bounds__(256, 3) k_sums_fwd(murm_slot_sums_args a, const int* offsets, const int* entries) {
   const int N = a.shape.tokens, D = a.shape.head_dim, M = a.shape.slots;
@@ -1342,7 +1348,7 @@ murm_status sa_bwd(const murm_select_attend_bwd_args& a, cudaStream_t st) {
     const auto ktok = per_lane_dims(D, k_sa_bwd_tok<T, 1, false>, k_sa_bwd_tok<T, 2, false>, k_sa_bwd_tok<T, 4, false>);
     MURM_LAUNCH("phase_select_attend_bwd_tokens", ktok, dim3((a.shape.tokens + 7) / 8, BH), 256, 0, st, a, coef);
   }
-  MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 3) / 4, BH), 256, 0, st, a,
+  MURM_LAUNCH("phase_select_attend_bwd_slots", kslot, dim3((a.shape.slots + 8 / kSumParts - 1) / (8 / kSumParts), BH), 256, 0, st, a,
               coef, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("select_attend backward");
 }
@@ -1358,7 +1364,7 @@ murm_status upd_fwd(const murm_slot_update_args& a, cudaStream_t st) {
   float* Uv = reinterpret_cast<float*>(sv + a256(BH * MD * 4));
   float* W = reinterpret_cast<float*>(sv + 2 * a256(BH * MD * 4));
   const auto kupd = per_lane_dims(a.shape.head_dim, k_upd_fwd<T, 1>, k_upd_fwd<T, 2>, k_upd_fwd<T, 4>);
-  MURM_LAUNCH("phase_update", kupd, dim3((a.shape.slots + 3) / 4, (unsigned)BH), 256, 0, st, a,
+  MURM_LAUNCH("phase_update", kupd, dim3((a.shape.slots + 8 / kSumParts - 1) / (8 / kSumParts), (unsigned)BH), 256, 0, st, a,
               reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries), Uk, Uv, W);
   return launched("slot_update forward");
 }
@@ -1405,7 +1411,7 @@ murm_status sums_fwd(const murm_slot_sums_args& a, cudaStream_t st) {
   const Sizes z = sizes(a.shape);
   launch_csr(a.shape, a.indices, ws, st);
   const auto ksum = per_lane_dims(a.shape.head_dim, k_sums_fwd<T, 1>, k_sums_fwd<T, 2>, k_sums_fwd<T, 4>);
-  MURM_LAUNCH("phase_sums", ksum, dim3((a.shape.slots + 3) / 4, a.shape.batch * a.shape.heads), 256, 0, st,
+  MURM_LAUNCH("phase_sums", ksum, dim3((a.shape.slots + 8 / kSumParts - 1) / (8 / kSumParts), a.shape.batch * a.shape.heads), 256, 0, st,
               a, reinterpret_cast<const int*>(ws), reinterpret_cast<const int*>(ws + z.off_csr_entries));
   return launched("slot sums forward");
 }
