@@ -443,7 +443,7 @@ __device__ __forceinline__ void tile_bitmap(const int64_t* ix, int N, int M, int
 
 // (1) grid (ntiles, BH): per-tile, per-slot pair counts -> cnt [BH][ntiles][M] (shared-memory
 // counters: the counts alone need no order)
-__global__ void __launch_bounds__(256) k_csr_count(const int64_t* idx, int N, int M, int tile, int words, int* cnt) {
+__global__ void __launch_bounds__(256) k_csr_count(const int64_t* idx, int N, int M, int tile, int* cnt) {
   extern __shared__ uint32_t smu[];  // [M] counters
   const int bh = blockIdx.y, ti = blockIdx.x;
   for (int m = threadIdx.x; m < M; m += blockDim.x) smu[m] = 0u;
@@ -1303,7 +1303,7 @@ void launch_csr(const murm_phase_shape& s, const int64_t* idx, uint8_t* ws, cuda
   int* entries = reinterpret_cast<int*>(ws + z.off_csr_entries);
   int* cnt = reinterpret_cast<int*>(ws + z.off_cnt);
   smem_opt_in(k_csr_fill, smem_fill);
-  MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, (size_t)M * 4, st, idx, N, M, tile, words, cnt);
+  MURM_LAUNCH("phase_csr_count", k_csr_count, dim3(ntiles, BH), 256, (size_t)M * 4, st, idx, N, M, tile, cnt);
   MURM_LAUNCH("phase_csr_scan", k_csr_scan, dim3(BH), 256, 0, st, ntiles, M, cnt, offsets);
   MURM_LAUNCH("phase_csr_fill", k_csr_fill, dim3(ntiles, BH), 256, smem_fill, st, idx, N, M, tile, words, cnt, offsets,
               entries);
