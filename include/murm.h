@@ -198,7 +198,8 @@ MURM_API murm_status murm_slot_murmurate_host_step(const murm_host_step_args* ar
  * selection mask, a position bias, effective (dynamic) M, separate token keys
  * and values, any head_dim that is a multiple of 8 up to 128, and M up to
  * 1024 (M x head_dim x 4 bytes at most 200 KiB). Slot sums are deterministic
- * (slot-major, token order). Conventions as above; grads are written in the
+ * (slot-major: each slot's entries in four fixed contiguous parts, each summed
+ * in token order, the parts added in order). Conventions as above; grads are written in the
  * tensors' dtype, weights fp32, indices int64 [B,H,N,7] contiguous.
  * ------------------------------------------------------------------------ */
 typedef struct murm_phase_shape {
